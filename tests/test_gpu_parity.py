@@ -1,0 +1,346 @@
+"""Parity of the CUDA path (through the C ABI) with the CPU oracle and with outputs
+recorded from the reference implementation.
+
+Tolerances (from the path's specification):
+  * INT8 codes: bit-exact given the same float32 coefficients;
+  * rSVD: relative reconstruction error within 1e-3 absolute of the reference's
+    algorithm on the same sketch;
+  * attention: cosine >= 0.9999 and max-abs error <= 1e-2 against the float32 oracle
+    over the same compressed cache (float32 caches are also held to 2e-4).
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import cuda_ok
+from oracle import spectral_oracle as so
+import golden_io as gio
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not cuda_ok(), reason="needs a CUDA device")]
+
+COS_MIN = 0.9999
+ABS_MAX = 1e-2
+
+
+def _cos(a, b):
+    a, b = np.ravel(a).astype(np.float64), np.ravel(b).astype(np.float64)
+    return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
+
+
+def _close(out, ref, abs_tol=ABS_MAX):
+    out = np.asarray(out, np.float64)
+    ref = np.asarray(ref, np.float64)
+    assert _cos(out, ref) >= COS_MIN, _cos(out, ref)
+    assert np.abs(out - ref).max() <= abs_tol, np.abs(out - ref).max()
+
+
+def _to_dtype_np(x, dtype):
+    t = torch.from_numpy(np.ascontiguousarray(x)).to(dtype)
+    return t.float().numpy()
+
+
+def cache_from_arrays(H, D, T, kK, kV, codes_K, scale_K, basis_K, codes_V, scale_V, basis_V, start_pos,
+                      hot_K, hot_V, hot_pos, dtype, B=1):
+    """Our device cache from per-block arrays in the reference's layout
+    (codes [nblk, H, T, k] or [B, nblk, H, T, k])."""
+    from unsloth_spectral import SpectralCache
+    dev = torch.device("cuda")
+    cache = SpectralCache(H, D, block_size=T, k_rank_keys=kK, k_rank_values=kV, device=dev, dtype=dtype)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    if codes_K is not None and len(codes_K):
+        if codes_K.ndim == 4:
+            codes_K, codes_V, scale_K, scale_V, basis_K, basis_V = (
+                x[None] for x in (codes_K, codes_V, scale_K, scale_V, basis_K, basis_V))
+        perm5 = lambda a: t(a).permute(0, 2, 1, 3, 4)
+        cache.set_cold(perm5(codes_K), t(scale_K).permute(0, 2, 1), perm5(basis_K), perm5(codes_V),
+                       t(scale_V).permute(0, 2, 1), perm5(basis_V), list(start_pos))
+    if hot_K is not None and hot_K.shape[2] > 0:
+        cache.set_hot(t(hot_K).to(dtype), t(hot_V).to(dtype), t(np.asarray(hot_pos).reshape(-1)))
+    return cache
+
+
+# ----------------------------------------------------------------------- quantiser
+def test_quantize_matches_reference_bit_exact():
+    from unsloth_spectral import _ops
+    z = gio.load("quant")
+    C = torch.from_numpy(z["C"]).cuda()
+    codes, scale, minmax, deq = _ops.quantize_int8(C)
+    assert np.array_equal(deq.cpu().numpy(), z["quantized"])
+    assert np.array_equal(minmax.cpu().numpy(), z["scales"])
+
+
+@pytest.mark.parametrize("shape", [(8, 512, 16), (64, 512, 32), (3, 17, 5), (1, 1, 1)])
+def test_quantize_random_bit_exact(shape):
+    from unsloth_spectral import _ops
+    g = torch.Generator().manual_seed(sum(shape))
+    C = torch.randn(*shape, generator=g) * torch.logspace(-4, 4, shape[0])[:, None, None]
+    codes, scale, minmax, deq = _ops.quantize_int8(C.cuda())
+    q, mm, ocodes, oscale = so.quantize_int8_batched(C.numpy())
+    assert np.array_equal(codes.cpu().numpy(), ocodes)
+    assert np.array_equal(scale.cpu().numpy(), oscale)
+    assert np.array_equal(minmax.cpu().numpy(), mm)
+    assert np.array_equal(deq.cpu().numpy(), q)
+
+
+# ------------------------------------------------------------------- decode (golden)
+def _golden_cache(c, dtype):
+    return cache_from_arrays(int(c["H_kv"]), int(c["D"]), int(c["T_blk"]), int(c["kK"]), int(c["kV"]),
+                             c["ck"], c["scale_K"], c["bk"], c["cv"], c["scale_V"], c["bv"], c["start_pos"],
+                             c["hot_K"], c["hot_V"], c["hot_pos"], dtype)
+
+
+@pytest.mark.parametrize("name", ["decode_cfg0", "decode_gqa_small", "decode_untied"])
+@pytest.mark.parametrize("masked", [False, True])
+def test_decode_matches_reference_fp32(name, masked):
+    from unsloth_spectral import spectral_attention_forward
+    from unsloth_spectral.kernels import spectral_attention_decode
+    c = gio.decode_case(name)
+    if masked and "mask" not in c:
+        pytest.skip("no mask recorded for this case")
+    cache = _golden_cache(c, torch.float32)
+    Q = torch.from_numpy(c["Q"]).cuda()
+    cos, sin = torch.from_numpy(c["cos"]).cuda(), torch.from_numpy(c["sin"]).cuda()
+    mask = torch.from_numpy(c["mask"]).cuda() if masked else None
+    qpos, scale = int(c["qpos"]), float(c["scale"])
+    fwd = spectral_attention_forward(Q, cache, cos, sin, qpos, attention_mask=mask, scale=scale).cpu().numpy()
+    dec = spectral_attention_decode(Q, cache, cos, sin, qpos, attention_mask=mask, scale=scale).cpu().numpy()
+    sfx = "_mask" if masked else ""
+    _close(fwd, c["out_forward" + sfx], 2e-4)
+    _close(dec, c["out_decode" + sfx], 2e-4)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("mode", ["forward", "decode"])
+def test_decode_half_precision_vs_oracle(dtype, mode):
+    from unsloth_spectral import spectral_attention_forward
+    from unsloth_spectral.kernels import spectral_attention_decode
+    c = gio.decode_case("decode_cfg0")
+    cache = _golden_cache(c, dtype)
+    Q = torch.from_numpy(c["Q"]).cuda().to(dtype)
+    cos, sin = torch.from_numpy(c["cos"]).cuda(), torch.from_numpy(c["sin"]).cuda()
+    fn = spectral_attention_forward if mode == "forward" else spectral_attention_decode
+    out = fn(Q, cache, cos, sin, int(c["qpos"]), scale=float(c["scale"])).float().cpu().numpy()
+    blocks = so.blocks_from_codes(c["ck"], c["scale_K"], _to_dtype_np(c["bk"], dtype), c["cv"], c["scale_V"],
+                                  _to_dtype_np(c["bv"], dtype), c["start_pos"])
+    ofn = so.spectral_attention_forward if mode == "forward" else so.spectral_attention_decode
+    ref = ofn(_to_dtype_np(c["Q"], dtype), blocks, _to_dtype_np(c["hot_K"], dtype), _to_dtype_np(c["hot_V"], dtype),
+              c["hot_pos"], c["cos"], c["sin"], int(c["qpos"]), scale=float(c["scale"]))
+    _close(out, ref)
+
+
+# ------------------------------------------------------------------ decode (random)
+def _random_case(seed, B, H, nrep, D, T, nblk, kK, kV, hot, masked, qpos_extra=0, untied=False):
+    rng = np.random.default_rng(seed)
+    codes_K = rng.integers(-127, 128, size=(B, nblk, H, T, kK), dtype=np.int8)
+    codes_V = rng.integers(-127, 128, size=(B, nblk, H, T, kV), dtype=np.int8)
+    scale_K = (rng.random((B, nblk, H)) * 0.02 + 0.005).astype(np.float32)
+    scale_V = (rng.random((B, nblk, H)) * 0.02 + 0.005).astype(np.float32)
+    def basis(k):
+        Qm = np.linalg.qr(rng.standard_normal((B, nblk, H, D, k)))[0]
+        return np.ascontiguousarray(np.swapaxes(Qm, -1, -2)).astype(np.float32)
+    basis_K, basis_V = basis(kK), basis(kV)
+    hot_K = rng.standard_normal((B, H, hot, D)).astype(np.float32)
+    hot_V = rng.standard_normal((B, H, hot, D)).astype(np.float32)
+    start = np.arange(nblk) * T
+    hot_pos = np.arange(nblk * T, nblk * T + hot)
+    qpos = nblk * T + hot + qpos_extra
+    L = qpos + 8
+    if untied:
+        cos = (rng.random((L, D)) * 2 - 1).astype(np.float32)
+        sin = (rng.random((L, D)) * 2 - 1).astype(np.float32)
+    else:
+        cc, ss = so.rope_tables(L, D, 1e6)
+        cos, sin = cc, ss
+    Q = (rng.standard_normal((B, H * nrep, 1, D)) / math.sqrt(D)).astype(np.float32)
+    mask = None
+    if masked:
+        mask = (rng.random((B, H * nrep, 1, nblk * T + hot)) > 0.2).astype(np.int64)
+    return dict(codes_K=codes_K, codes_V=codes_V, scale_K=scale_K, scale_V=scale_V, basis_K=basis_K,
+                basis_V=basis_V, hot_K=hot_K, hot_V=hot_V, start=start, hot_pos=hot_pos, qpos=qpos, cos=cos,
+                sin=sin, Q=Q, mask=mask, B=B, H=H, D=D, T=T, kK=kK, kV=kV, nblk=nblk)
+
+
+def _run_random(r, dtype, mode):
+    from unsloth_spectral import spectral_attention_forward
+    from unsloth_spectral.kernels import spectral_attention_decode
+    B, H, D, T = r["B"], r["H"], r["D"], r["T"]
+    cache = cache_from_arrays(H, D, T, r["kK"], r["kV"], r["codes_K"] if r["nblk"] else None, r["scale_K"],
+                              r["basis_K"], r["codes_V"], r["scale_V"], r["basis_V"], r["start"], r["hot_K"],
+                              r["hot_V"], r["hot_pos"], dtype, B=B)
+    Q = torch.from_numpy(r["Q"]).cuda().to(dtype)
+    cos, sin = torch.from_numpy(r["cos"]).cuda(), torch.from_numpy(r["sin"]).cuda()
+    mask = None if r["mask"] is None else torch.from_numpy(r["mask"]).cuda()
+    fn = spectral_attention_forward if mode == "forward" else spectral_attention_decode
+    out = fn(Q, cache, cos, sin, r["qpos"], attention_mask=mask).float().cpu().numpy()
+    ofn = so.spectral_attention_forward if mode == "forward" else so.spectral_attention_decode
+    refs = []
+    for b in range(B):
+        blocks = so.blocks_from_codes(r["codes_K"][b], r["scale_K"][b], _to_dtype_np(r["basis_K"][b], dtype),
+                                      r["codes_V"][b], r["scale_V"][b], _to_dtype_np(r["basis_V"][b], dtype),
+                                      r["start"]) if r["nblk"] else []
+        refs.append(ofn(_to_dtype_np(r["Q"][b:b + 1], dtype), blocks, _to_dtype_np(r["hot_K"][b:b + 1], dtype),
+                        _to_dtype_np(r["hot_V"][b:b + 1], dtype), r["hot_pos"], r["cos"], r["sin"], r["qpos"],
+                        attention_mask=None if r["mask"] is None else r["mask"][b:b + 1]))
+    return out, np.concatenate(refs, 0)
+
+
+CASES = [
+    # seed, B, H, nrep, D, T, nblk, kK, kV, hot, masked
+    (1, 2, 8, 4, 128, 512, 3, 32, 32, 64, False),
+    (2, 1, 8, 4, 128, 512, 2, 16, 32, 0, False),      # no hot tier
+    (3, 3, 2, 1, 64, 256, 2, 48, 16, 17, True),       # MHA, ragged hot tier, mask
+    (4, 1, 4, 8, 128, 128, 5, 64, 64, 200, False),
+    (5, 2, 8, 4, 128, 512, 0, 16, 16, 130, False),    # hot tier only
+    (6, 1, 2, 4, 64, 64, 7, 16, 16, 3, True),
+    (7, 2, 1, 16, 128, 256, 1, 32, 48, 1, False),
+]
+
+
+@pytest.mark.parametrize("case", CASES)
+@pytest.mark.parametrize("mode", ["forward", "decode"])
+def test_decode_random_shapes_fp32(case, mode):
+    r = _random_case(*case)
+    out, ref = _run_random(r, torch.float32, mode)
+    _close(out, ref, 5e-4)
+
+
+@pytest.mark.parametrize("case", CASES[:3])
+def test_decode_random_shapes_fp16(case):
+    r = _random_case(*case)
+    out, ref = _run_random(r, torch.float16, "decode")
+    _close(out, ref)
+
+
+def test_decode_untied_tables_and_late_query():
+    r = _random_case(11, 1, 2, 4, 64, 128, 3, 16, 16, 9, False, qpos_extra=-200, untied=True)
+    for mode in ("forward", "decode"):
+        out, ref = _run_random(r, torch.float32, mode)
+        _close(out, ref, 5e-4)
+
+
+def test_empty_cache_raises_value_error():
+    from unsloth_spectral import SpectralCache, spectral_attention_forward
+    cache = SpectralCache(8, 128, device="cuda", dtype=torch.float16)
+    Q = torch.zeros(1, 32, 1, 128, device="cuda", dtype=torch.float16)
+    cos = torch.ones(16, 128, device="cuda")
+    with pytest.raises(ValueError, match="Empty cache"):
+        spectral_attention_forward(Q, cache, cos, cos * 0, 3)
+
+
+def test_fully_masked_row_is_nan_like_reference():
+    r = _random_case(21, 1, 2, 2, 64, 64, 1, 16, 16, 4, True)
+    r["mask"][:, 0] = 0
+    out, ref = _run_random(r, torch.float32, "decode")
+    assert np.isnan(ref[:, 0]).all() and np.isnan(out[:, 0]).all()
+    _close(out[:, 1:], ref[:, 1:], 5e-4)
+
+
+# -------------------------------------------------------------- per-block helpers
+def test_block_score_and_value_match_reference():
+    from unsloth_spectral.kernels import spectral_score_forward, spectral_value_forward
+    c = gio.decode_case("decode_cfg0")
+    b0 = c["blocks"][0]
+    Q = torch.from_numpy(c["Q"]).cuda()
+    cos, sin = torch.from_numpy(c["cos"]).cuda(), torch.from_numpy(c["sin"]).cuda()
+    s = spectral_score_forward(Q, torch.from_numpy(b0.coeffs_K).cuda(), torch.from_numpy(b0.basis_K).cuda(), cos,
+                               sin, b0.start_position, int(c["qpos"]))
+    np.testing.assert_allclose(s.cpu().numpy(), c["scores_block0"], atol=2e-4, rtol=1e-4)
+    v = spectral_value_forward(torch.from_numpy(c["attn_block0"]).cuda(), torch.from_numpy(b0.coeffs_V).cuda(),
+                               torch.from_numpy(b0.basis_V).cuda(), 128)
+    np.testing.assert_allclose(v.cpu().numpy(), c["values_block0"], atol=1e-5, rtol=1e-4)
+
+
+def test_get_kv_matches_reference():
+    c = gio.decode_case("decode_cfg0")
+    cache = _golden_cache(c, torch.float32)
+    K, V = cache.get_kv()
+    assert abs(K.double().sum().item() - float(c["getkv_K_sum"])) < 1e-2
+    assert abs(V.double().sum().item() - float(c["getkv_V_sum"])) < 1e-2
+    Ko, Vo = so.get_kv(c["blocks"], c["hot_K"], c["hot_V"])
+    np.testing.assert_allclose(K.cpu().numpy(), Ko, atol=1e-4)
+    np.testing.assert_allclose(V.cpu().numpy(), Vo, atol=1e-4)
+    blocks = cache.cold_blocks
+    np.testing.assert_array_equal(blocks[1].coeffs_K.cpu().numpy(), c["blocks"][1].coeffs_K)
+    assert blocks[2].start_position == 1024
+
+
+# ------------------------------------------------------------------------------ rSVD
+@pytest.mark.parametrize("i", range(4))
+def test_rsvd_matches_reference_error(i):
+    from unsloth_spectral import _ops
+    z = gio.load("rsvd")
+    M16, Omega = gio.rsvd_inputs(z, i)
+    k, q = int(z[f"c{i}_k"]), int(z[f"c{i}_q"])
+    U, S, Vh = _ops.rsvd(M16.cuda(), Omega.cuda(), k, q)
+    M = M16.float().numpy()
+    err = so.relative_reconstruction_error(M, U.cpu().numpy(), S.cpu().numpy(), Vh.cpu().numpy())
+    assert np.abs(err - z[f"c{i}_err64"]).max() <= 1e-3
+    # where the reference's float32 run is not rounding-dominated, match it as well
+    stable = np.abs(z[f"c{i}_err"] - z[f"c{i}_err64"]) < 1e-4
+    assert np.abs(err - z[f"c{i}_err"])[stable].max(initial=0) <= 1e-3
+    np.testing.assert_allclose(S.cpu().numpy(), z[f"c{i}_S64"], rtol=2e-3)
+    # orthonormal factors
+    Uc, Vc = U.double(), Vh.double()
+    assert torch.allclose(Uc.transpose(1, 2) @ Uc, torch.eye(k, dtype=torch.float64, device="cuda")[None], atol=1e-4)
+    assert torch.allclose(Vc @ Vc.transpose(1, 2), torch.eye(k, dtype=torch.float64, device="cuda")[None], atol=1e-4)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+def test_public_rsvd_draws_the_reference_sketch(dtype):
+    """batched_randomized_svd draws its sketch as rsvd.py:95 does; with the same seed the
+    oracle (fed that sketch) gives the same reconstruction error."""
+    from unsloth_spectral import batched_randomized_svd
+    g = torch.Generator().manual_seed(5)
+    M = torch.randn(6, 512, 128, generator=g).to(dtype).cuda()
+    torch.manual_seed(123)
+    U, S, Vh = batched_randomized_svd(M, 16, n_iter=2, oversampling=8)
+    torch.manual_seed(123)
+    omega = torch.randn(6, 128, 24, device="cuda")
+    Mf = M.float().cpu().numpy()
+    ref = so.relative_reconstruction_error(Mf, *so.batched_randomized_svd(Mf, 16, 2, 8, omega.cpu().numpy()))
+    got = so.relative_reconstruction_error(Mf, U.float().cpu().numpy(), S.float().cpu().numpy(),
+                                           Vh.float().cpu().numpy())
+    assert np.abs(got - ref).max() <= 1e-3
+    assert U.dtype == dtype
+
+
+def test_cache_compression_codes_bit_exact_and_error_parity():
+    """Appending a full block compresses it on the device; the stored INT8 codes equal
+    the oracle quantiser applied to the kernel's own C = U*S, and the block's
+    reconstruction error matches the reference algorithm on the same sketch."""
+    from unsloth_spectral import SpectralCache, _ops
+    from unsloth_spectral import synthetic as syn
+    H, D, T = 8, 128, 512
+    K, V = syn.kv_per_head(1, 0, 1, H, T + 5, D, 24, 0.85)
+    cache = SpectralCache(H, D, block_size=T, k_rank_keys=16, k_rank_values=32, device="cuda",
+                          dtype=torch.float16, oversampling=8)
+    torch.manual_seed(77)
+    cache.append(K.half().cuda(), V.half().cuda())
+    assert cache.num_cold_blocks == 1 and cache.hot_len == 5
+    torch.manual_seed(77)
+    om_k = torch.randn(H, D, 24, device="cuda")
+    om_v = torch.randn(H, D, 40, device="cuda")
+    Kb = K[0, :, :T].half().cuda()
+    U, S, Vh = _ops.rsvd(Kb, om_k, 16, 2)
+    C = (U * S[:, None, :]).cpu().numpy()
+    _, mm, codes, scale = so.quantize_int8_batched(C)
+    t = cache.tiers
+    np.testing.assert_array_equal(t.codes_k[0, :, 0, :, :16].cpu().numpy(), codes)
+    assert (t.codes_k[0, :, 0, :, 16:] == 0).all()
+    np.testing.assert_array_equal(t.scale_k[0, :, 0].cpu().numpy(), scale)
+    np.testing.assert_array_equal(t.minmax_k[0, :, 0].cpu().numpy(), mm)
+    # reconstruction error of the stored block vs the oracle on the same sketches
+    Kr, Vr = cache.get_kv()
+    for X, Xr, om, k in ((K, Kr, om_k, 16), (V, Vr, om_v, 32)):
+        Xh = X[0, :, :T].half().float().numpy()
+        got = np.linalg.norm((Xr[0, :, :T].float().cpu().numpy() - Xh).reshape(H, -1), axis=1) / \
+            np.linalg.norm(Xh.reshape(H, -1), axis=1)
+        q, Vh_, mm_, codes_, sc_ = so.compress_tensor(Xh, k, om.cpu().numpy(), 2, 8)
+        ref = np.linalg.norm((np.matmul(q, Vh_) - Xh).reshape(H, -1), axis=1) / \
+            np.linalg.norm(Xh.reshape(H, -1), axis=1)
+        assert np.abs(got - ref).max() <= 1e-3, (got, ref)
+    # the hot remainder is the last 5 tokens
+    np.testing.assert_array_equal(cache.hot_K.cpu().numpy(), K[:, :, T:].half().numpy())
+    assert cache.hot_position_ids.cpu().tolist() == [[512, 513, 514, 515, 516]]

@@ -1,0 +1,379 @@
+// Spectral decode attention over the three-tier cache (host entry + generic kernels).
+//
+// Semantics follow unsloth_spectral/spectral_attention.py:117-349 (DISTANCE mode) and
+// unsloth_spectral/kernels/spectral_attention.py:684-857 (ABSOLUTE mode).  Both rotate
+// the query per key token; here the rotation is moved onto the reconstructed key, which
+// is the same number:
+//   score_t = Q . R^-1_{a_t}-rotated ... = sum_i Q1_i (c1 K1 - s2 K2) + Q2_i (s1 K1 + c2 K2)
+// with K~_t = scale_k * codes_t @ B_k, (c1, s1) = (cos, sin)[a_t, i], (c2, s2) the same
+// at i + D/2 (DISTANCE mode uses the first half for both, like apply_rope at
+// spectral_attention.py:80-114).  Hot keys are RoPE'd at their absolute positions.
+//
+// Pipeline: one partial (running max m, sum l, un-normalised output o[D]) per cold
+// block and (layer, sequence, KV head, q-head), written to the workspace, then one
+// kernel per (layer, sequence, KV head) that scores the hot tier and merges every
+// partial with the log-sum-exp rule into the output.
+#include <math.h>
+
+#include "spx_common.cuh"
+#include "spx_decode.cuh"
+
+namespace spx {
+
+constexpr int kMaxRep = 16;
+constexpr size_t kMaxSmem = 227 * 1024;
+
+// ------------------------------------------------------------------ cold, generic ---
+template <typename T, int RKT>
+__global__ void __launch_bounds__(256) cold_generic_kernel(DecodeParams p) {
+  const int j = blockIdx.x, g = blockIdx.y, lb = blockIdx.z;
+  const int b = lb % p.B;
+  const int D = p.D, half = D / 2, Tb = p.Tb, RV = p.RV, nrep = p.nrep;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  extern __shared__ float sm[];
+  float* sbk = sm;                  // [RKT][D]
+  float* sbv = sbk + RKT * D;       // [RV][D]
+  float* sq = sbv + RV * D;         // [nrep][D]
+  float* ssc = sq + nrep * D;       // [nrep][Tb]
+  float* svl = ssc + nrep * Tb;     // [nrep][RV]
+  float* sml = svl + nrep * RV;     // [nrep][2]
+  const int64_t lbg = (int64_t)lb * p.H + g;
+  const int64_t slot = lbg * p.NBc + j;
+  const T* bk = reinterpret_cast<const T*>(p.bk) + slot * RKT * D;
+  const T* bv = reinterpret_cast<const T*>(p.bv) + slot * (int64_t)RV * D;
+  const T* q = reinterpret_cast<const T*>(p.q) + ((int64_t)lb * p.Hq + (int64_t)g * nrep) * D;
+  for (int i = tid; i < RKT * D; i += blockDim.x) sbk[i] = to_f(bk[i]);
+  for (int i = tid; i < RV * D; i += blockDim.x) sbv[i] = to_f(bv[i]);
+  for (int i = tid; i < nrep * D; i += blockDim.x) sq[i] = to_f(q[i]);
+  __syncthreads();
+  const float sK = p.sk[slot] * p.scale, sV = p.sv[slot];
+  const int64_t p0 = p.bpos[j];
+  const bool second_half = (p.mode == SPX_ROPE_ABSOLUTE) && !p.tied;
+  for (int t = tid; t < Tb; t += blockDim.x) {
+    float c[RKT];
+    const int4* crow = reinterpret_cast<const int4*>(p.ck + (slot * Tb + t) * RKT);
+#pragma unroll
+    for (int v = 0; v < RKT / 16; ++v) {
+      const int4 w = crow[v];
+      const int ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int bb = 0; bb < 4; ++bb) c[v * 16 + u * 4 + bb] = (float)(int8_t)((ws[u] >> (8 * bb)) & 0xff);
+    }
+    const int64_t kp = p0 + t;
+    int64_t a = p.mode == SPX_ROPE_DISTANCE ? (p.qpos - kp > 0 ? p.qpos - kp : 0) : kp;
+    a = a < 0 ? 0 : (a >= p.rope_len ? p.rope_len - 1 : a);
+    const float* cr = p.cosT + a * D;
+    const float* sr = p.sinT + a * D;
+    float s[kMaxRep];
+#pragma unroll
+    for (int h = 0; h < kMaxRep; ++h) s[h] = 0.f;
+    for (int i = 0; i < half; ++i) {
+      float k1 = 0.f, k2 = 0.f;
+#pragma unroll
+      for (int r = 0; r < RKT; ++r) {
+        k1 = fmaf(c[r], sbk[r * D + i], k1);
+        k2 = fmaf(c[r], sbk[r * D + i + half], k2);
+      }
+      const float c1 = cr[i], s1 = sr[i];
+      const float c2 = second_half ? cr[i + half] : c1;
+      const float s2 = second_half ? sr[i + half] : s1;
+      const float kp1 = c1 * k1 - s2 * k2;
+      const float kp2 = s1 * k1 + c2 * k2;
+#pragma unroll
+      for (int h = 0; h < kMaxRep; ++h)
+        if (h < nrep) s[h] = fmaf(sq[h * D + i], kp1, fmaf(sq[h * D + i + half], kp2, s[h]));
+    }
+#pragma unroll
+    for (int h = 0; h < kMaxRep; ++h) {
+      if (h < nrep) {
+        float v = s[h] * sK;
+        if (p.mask && p.mask[((int64_t)b * p.Hq + g * nrep + h) * p.mask_stride + (int64_t)j * Tb + t] == 0)
+          v = -INFINITY;
+        ssc[h * Tb + t] = v;
+      }
+    }
+  }
+  __syncthreads();
+  for (int h = warp; h < nrep; h += nwarps) {
+    float m = -INFINITY;
+    for (int t = lane; t < Tb; t += 32) m = fmaxf(m, ssc[h * Tb + t]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int t = lane; t < Tb; t += 32) {
+      const float e = m == -INFINITY ? 0.f : __expf(ssc[h * Tb + t] - m);
+      ssc[h * Tb + t] = e;
+      l += e;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      sml[2 * h] = m;
+      sml[2 * h + 1] = l;
+    }
+  }
+  __syncthreads();
+  const int8_t* cvb = p.cv + slot * (int64_t)RV * Tb;
+  for (int pr = warp; pr < nrep * RV; pr += nwarps) {
+    const int h = pr / RV, r = pr - h * RV;
+    float acc = 0.f;
+    for (int t = lane; t < Tb; t += 32) acc = fmaf(ssc[h * Tb + t], (float)cvb[(int64_t)r * Tb + t], acc);
+    acc = warp_sum(acc);
+    if (lane == 0) svl[pr] = acc;
+  }
+  __syncthreads();
+  float* rec = p.ws + ((lbg * p.nparts + j) * nrep) * (int64_t)(D + 4);
+  for (int e = tid; e < nrep * D; e += blockDim.x) {
+    const int h = e / D, d = e - h * D;
+    float acc = 0.f;
+    for (int r = 0; r < RV; ++r) acc = fmaf(svl[h * RV + r], sbv[r * D + d], acc);
+    rec[(int64_t)h * (D + 4) + 4 + d] = acc * sV;
+  }
+  if (tid < nrep) {
+    rec[(int64_t)tid * (D + 4) + 0] = sml[2 * tid];
+    rec[(int64_t)tid * (D + 4) + 1] = sml[2 * tid + 1];
+  }
+}
+
+// ------------------------------------------------------------- hot tier + merge ---
+template <typename T>
+__global__ void __launch_bounds__(256) hot_merge_kernel(DecodeParams p) {
+  const int g = blockIdx.x, lb = blockIdx.y;
+  const int b = lb % p.B;
+  const int D = p.D, half = D / 2, nrep = p.nrep, hot = p.hot, nb = p.nblk;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  extern __shared__ float sm[];
+  float* sq = sm;                   // [nrep][D]
+  float* ssc = sq + nrep * D;       // [nrep][hot]
+  float* sml = ssc + nrep * hot;    // [nrep][2]
+  float* swt = sml + 2 * nrep;      // [nrep][nb + 1] merge weights, then 1/L
+  const int64_t lbg = (int64_t)lb * p.H + g;
+  const T* q = reinterpret_cast<const T*>(p.q) + ((int64_t)lb * p.Hq + (int64_t)g * nrep) * D;
+  for (int i = tid; i < nrep * D; i += blockDim.x) sq[i] = to_f(q[i]);
+  __syncthreads();
+  const T* hk = reinterpret_cast<const T*>(p.hk) + lbg * p.HC * D;
+  const T* hv = reinterpret_cast<const T*>(p.hv) + lbg * p.HC * D;
+  const bool second_half = (p.mode == SPX_ROPE_ABSOLUTE) && !p.tied;
+  for (int t = tid; t < hot; t += blockDim.x) {
+    int64_t a = p.hpos[t];
+    a = a < 0 ? 0 : (a >= p.rope_len ? p.rope_len - 1 : a);
+    const float* cr = p.cosT + a * D;
+    const float* sr = p.sinT + a * D;
+    const T* krow = hk + (int64_t)t * D;
+    float s[kMaxRep];
+#pragma unroll
+    for (int h = 0; h < kMaxRep; ++h) s[h] = 0.f;
+    for (int i = 0; i < half; ++i) {
+      const float k1 = to_f(krow[i]), k2 = to_f(krow[i + half]);
+      const float c1 = cr[i], s1 = sr[i];
+      const float c2 = second_half ? cr[i + half] : c1;
+      const float s2 = second_half ? sr[i + half] : s1;
+      const float kp1 = k1 * c1 - k2 * s1;   // apply_rope: x1*cos1 - x2*sin1
+      const float kp2 = k2 * c2 + k1 * s2;   //             x2*cos2 + x1*sin2
+#pragma unroll
+      for (int h = 0; h < kMaxRep; ++h)
+        if (h < nrep) s[h] = fmaf(sq[h * D + i], kp1, fmaf(sq[h * D + i + half], kp2, s[h]));
+    }
+#pragma unroll
+    for (int h = 0; h < kMaxRep; ++h) {
+      if (h < nrep) {
+        float v = s[h] * p.scale;
+        if (p.mask && p.mask[((int64_t)b * p.Hq + g * nrep + h) * p.mask_stride + (int64_t)nb * p.Tb + t] == 0)
+          v = -INFINITY;
+        ssc[h * hot + t] = v;
+      }
+    }
+  }
+  __syncthreads();
+  for (int h = warp; h < nrep; h += nwarps) {
+    float m = -INFINITY;
+    for (int t = lane; t < hot; t += 32) m = fmaxf(m, ssc[h * hot + t]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int t = lane; t < hot; t += 32) {
+      const float e = m == -INFINITY ? 0.f : __expf(ssc[h * hot + t] - m);
+      ssc[h * hot + t] = e;
+      l += e;
+    }
+    l = warp_sum(l);
+    // merge weights over the cold partials and the hot partial
+    const float* recs = p.ws + (lbg * p.nparts) * nrep * (int64_t)(D + 4);
+    float M = m;
+    for (int jj = lane; jj < nb; jj += 32) M = fmaxf(M, recs[((int64_t)jj * nrep + h) * (D + 4)]);
+    M = warp_max(M);
+    float L = 0.f;
+    for (int jj = lane; jj < nb; jj += 32) {
+      const float* r = recs + ((int64_t)jj * nrep + h) * (D + 4);
+      const float w = M == -INFINITY ? 0.f : __expf(r[0] - M);
+      swt[h * (nb + 1) + jj] = w;
+      L += w * r[1];
+    }
+    L = warp_sum(L);
+    if (lane == 0) {
+      const float wh = M == -INFINITY ? 0.f : __expf(m - M);
+      L += wh * l;
+      sml[2 * h] = wh;
+      sml[2 * h + 1] = (M == -INFINITY || L == 0.f) ? NAN : 1.f / L;  // fully masked -> NaN
+    }
+  }
+  __syncthreads();
+  T* out = reinterpret_cast<T*>(p.out) + ((int64_t)lb * p.Hq + (int64_t)g * nrep) * D;
+  const float* recs = p.ws + (lbg * p.nparts) * nrep * (int64_t)(D + 4);
+  for (int e = tid; e < nrep * D; e += blockDim.x) {
+    const int h = e / D, d = e - h * D;
+    float acc = 0.f;
+    for (int t = 0; t < hot; ++t) acc = fmaf(ssc[h * hot + t], to_f(hv[(int64_t)t * D + d]), acc);
+    acc *= sml[2 * h];
+    for (int jj = 0; jj < nb; ++jj) acc = fmaf(swt[h * (nb + 1) + jj], recs[((int64_t)jj * nrep + h) * (D + 4) + 4 + d], acc);
+    out[(int64_t)h * D + d] = from_f<T>(acc * sml[2 * h + 1]);
+  }
+}
+
+template <typename T, int RKT>
+static int launch_cold_generic(const DecodeParams& p, cudaStream_t st) {
+  const size_t smem = ((size_t)RKT * p.D + (size_t)p.RV * p.D + (size_t)p.nrep * p.D + (size_t)p.nrep * p.Tb +
+                       (size_t)p.nrep * p.RV + 2 * p.nrep) * sizeof(float);
+  SPX_REQUIRE(smem <= kMaxSmem, SPX_ERR_UNSUPPORTED, "cold tier needs %zu bytes of shared memory", smem);
+  cudaFuncSetAttribute(cold_generic_kernel<T, RKT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  dim3 grid(p.nblk, p.H, p.L * p.B);
+  cold_generic_kernel<T, RKT><<<grid, 256, smem, st>>>(p);
+  return launch_status("cold_generic_kernel");
+}
+
+template <typename T>
+static int launch_generic(const DecodeParams& p, cudaStream_t st) {
+  int rc = SPX_OK;
+  if (p.nblk > 0) {
+    switch (p.RK) {
+      case 16: rc = launch_cold_generic<T, 16>(p, st); break;
+      case 32: rc = launch_cold_generic<T, 32>(p, st); break;
+      case 48: rc = launch_cold_generic<T, 48>(p, st); break;
+      case 64: rc = launch_cold_generic<T, 64>(p, st); break;
+      default: set_error("rank_k %d not in {16,32,48,64}", p.RK); return SPX_ERR_UNSUPPORTED;
+    }
+    if (rc != SPX_OK) return rc;
+  }
+  const size_t smem = ((size_t)p.nrep * p.D + (size_t)p.nrep * p.hot + 2 * p.nrep + (size_t)p.nrep * (p.nblk + 1)) *
+                      sizeof(float);
+  SPX_REQUIRE(smem <= kMaxSmem, SPX_ERR_UNSUPPORTED,
+              "hot tier of %d tokens with %d blocks needs %zu bytes of shared memory", p.hot, p.nblk, smem);
+  cudaFuncSetAttribute(hot_merge_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  dim3 grid(p.H, p.L * p.B);
+  hot_merge_kernel<T><<<grid, 256, smem, st>>>(p);
+  return launch_status("hot_merge_kernel");
+}
+
+// ------------------------------------------------------------------- host side ---
+static int make_params(const spx_decode_args* a, DecodeParams* p) {
+  SPX_REQUIRE(a, SPX_ERR_NULL, "args is NULL");
+  SPX_REQUIRE(a->num_layers >= 1 && a->batch >= 1 && a->num_kv_heads >= 1 && a->num_q_heads >= 1,
+              SPX_ERR_SHAPE, "layers, batch and head counts must be >= 1");
+  SPX_REQUIRE(a->num_q_heads % a->num_kv_heads == 0, SPX_ERR_SHAPE, "num_q_heads %% num_kv_heads != 0");
+  const int nrep = a->num_q_heads / a->num_kv_heads;
+  SPX_REQUIRE(nrep <= kMaxRep, SPX_ERR_UNSUPPORTED, "GQA group %d > %d", nrep, kMaxRep);
+  SPX_REQUIRE(a->head_dim >= 16 && a->head_dim <= 256 && a->head_dim % 16 == 0, SPX_ERR_SHAPE,
+              "head_dim %d must be a multiple of 16 in [16, 256]", a->head_dim);
+  SPX_REQUIRE(dtype_ok(a->dtype), SPX_ERR_UNSUPPORTED, "bad dtype %d", a->dtype);
+  SPX_REQUIRE(a->rope_mode == SPX_ROPE_DISTANCE || a->rope_mode == SPX_ROPE_ABSOLUTE, SPX_ERR_SHAPE,
+              "bad rope_mode");
+  SPX_REQUIRE(a->num_blocks >= 0 && a->num_blocks <= a->block_capacity, SPX_ERR_SHAPE,
+              "num_blocks %d outside [0, block_capacity %d]", a->num_blocks, a->block_capacity);
+  SPX_REQUIRE(a->hot_len >= 0 && a->hot_len <= a->hot_capacity, SPX_ERR_SHAPE, "hot_len outside [0, hot_capacity]");
+  SPX_REQUIRE(a->num_blocks > 0 || a->hot_len > 0, SPX_ERR_EMPTY, "Empty cache - no keys available");
+  SPX_REQUIRE(a->q && a->out && a->cos_table && a->sin_table, SPX_ERR_NULL, "q, out, cos and sin are required");
+  SPX_REQUIRE(a->rope_len >= 1, SPX_ERR_SHAPE, "rope_len must be >= 1");
+  if (a->num_blocks > 0) {
+    SPX_REQUIRE(a->block_size >= 16 && a->block_size <= 1024 && a->block_size % 16 == 0, SPX_ERR_SHAPE,
+                "block_size %d must be a multiple of 16 in [16, 1024]", a->block_size);
+    SPX_REQUIRE(a->rank_k % 16 == 0 && a->rank_k >= 16 && a->rank_k <= 64 && a->rank_v % 16 == 0 &&
+                    a->rank_v >= 16 && a->rank_v <= 64,
+                SPX_ERR_UNSUPPORTED, "stored ranks must be 16, 32, 48 or 64");
+    SPX_REQUIRE(a->codes_k && a->codes_v && a->scale_k && a->scale_v && a->basis_k && a->basis_v && a->block_pos,
+                SPX_ERR_NULL, "cold-tier pointers are required when num_blocks > 0");
+    SPX_REQUIRE(aligned16(a->codes_k) && aligned16(a->codes_v) && aligned16(a->basis_k) && aligned16(a->basis_v),
+                SPX_ERR_ALIGN, "cold-tier tensors must be 16-byte aligned");
+  }
+  if (a->hot_len > 0)
+    SPX_REQUIRE(a->hot_k && a->hot_v && a->hot_pos, SPX_ERR_NULL, "hot-tier pointers are required when hot_len > 0");
+  if (a->mask)
+    SPX_REQUIRE(a->mask_stride >= a->num_blocks * a->block_size + a->hot_len, SPX_ERR_SHAPE,
+                "mask_stride shorter than the key count");
+  p->L = a->num_layers;
+  p->B = a->batch;
+  p->Hq = a->num_q_heads;
+  p->H = a->num_kv_heads;
+  p->D = a->head_dim;
+  p->Tb = a->num_blocks > 0 ? a->block_size : 0;
+  p->nblk = a->num_blocks;
+  p->NBc = a->block_capacity;
+  p->RK = a->rank_k;
+  p->RV = a->rank_v;
+  p->hot = a->hot_len;
+  p->HC = a->hot_capacity;
+  p->nrep = nrep;
+  p->mode = a->rope_mode;
+  p->tied = a->rope_tied ? 1 : 0;
+  p->rope_len = a->rope_len;
+  p->mask_stride = a->mask_stride;
+  p->nparts = a->num_blocks > 0 ? a->num_blocks : 1;
+  p->qpos = a->query_position;
+  p->scale = a->scale;
+  p->q = a->q;
+  p->ck = a->codes_k;
+  p->cv = a->codes_v;
+  p->sk = a->scale_k;
+  p->sv = a->scale_v;
+  p->bk = a->basis_k;
+  p->bv = a->basis_v;
+  p->bpos = a->block_pos;
+  p->hk = a->hot_k;
+  p->hv = a->hot_v;
+  p->hpos = a->hot_pos;
+  p->cosT = a->cos_table;
+  p->sinT = a->sin_table;
+  p->mask = a->mask;
+  p->out = a->out;
+  p->ws = reinterpret_cast<float*>(a->workspace);
+  return SPX_OK;
+}
+
+size_t decode_workspace_bytes(const DecodeParams& p) {
+  return (size_t)p.L * p.B * p.H * p.nparts * p.nrep * (p.D + 4) * sizeof(float);
+}
+
+int decode_dispatch(const DecodeParams& p, cudaStream_t st) {
+  if (decode_fast_supported(p)) return decode_fast_launch(p, st);
+  return SPX_DISPATCH_DTYPE(p.dtype, T, [&] { return launch_generic<T>(p, st); });
+}
+
+int decode_generic(const DecodeParams& p, cudaStream_t st) {
+  return SPX_DISPATCH_DTYPE(p.dtype, T, [&] { return launch_generic<T>(p, st); });
+}
+
+}  // namespace spx
+
+using namespace spx;
+
+extern "C" {
+
+size_t spx_decode_workspace_size(const spx_decode_args* a) {
+  DecodeParams p;
+  if (make_params(a, &p) != SPX_OK) return 0;
+  p.dtype = a->dtype;
+  return decode_workspace_bytes(p);
+}
+
+int spx_decode_attn(const spx_decode_args* a, void* stream) {
+  DecodeParams p;
+  int rc = make_params(a, &p);
+  if (rc != SPX_OK) return rc;
+  p.dtype = a->dtype;
+  const size_t need = decode_workspace_bytes(p);
+  if (p.nblk > 0) {
+    SPX_REQUIRE(a->workspace && a->workspace_bytes >= need, SPX_ERR_WORKSPACE,
+                "workspace of %zu bytes required, %zu given", need, a->workspace_bytes);
+  }
+  return decode_dispatch(p, (cudaStream_t)stream);
+}
+
+}  // extern "C"

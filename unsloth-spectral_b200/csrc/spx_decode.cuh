@@ -1,0 +1,38 @@
+// Parameters shared by the decode kernels (generic and fast paths).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace spx {
+
+struct DecodeParams {
+  int L, B, Hq, H, D, Tb, nblk, NBc, RK, RV, hot, HC, nrep, mode, tied, rope_len, mask_stride, nparts, dtype;
+  int64_t qpos;
+  float scale;
+  const void* q;
+  const int8_t* ck;
+  const int8_t* cv;
+  const float* sk;
+  const float* sv;
+  const void* bk;
+  const void* bv;
+  const int64_t* bpos;
+  const void* hk;
+  const void* hv;
+  const int64_t* hpos;
+  const float* cosT;
+  const float* sinT;
+  const uint8_t* mask;
+  void* out;
+  float* ws;  // cold partials: [L*B*H][nparts][nrep][D + 4] = (m, l, -, -, o[D])
+};
+
+size_t decode_workspace_bytes(const DecodeParams& p);
+int decode_dispatch(const DecodeParams& p, cudaStream_t st);
+int decode_generic(const DecodeParams& p, cudaStream_t st);
+
+// Fast cold-tier path (spx_decode_fast.cu): returns true when the shape is covered.
+bool decode_fast_supported(const DecodeParams& p);
+int decode_fast_launch(const DecodeParams& p, cudaStream_t st);
+
+}  // namespace spx

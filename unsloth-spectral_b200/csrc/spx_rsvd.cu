@@ -1,0 +1,500 @@
+// Batched randomized SVD + INT8 block compression (spx_rsvd_compress).
+//
+// Algorithm (unsloth_spectral/rsvd.py:74-157, spectral_cache.py:345-407):
+//   Y = M Omega; Q = orth(Y)
+//   repeat n_iter: Z = orth(M^T Q); Q = orth(M Z)      (subspace iteration)
+//   Bp^T = M^T Q                                        ([n, r])
+//   Bp Bp^T = W diag(lambda) W^T   (cyclic Jacobi, float64, parallel ordering)
+//   S = sqrt(lambda), Vh_j = W_j^T Bp / S_j, U = Q W     (truncated to k)
+//   C = U * S -> per-matrix INT8 codes, scale, (min, max); basis = Vh in basis dtype.
+// The reference runs the power iterations un-normalised; re-orthonormalising every
+// step spans the same subspace in exact arithmetic and avoids the float32 loss of the
+// un-normalised form.  orth() is classical Gram-Schmidt applied twice (CGS2), which is
+// as stable as Householder QR for these sizes.
+#include <math.h>
+
+#include "spx_common.cuh"
+#include "spx_rsvd.cuh"
+
+namespace spx {
+
+// ------------------------------------------------------------ Y = M X  (CUDA cores)
+// X: f32 [n][r] per matrix.  Y: f32 [m][r].  grid (ceil(m/64), Nb), 256 threads.
+template <typename T>
+__global__ void __launch_bounds__(256) gemm_mx_kernel(const T* __restrict__ M, int64_t ms,
+                                                      const float* __restrict__ X, float* __restrict__ Y, int m,
+                                                      int n, int r) {
+  extern __shared__ float sm[];
+  float* sx = sm;            // [n][r]
+  float* smt = sx + n * r;   // [64][n + 1]
+  const int i = blockIdx.y, row0 = blockIdx.x * 64;
+  const T* Mi = M + (int64_t)i * ms;
+  const float* Xi = X + (int64_t)i * n * r;
+  for (int e = threadIdx.x; e < n * r; e += blockDim.x) sx[e] = Xi[e];
+  const int rows = min(64, m - row0);
+  for (int e = threadIdx.x; e < rows * n; e += blockDim.x) {
+    const int t = e / n, d = e - t * n;
+    smt[t * (n + 1) + d] = to_f(Mi[(int64_t)(row0 + t) * n + d]);
+  }
+  __syncthreads();
+  float* Yi = Y + (int64_t)i * m * r;
+  for (int e = threadIdx.x; e < rows * r; e += blockDim.x) {
+    const int t = e / r, c = e - t * r;
+    float acc = 0.f;
+    for (int d = 0; d < n; ++d) acc = fmaf(smt[t * (n + 1) + d], sx[d * r + c], acc);
+    Yi[(int64_t)(row0 + t) * r + c] = acc;
+  }
+}
+
+// ---------------------------------------------------------- Z = M^T Y (CUDA cores)
+// Y: f32 [m][r]; Z: f32 [n][r].  grid (ceil(n/32), Nb), 256 threads.
+template <typename T>
+__global__ void __launch_bounds__(256) gemm_mty_kernel(const T* __restrict__ M, int64_t ms,
+                                                       const float* __restrict__ Y, float* __restrict__ Z, int m,
+                                                       int n, int r) {
+  __shared__ float smt[64][33];
+  __shared__ float sy[64][65];
+  const int i = blockIdx.y, col0 = blockIdx.x * 32;
+  const int cols = min(32, n - col0);
+  const T* Mi = M + (int64_t)i * ms;
+  const float* Yi = Y + (int64_t)i * m * r;
+  float acc[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) acc[u] = 0.f;
+  // thread owns outputs e = tid + 256*u, (col = e / r, c = e % r) for e < 32*r
+  for (int t0 = 0; t0 < m; t0 += 64) {
+    const int rows = min(64, m - t0);
+    __syncthreads();
+    for (int e = threadIdx.x; e < 64 * 32; e += blockDim.x) {
+      const int t = e / 32, d = e - t * 32;
+      smt[t][d] = (t < rows && d < cols) ? to_f(Mi[(int64_t)(t0 + t) * n + col0 + d]) : 0.f;
+    }
+    for (int e = threadIdx.x; e < 64 * r; e += blockDim.x) {
+      const int t = e / r, c = e - t * r;
+      sy[t][c] = t < rows ? Yi[(int64_t)(t0 + t) * r + c] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int e = threadIdx.x + 256 * u;
+      if (e < 32 * r) {
+        const int d = e / r, c = e - d * r;
+        float a = acc[u];
+        for (int t = 0; t < 64; ++t) a = fmaf(smt[t][d], sy[t][c], a);
+        acc[u] = a;
+      }
+    }
+  }
+  float* Zi = Z + (int64_t)i * n * r;
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const int e = threadIdx.x + 256 * u;
+    if (e < 32 * r) {
+      const int d = e / r, c = e - d * r;
+      if (d < cols) Zi[(int64_t)(col0 + d) * r + c] = acc[u];
+    }
+  }
+}
+
+// ------------------------------------------------ in-place CGS2 orthonormalisation
+// X: f32 [rows][r] per matrix, one CTA per matrix, the matrix held in shared memory.
+__global__ void __launch_bounds__(256) orth_kernel(float* __restrict__ X, int rows, int r) {
+  extern __shared__ float sm[];
+  float* sx = sm;                 // [rows][r]
+  float* coef = sx + rows * r;    // [r]
+  __shared__ float red[32];
+  const int i = blockIdx.x;
+  float* Xi = X + (int64_t)i * rows * r;
+  for (int e = threadIdx.x; e < rows * r; e += blockDim.x) sx[e] = Xi[e];
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int j = 0; j < r; ++j) {
+    for (int pass = 0; pass < 2; ++pass) {
+      for (int c = warp; c < j; c += nw) {
+        float a = 0.f;
+        for (int t = lane; t < rows; t += 32) a = fmaf(sx[t * r + c], sx[t * r + j], a);
+        a = warp_sum(a);
+        if (lane == 0) coef[c] = a;
+      }
+      __syncthreads();
+      for (int t = threadIdx.x; t < rows; t += blockDim.x) {
+        float v = sx[t * r + j];
+        for (int c = 0; c < j; ++c) v = fmaf(-coef[c], sx[t * r + c], v);
+        sx[t * r + j] = v;
+      }
+      __syncthreads();
+    }
+    float a = 0.f;
+    for (int t = threadIdx.x; t < rows; t += blockDim.x) a = fmaf(sx[t * r + j], sx[t * r + j], a);
+    a = warp_sum(a);
+    if (lane == 0) red[warp] = a;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float s = 0.f;
+      for (int w = 0; w < nw; ++w) s += red[w];
+      red[0] = s > 1e-36f ? rsqrtf(s) : 0.f;  // a numerically zero column stays zero
+    }
+    __syncthreads();
+    const float inv = red[0];
+    for (int t = threadIdx.x; t < rows; t += blockDim.x) sx[t * r + j] *= inv;
+    __syncthreads();
+  }
+  for (int e = threadIdx.x; e < rows * r; e += blockDim.x) Xi[e] = sx[e];
+}
+
+// ----------------------------------------------- small SVD through a Jacobi eigensolve
+// Z = Bp^T: f32 [n][r].  Outputs Wk f32 [r][k], S f32 [k], Vh f32 [k][n].
+__global__ void __launch_bounds__(256) small_svd_kernel(const float* __restrict__ Z, float* __restrict__ Wk,
+                                                        float* __restrict__ S, float* __restrict__ Vh, int n, int r,
+                                                        int k) {
+  extern __shared__ double smd[];
+  const int rp = (r + 1) & ~1;        // padded to even for the round-robin ordering
+  double* G = smd;                    // [rp][rp]
+  double* W = G + rp * rp;            // [rp][rp]
+  double* cs = W + rp * rp;           // [rp/2][2]
+  int* pairs = reinterpret_cast<int*>(cs + rp);   // [rp]
+  int* perm = pairs + rp;                          // [rp]
+  float* sz = reinterpret_cast<float*>(perm + rp); // [n][r]
+  __shared__ double off_s[32];
+  __shared__ int done;
+  const int i = blockIdx.x;
+  const float* Zi = Z + (int64_t)i * n * r;
+  for (int e = threadIdx.x; e < n * r; e += blockDim.x) sz[e] = Zi[e];
+  __syncthreads();
+  // Gram matrix in float64, identity for the padding index
+  for (int e = threadIdx.x; e < rp * rp; e += blockDim.x) {
+    const int a = e / rp, b = e - a * rp;
+    double g = 0.0;
+    if (a < r && b < r) {
+      for (int d = 0; d < n; ++d) g += (double)sz[d * r + a] * (double)sz[d * r + b];
+    }
+    G[e] = g;
+    W[e] = (a == b) ? 1.0 : 0.0;
+  }
+  if (threadIdx.x < rp) pairs[threadIdx.x] = threadIdx.x;
+  if (threadIdx.x == 0) done = 0;
+  __syncthreads();
+  const int np = rp / 2;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int sweep = 0; sweep < 30 && !done; ++sweep) {
+    for (int round = 0; round < rp - 1; ++round) {
+      // pair u couples pairs[u] and pairs[rp-1-u]
+      if (threadIdx.x < np) {
+        int p = pairs[threadIdx.x], q = pairs[rp - 1 - threadIdx.x];
+        if (p > q) { const int tmp = p; p = q; q = tmp; }
+        double c = 1.0, s = 0.0;
+        const double apq = G[p * rp + q];
+        if (q < r && fabs(apq) > 1e-300) {
+          const double tau = (G[q * rp + q] - G[p * rp + p]) / (2.0 * apq);
+          const double t = (tau >= 0 ? 1.0 : -1.0) / (fabs(tau) + sqrt(1.0 + tau * tau));
+          c = 1.0 / sqrt(1.0 + t * t);
+          s = t * c;
+        }
+        cs[2 * threadIdx.x] = c;
+        cs[2 * threadIdx.x + 1] = s;
+      }
+      __syncthreads();
+      // rows: new_p = c row_p - s row_q ; new_q = s row_p + c row_q
+      for (int e = threadIdx.x; e < np * rp; e += blockDim.x) {
+        const int u = e / rp, col = e - u * rp;
+        int p = pairs[u], q = pairs[rp - 1 - u];
+        if (p > q) { const int tmp = p; p = q; q = tmp; }
+        const double c = cs[2 * u], s = cs[2 * u + 1];
+        const double gp = G[p * rp + col], gq = G[q * rp + col];
+        G[p * rp + col] = c * gp - s * gq;
+        G[q * rp + col] = s * gp + c * gq;
+      }
+      __syncthreads();
+      // columns of G and W
+      for (int e = threadIdx.x; e < np * rp; e += blockDim.x) {
+        const int u = e / rp, row = e - u * rp;
+        int p = pairs[u], q = pairs[rp - 1 - u];
+        if (p > q) { const int tmp = p; p = q; q = tmp; }
+        const double c = cs[2 * u], s = cs[2 * u + 1];
+        const double gp = G[row * rp + p], gq = G[row * rp + q];
+        G[row * rp + p] = c * gp - s * gq;
+        G[row * rp + q] = s * gp + c * gq;
+        const double wp = W[row * rp + p], wq = W[row * rp + q];
+        W[row * rp + p] = c * wp - s * wq;
+        W[row * rp + q] = s * wp + c * wq;
+      }
+      __syncthreads();
+      // rotate the tournament: keep pairs[0], shift the rest by one
+      if (threadIdx.x == 0) {
+        const int last = pairs[rp - 1];
+        for (int u = rp - 1; u > 1; --u) pairs[u] = pairs[u - 1];
+        pairs[1] = last;
+      }
+      __syncthreads();
+    }
+    // convergence: off-diagonal mass relative to the diagonal
+    double off = 0.0, dia = 0.0;
+    for (int e = threadIdx.x; e < r * r; e += blockDim.x) {
+      const int a = e / r, b = e - a * r;
+      const double g = G[a * rp + b];
+      if (a == b) dia += g * g; else off += g * g;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      off += __shfl_xor_sync(0xffffffffu, off, o);
+      dia += __shfl_xor_sync(0xffffffffu, dia, o);
+    }
+    if (lane == 0) {
+      off_s[warp] = off;
+      off_s[16 + warp] = dia;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double o2 = 0.0, d2 = 0.0;
+      for (int w = 0; w < nw; ++w) {
+        o2 += off_s[w];
+        d2 += off_s[16 + w];
+      }
+      if (o2 <= 1e-28 * d2 || d2 == 0.0) done = 1;
+    }
+    __syncthreads();
+  }
+  // order eigenvalues descending
+  if (threadIdx.x == 0) {
+    for (int a = 0; a < r; ++a) perm[a] = a;
+    for (int a = 0; a < r; ++a) {
+      int best = a;
+      for (int b = a + 1; b < r; ++b)
+        if (G[perm[b] * rp + perm[b]] > G[perm[best] * rp + perm[best]]) best = b;
+      const int tmp = perm[a];
+      perm[a] = perm[best];
+      perm[best] = tmp;
+    }
+  }
+  __syncthreads();
+  const double lam0 = fmax(G[perm[0] * rp + perm[0]], 0.0);
+  for (int j = threadIdx.x; j < k; j += blockDim.x) {
+    const double lam = fmax(G[perm[j] * rp + perm[j]], 0.0);
+    S[(int64_t)i * k + j] = (float)sqrt(lam);
+  }
+  for (int e = threadIdx.x; e < r * k; e += blockDim.x) {
+    const int a = e / k, j = e - a * k;
+    Wk[(int64_t)i * r * k + e] = (float)W[a * rp + perm[j]];
+  }
+  for (int e = threadIdx.x; e < k * n; e += blockDim.x) {
+    const int j = e / n, d = e - j * n;
+    const int pj = perm[j];
+    const double lam = fmax(G[pj * rp + pj], 0.0);
+    double v = 0.0;
+    if (lam > 1e-24 * lam0 && lam > 0.0) {
+      for (int a = 0; a < r; ++a) v += W[a * rp + pj] * (double)sz[d * r + a];
+      v /= sqrt(lam);
+    }
+    Vh[(int64_t)i * k * n + e] = (float)v;
+  }
+}
+
+// ------------------------------------------------- lift, C = U S, INT8 quantisation
+__global__ void __launch_bounds__(256) lift_quant_kernel(LiftParams p) {
+  extern __shared__ float sm[];
+  const int m = p.m, r = p.r, k = p.k, n = p.n;
+  float* sw = sm;                 // [r][k]
+  float* sc = sw + r * k;         // [m][k]  C = U * S
+  __shared__ float ss[64];
+  __shared__ float red[3][32];
+  const int i = blockIdx.x;
+  for (int e = threadIdx.x; e < r * k; e += blockDim.x) sw[e] = p.Wk[(int64_t)i * r * k + e];
+  if (threadIdx.x < k) ss[threadIdx.x] = p.Sw[(int64_t)i * k + threadIdx.x];
+  __syncthreads();
+  const float* Qi = p.Q + (int64_t)i * m * r;
+  float mn = INFINITY, mx = -INFINITY, am = 0.f;
+  for (int e = threadIdx.x; e < m * k; e += blockDim.x) {
+    const int t = e / k, j = e - t * k;
+    float u = 0.f;
+    for (int a = 0; a < r; ++a) u = fmaf(Qi[(int64_t)t * r + a], sw[a * k + j], u);
+    if (p.U) p.U[(int64_t)i * m * k + e] = u;
+    const float c = u * ss[j];
+    sc[e] = c;
+    mn = fminf(mn, c);
+    mx = fmaxf(mx, c);
+    am = fmaxf(am, fabsf(c));
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (lane == 0) {
+    red[0][warp] = mn;
+    red[1][warp] = mx;
+    red[2][warp] = am;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < nw; ++w) {
+      mn = fminf(mn, red[0][w]);
+      mx = fmaxf(mx, red[1][w]);
+      am = fmaxf(am, red[2][w]);
+    }
+    red[0][0] = mn;
+    red[1][0] = mx;
+    red[2][0] = __fdiv_rn(fmaxf(am, 1e-8f), 127.0f);
+  }
+  __syncthreads();
+  const float scale = red[2][0];
+  if (threadIdx.x == 0) {
+    if (p.codes) p.qscale[(int64_t)i * p.scale_mat_stride] = scale;
+    if (p.qminmax) {
+      p.qminmax[(int64_t)i * p.minmax_mat_stride] = red[0][0];
+      p.qminmax[(int64_t)i * p.minmax_mat_stride + 1] = red[1][0];
+    }
+  }
+  if (p.codes) {
+    const int kp = p.rank_pad;
+    int8_t* ci = p.codes + (int64_t)i * p.codes_mat_stride;
+    for (int e = threadIdx.x; e < m * kp; e += blockDim.x) {
+      int t, j;
+      if (p.codes_j_stride == 1) { t = e / kp; j = e - t * kp; }   // walk the contiguous index fastest
+      else { j = e / m; t = e - j * m; }
+      const int8_t v = j < k ? (int8_t)(int)rintf(__fdiv_rn(sc[t * k + j], scale)) : (int8_t)0;
+      ci[(int64_t)t * p.codes_t_stride + (int64_t)j * p.codes_j_stride] = v;
+    }
+  }
+  if (p.S && threadIdx.x < k) p.S[(int64_t)i * k + threadIdx.x] = ss[threadIdx.x];
+  const float* Vhw = p.Vhw + (int64_t)i * k * n;
+  if (p.Vh)
+    for (int e = threadIdx.x; e < k * n; e += blockDim.x) p.Vh[(int64_t)i * k * n + e] = Vhw[e];
+  if (p.basis) {
+    const int kp = p.rank_pad;
+    for (int e = threadIdx.x; e < kp * n; e += blockDim.x) {
+      const float v = e < k * n ? Vhw[e] : 0.f;
+      const int64_t o = (int64_t)i * p.basis_mat_stride + e;
+      if (p.basis_dtype == SPX_F32) reinterpret_cast<float*>(p.basis)[o] = v;
+      else if (p.basis_dtype == SPX_F16) reinterpret_cast<__half*>(p.basis)[o] = __float2half_rn(v);
+      else reinterpret_cast<__nv_bfloat16*>(p.basis)[o] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
+// ------------------------------------------------------------------- host side ---
+static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+struct RsvdWs {
+  float *Y, *Z, *Wk, *S, *Vh;
+  size_t bytes;
+};
+
+static RsvdWs carve(const spx_rsvd_args* a, char* base) {
+  RsvdWs w;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    char* p = base ? base + off : nullptr;
+    off += align256(bytes);
+    return reinterpret_cast<float*>(p);
+  };
+  const size_t Nb = a->num_mats;
+  w.Y = take(Nb * a->m * a->r * sizeof(float));
+  w.Z = take(Nb * a->n * a->r * sizeof(float));
+  w.Wk = take(Nb * a->r * a->k * sizeof(float));
+  w.S = take(Nb * a->k * sizeof(float));
+  w.Vh = take(Nb * a->k * a->n * sizeof(float));
+  w.bytes = off;
+  return w;
+}
+
+static int validate(const spx_rsvd_args* a) {
+  SPX_REQUIRE(a, SPX_ERR_NULL, "args is NULL");
+  SPX_REQUIRE(a->num_mats >= 0, SPX_ERR_SHAPE, "num_mats < 0");
+  SPX_REQUIRE(a->m >= 16 && a->m <= 1024 && a->n >= 16 && a->n <= 128, SPX_ERR_SHAPE,
+              "matrix %dx%d outside [16,1024]x[16,128]", a->m, a->n);
+  SPX_REQUIRE(a->k >= 1 && a->k <= 64 && a->r > a->k && a->r <= 64 && a->r <= (a->m < a->n ? a->m : a->n) - 2,
+              SPX_ERR_SHAPE, "need 1 <= k < r <= min(64, min(m,n)-2); got k=%d r=%d", a->k, a->r);
+  SPX_REQUIRE(a->n_iter >= 0 && a->n_iter <= 8, SPX_ERR_SHAPE, "n_iter %d outside [0, 8]", a->n_iter);
+  SPX_REQUIRE(dtype_ok(a->in_dtype), SPX_ERR_UNSUPPORTED, "bad input dtype");
+  SPX_REQUIRE((size_t)a->m * a->r * 4 + 4 * 64 <= 200 * 1024, SPX_ERR_UNSUPPORTED, "m*r too large for one CTA");
+  SPX_REQUIRE((size_t)a->m * a->k * 4 + (size_t)a->r * a->k * 4 <= 200 * 1024, SPX_ERR_UNSUPPORTED,
+              "m*k too large for one CTA");
+  if (a->num_mats == 0) return SPX_OK;
+  SPX_REQUIRE(a->M && a->omega, SPX_ERR_NULL, "M and omega are required");
+  SPX_REQUIRE(a->M_mat_stride == 0 || a->M_mat_stride >= (int64_t)a->m * a->n, SPX_ERR_SHAPE,
+              "M_mat_stride smaller than m*n");
+  if (a->codes) {
+    SPX_REQUIRE(a->qscale, SPX_ERR_NULL, "qscale is required with codes");
+    SPX_REQUIRE(a->codes_rank_pad >= a->k, SPX_ERR_SHAPE, "codes_rank_pad < k");
+    SPX_REQUIRE(a->codes_j_stride == 1 || a->codes_t_stride == 1, SPX_ERR_SHAPE,
+                "codes must be token-major or rank-major");
+  }
+  if (a->basis) {
+    SPX_REQUIRE(dtype_ok(a->basis_dtype), SPX_ERR_UNSUPPORTED, "bad basis dtype");
+    SPX_REQUIRE(a->codes_rank_pad >= a->k, SPX_ERR_SHAPE, "codes_rank_pad < k");
+  }
+  return SPX_OK;
+}
+
+template <typename T>
+static int run_chain(const spx_rsvd_args* a, const RsvdWs& w, cudaStream_t st) {
+  const int Nb = a->num_mats, m = a->m, n = a->n, r = a->r, k = a->k;
+  const T* M = reinterpret_cast<const T*>(a->M);
+  const int64_t ms = a->M_mat_stride > 0 ? a->M_mat_stride : (int64_t)m * n;
+  const size_t smx = ((size_t)n * r + 64 * (size_t)(n + 1)) * sizeof(float);
+  cudaFuncSetAttribute(gemm_mx_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smx);
+  cudaFuncSetAttribute(orth_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+  const dim3 gmx((m + 63) / 64, Nb), gmty((n + 31) / 32, Nb);
+  auto orth = [&](float* X, int rows) {
+    orth_kernel<<<Nb, 256, ((size_t)rows * r + r) * sizeof(float), st>>>(X, rows, r);
+  };
+  gemm_mx_kernel<T><<<gmx, 256, smx, st>>>(M, ms, a->omega, w.Y, m, n, r);
+  orth(w.Y, m);
+  for (int it = 0; it < a->n_iter; ++it) {
+    gemm_mty_kernel<T><<<gmty, 256, 0, st>>>(M, ms, w.Y, w.Z, m, n, r);
+    orth(w.Z, n);
+    gemm_mx_kernel<T><<<gmx, 256, smx, st>>>(M, ms, w.Z, w.Y, m, n, r);
+    orth(w.Y, m);
+  }
+  gemm_mty_kernel<T><<<gmty, 256, 0, st>>>(M, ms, w.Y, w.Z, m, n, r);
+  int rc = launch_status("rsvd gemm/orth chain");
+  if (rc != SPX_OK) return rc;
+  const int rp = (r + 1) & ~1;
+  const size_t ssvd = (2 * (size_t)rp * rp + rp) * sizeof(double) + 2 * rp * sizeof(int) + (size_t)n * r * sizeof(float);
+  cudaFuncSetAttribute(small_svd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssvd);
+  small_svd_kernel<<<Nb, 256, ssvd, st>>>(w.Z, w.Wk, w.S, w.Vh, n, r, k);
+  rc = launch_status("small_svd_kernel");
+  if (rc != SPX_OK) return rc;
+  LiftParams lp;
+  lp.m = m; lp.n = n; lp.r = r; lp.k = k;
+  lp.Q = w.Y; lp.Wk = w.Wk; lp.Sw = w.S; lp.Vhw = w.Vh;
+  lp.U = a->U; lp.S = a->S; lp.Vh = a->Vh;
+  lp.codes = a->codes;
+  lp.codes_mat_stride = a->codes_mat_stride;
+  lp.codes_t_stride = a->codes_t_stride;
+  lp.codes_j_stride = a->codes_j_stride;
+  lp.rank_pad = a->codes_rank_pad > k ? a->codes_rank_pad : k;
+  lp.qscale = a->qscale; lp.scale_mat_stride = a->scale_mat_stride;
+  lp.qminmax = a->qminmax; lp.minmax_mat_stride = a->minmax_mat_stride;
+  lp.basis = a->basis; lp.basis_dtype = a->basis_dtype; lp.basis_mat_stride = a->basis_mat_stride;
+  const size_t slq = ((size_t)r * k + (size_t)m * k) * sizeof(float);
+  cudaFuncSetAttribute(lift_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)slq);
+  lift_quant_kernel<<<Nb, 256, slq, st>>>(lp);
+  return launch_status("lift_quant_kernel");
+}
+
+}  // namespace spx
+
+using namespace spx;
+
+extern "C" {
+
+size_t spx_rsvd_workspace_size(const spx_rsvd_args* a) {
+  if (validate(a) != SPX_OK) return 0;
+  return carve(a, nullptr).bytes;
+}
+
+int spx_rsvd_compress(const spx_rsvd_args* a, void* stream) {
+  int rc = validate(a);
+  if (rc != SPX_OK) return rc;
+  if (a->num_mats == 0) return SPX_OK;
+  const RsvdWs need = carve(a, nullptr);
+  SPX_REQUIRE(a->workspace && a->workspace_bytes >= need.bytes, SPX_ERR_WORKSPACE,
+              "workspace of %zu bytes required, %zu given", need.bytes, a->workspace_bytes);
+  SPX_REQUIRE((reinterpret_cast<uintptr_t>(a->workspace) & 255u) == 0, SPX_ERR_ALIGN,
+              "workspace must be 256-byte aligned");
+  const RsvdWs w = carve(a, reinterpret_cast<char*>(a->workspace));
+  return SPX_DISPATCH_DTYPE(a->in_dtype, T, [&] { return run_chain<T>(a, w, (cudaStream_t)stream); });
+}
+
+}  // extern "C"

@@ -1,0 +1,187 @@
+"""Tensor-level wrappers over the spx C ABI.  Every function here launches CUDA work
+through ``libspx.so``; none has a CPU or pure-torch fallback."""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from . import _native as N
+
+_rope_cache = {}
+
+
+def _key(t: torch.Tensor):
+    return (t.data_ptr(), tuple(t.shape), tuple(t.stride()), t.dtype, t._version)
+
+
+def rope_table_f32(t: torch.Tensor, device) -> torch.Tensor:
+    """``t`` as a contiguous float32 ``[rope_len, D]`` table on ``device``."""
+    if t.dim() == 3 and t.shape[0] == 1:
+        t = t[0]
+    if t.dim() != 2:
+        raise ValueError(f"cos/sin must be [max_len, head_dim] tables, got shape {tuple(t.shape)}")
+    return t.to(device=device, dtype=torch.float32).contiguous()
+
+
+def rope_tied(cos: torch.Tensor, sin: torch.Tensor) -> bool:
+    """True when both tables repeat their first half (HF ``cat(freqs, freqs)`` layout).
+    Memoised per tensor version, so the device comparison runs once per table."""
+    k = (_key(cos), _key(sin))
+    v = _rope_cache.get(k)
+    if v is None:
+        h = cos.shape[-1] // 2
+        v = bool(torch.equal(cos[..., :h], cos[..., h:]) and torch.equal(sin[..., :h], sin[..., h:]))
+        if len(_rope_cache) > 64:
+            _rope_cache.clear()
+        _rope_cache[k] = v
+    return v
+
+
+def quantize_int8(x: torch.Tensor):
+    """Per-leading-index INT8 quantisation; returns (codes int8, scale f32 [N],
+    minmax f32 [N, 2], dequantised f32) -- bit-exact with the reference's
+    ``_quantize_int8_batched``."""
+    lib = N.lib_for(x.device)
+    xf = x.to(torch.float32).contiguous()
+    N_ = xf.shape[0]
+    codes = torch.empty(xf.shape, dtype=torch.int8, device=x.device)
+    scale = torch.empty(N_, dtype=torch.float32, device=x.device)
+    minmax = torch.empty(N_, 2, dtype=torch.float32, device=x.device)
+    deq = torch.empty_like(xf)
+    a = N.QuantArgs(num_groups=N_, group_elems=xf[0].numel() if N_ else 1, x=N.ptr(xf), codes=N.ptr(codes),
+                    scale=N.ptr(scale), minmax=N.ptr(minmax), dequant=N.ptr(deq))
+    N.check(lib, lib.spx_quantize_int8(a, N.stream_handle(x.device)), "spx_quantize_int8")
+    return codes, scale, minmax, deq
+
+
+def rsvd(M: torch.Tensor, omega: torch.Tensor, k: int, n_iter: int, *, want_factors: bool = True,
+         codes: Optional[torch.Tensor] = None, codes_strides=None, rank_pad: Optional[int] = None,
+         qscale: Optional[torch.Tensor] = None, scale_stride: int = 1, qminmax: Optional[torch.Tensor] = None,
+         minmax_stride: int = 2, basis: Optional[torch.Tensor] = None, basis_stride: int = 0,
+         M_mat_stride: int = 0, num_mats: Optional[int] = None, m: Optional[int] = None,
+         n: Optional[int] = None):
+    """Run ``spx_rsvd_compress``.  ``M`` is ``[Nb, m, n]`` (or a strided view described by
+    ``num_mats``/``m``/``n``/``M_mat_stride``); ``omega`` is ``[Nb, n, r]`` float32.
+    Returns (U, S, Vh) float32 when ``want_factors``; compressed outputs are written in
+    place into ``codes``/``qscale``/``qminmax``/``basis``."""
+    lib = N.lib_for(M.device)
+    if num_mats is None:
+        num_mats, m, n = M.shape
+    r = omega.shape[-1]
+    omega = omega.to(torch.float32).contiguous()
+    dev = M.device
+    U = S = Vh = None
+    if want_factors:
+        U = torch.empty(num_mats, m, k, dtype=torch.float32, device=dev)
+        S = torch.empty(num_mats, k, dtype=torch.float32, device=dev)
+        Vh = torch.empty(num_mats, k, n, dtype=torch.float32, device=dev)
+    cs = codes_strides or (0, 0, 0)
+    a = N.RsvdArgs(num_mats=num_mats, m=m, n=n, k=k, r=r, n_iter=n_iter, in_dtype=N.dtype_code(M.dtype),
+                   M=N.ptr(M), omega=N.ptr(omega), U=N.ptr(U), S=N.ptr(S), Vh=N.ptr(Vh),
+                   M_mat_stride=M_mat_stride, codes=N.ptr(codes), codes_mat_stride=cs[0], codes_t_stride=cs[1],
+                   codes_j_stride=cs[2], codes_rank_pad=rank_pad or k, qscale=N.ptr(qscale),
+                   scale_mat_stride=scale_stride, qminmax=N.ptr(qminmax), minmax_mat_stride=minmax_stride,
+                   basis=N.ptr(basis), basis_dtype=N.dtype_code(basis.dtype) if basis is not None else 0,
+                   basis_mat_stride=basis_stride)
+    need = lib.spx_rsvd_workspace_size(a)
+    if need == 0 and num_mats > 0:
+        N.check(lib, lib.spx_rsvd_compress(a, N.stream_handle(dev)), "spx_rsvd_compress")
+    ws = N.workspace(dev, need)
+    a.workspace, a.workspace_bytes = N.ptr(ws), ws.numel()
+    N.check(lib, lib.spx_rsvd_compress(a, N.stream_handle(dev)), "spx_rsvd_compress")
+    return U, S, Vh
+
+
+def decode(q: torch.Tensor, tiers, cos: torch.Tensor, sin: torch.Tensor, query_position: int, *,
+           rope_mode: int, mask: Optional[torch.Tensor] = None, scale: Optional[float] = None,
+           out: Optional[torch.Tensor] = None, tied: Optional[bool] = None) -> torch.Tensor:
+    """Run ``spx_decode_attn`` over ``tiers`` (a ``DeviceTiers``).  ``q`` is
+    ``[L, B, H_q, D]`` in the tiers' dtype; returns ``[L, B, H_q, D]``."""
+    dev = q.device
+    lib = N.lib_for(dev)
+    L, B, Hq, D = q.shape
+    t = tiers
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    cos32 = rope_table_f32(cos, dev)
+    sin32 = rope_table_f32(sin, dev)
+    if tied is None:
+        tied = rope_tied(cos32, sin32)
+    if out is None:
+        out = torch.empty(L, B, Hq, D, dtype=t.dtype, device=dev)
+    mask_u8 = None
+    mask_stride = 0
+    if mask is not None:
+        T_total = t.num_blocks * t.block_size + t.hot_len
+        mk = mask
+        if mk.dim() == 4:
+            mk = mk[:, :, -1, :]            # [B, H, T] for a single query row
+        mk = mk.expand(B, Hq, mk.shape[-1])
+        if mk.shape[-1] < T_total:
+            raise ValueError(f"attention_mask covers {mk.shape[-1]} keys, cache holds {T_total}")
+        mask_u8 = (mk != 0).to(device=dev, dtype=torch.uint8).contiguous()
+        mask_stride = mask_u8.shape[-1]
+    a = N.DecodeArgs(
+        num_layers=L, batch=B, num_q_heads=Hq, num_kv_heads=t.num_heads, head_dim=D,
+        block_size=t.block_size, num_blocks=t.num_blocks, block_capacity=t.block_capacity,
+        rank_k=t.rank_k_pad, rank_v=t.rank_v_pad, hot_len=t.hot_len, hot_capacity=t.hot_capacity,
+        dtype=N.dtype_code(t.dtype), rope_mode=rope_mode, rope_tied=int(bool(tied)), rope_len=cos32.shape[0],
+        query_position=int(query_position), scale=float(scale), mask_stride=mask_stride,
+        q=N.ptr(q), codes_k=N.ptr(t.codes_k), codes_v=N.ptr(t.codes_v), scale_k=N.ptr(t.scale_k),
+        scale_v=N.ptr(t.scale_v), basis_k=N.ptr(t.basis_k), basis_v=N.ptr(t.basis_v),
+        block_pos=N.ptr(t.block_pos), hot_k=N.ptr(t.hot_k), hot_v=N.ptr(t.hot_v), hot_pos=N.ptr(t.hot_pos),
+        cos_table=N.ptr(cos32), sin_table=N.ptr(sin32), mask=N.ptr(mask_u8), out=N.ptr(out))
+    need = lib.spx_decode_workspace_size(a)
+    ws = N.workspace(dev, need)
+    a.workspace, a.workspace_bytes = N.ptr(ws), ws.numel()
+    N.check(lib, lib.spx_decode_attn(a, N.stream_handle(dev)), "spx_decode_attn")
+    return out
+
+
+def reconstruct(codes, scale, basis, *, batch, num_heads, head_dim, block_size, num_blocks, block_capacity, rank,
+                rank_major, out, out_tokens):
+    lib = N.lib_for(out.device)
+    a = N.ReconstructArgs(batch=batch, num_kv_heads=num_heads, head_dim=head_dim, block_size=block_size,
+                          num_blocks=num_blocks, block_capacity=block_capacity, rank=rank,
+                          rank_major=int(rank_major), dtype=N.dtype_code(out.dtype), out_tokens=out_tokens,
+                          codes=N.ptr(codes), scale=N.ptr(scale), basis=N.ptr(basis), out=N.ptr(out))
+    N.check(lib, lib.spx_reconstruct(a, N.stream_handle(out.device)), "spx_reconstruct")
+    return out
+
+
+def block_scores(q, coeffs, basis, cos, sin, start_position: int) -> torch.Tensor:
+    """[B, H_q, T] float32 scores of one block (absolute-position RoPE)."""
+    dev = q.device
+    lib = N.lib_for(dev)
+    B, Hq, _, D = q.shape
+    H, T, R = coeffs.shape
+    qf = q.reshape(B, Hq, D).to(torch.float32).contiguous()
+    cf = coeffs.to(device=dev, dtype=torch.float32).contiguous()
+    bf = basis.to(device=dev, dtype=torch.float32).contiguous()
+    c32, s32 = rope_table_f32(cos, dev), rope_table_f32(sin, dev)
+    out = torch.empty(B, Hq, T, dtype=torch.float32, device=dev)
+    a = N.BlockScoreArgs(batch=B, num_q_heads=Hq, num_kv_heads=H, head_dim=D, block_size=T, rank=R,
+                         rope_len=c32.shape[0], start_position=int(start_position), q=N.ptr(qf),
+                         coeffs=N.ptr(cf), basis=N.ptr(bf), cos_table=N.ptr(c32), sin_table=N.ptr(s32),
+                         scores=N.ptr(out))
+    N.check(lib, lib.spx_block_scores(a, N.stream_handle(dev)), "spx_block_scores")
+    return out
+
+
+def block_values(attn, coeffs, basis) -> torch.Tensor:
+    """[B, H_q, D] float32 values of one block."""
+    dev = attn.device
+    lib = N.lib_for(dev)
+    B, Hq, _, T = attn.shape
+    H, _, R = coeffs.shape
+    D = basis.shape[-1]
+    af = attn.reshape(B, Hq, T).to(torch.float32).contiguous()
+    cf = coeffs.to(device=dev, dtype=torch.float32).contiguous()
+    bf = basis.to(device=dev, dtype=torch.float32).contiguous()
+    out = torch.empty(B, Hq, D, dtype=torch.float32, device=dev)
+    a = N.BlockValueArgs(batch=B, num_q_heads=Hq, num_kv_heads=H, head_dim=D, block_size=T, rank=R,
+                         attn=N.ptr(af), coeffs=N.ptr(cf), basis=N.ptr(bf), out=N.ptr(out))
+    N.check(lib, lib.spx_block_values(a, N.stream_handle(dev)), "spx_block_values")
+    return out
