@@ -14,6 +14,8 @@
 // kernel per (layer, sequence, KV head) that scores the hot tier and merges every
 // partial with the log-sum-exp rule into the output.
 #include <math.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include "spx_common.cuh"
 #include "spx_decode.cuh"
@@ -150,6 +152,8 @@ __global__ void __launch_bounds__(256) hot_merge_kernel(DecodeParams p) {
   const int64_t lbg = (int64_t)lb * p.H + g;
   const T* q = reinterpret_cast<const T*>(p.q) + ((int64_t)lb * p.Hq + (int64_t)g * nrep) * D;
   for (int i = tid; i < nrep * D; i += blockDim.x) sq[i] = to_f(q[i]);
+  // a cold-tier kernel that gave up waiting marks the workspace header: report NaN
+  const bool cold_failed = nb > 0 && reinterpret_cast<const int*>(p.ws)[-64] != 0;
   __syncthreads();
   const T* hk = reinterpret_cast<const T*>(p.hk) + lbg * p.HC * D;
   const T* hv = reinterpret_cast<const T*>(p.hv) + lbg * p.HC * D;
@@ -225,7 +229,7 @@ __global__ void __launch_bounds__(256) hot_merge_kernel(DecodeParams p) {
     for (int t = 0; t < hot; ++t) acc = fmaf(ssc[h * hot + t], to_f(hv[(int64_t)t * D + d]), acc);
     acc *= sml[2 * h];
     for (int jj = 0; jj < nb; ++jj) acc = fmaf(swt[h * (nb + 1) + jj], recs[((int64_t)jj * nrep + h) * (D + 4) + 4 + d], acc);
-    out[(int64_t)h * D + d] = from_f<T>(acc * sml[2 * h + 1]);
+    out[(int64_t)h * D + d] = from_f<T>(cold_failed ? NAN : acc * sml[2 * h + 1]);
   }
 }
 
@@ -241,18 +245,18 @@ static int launch_cold_generic(const DecodeParams& p, cudaStream_t st) {
 }
 
 template <typename T>
-static int launch_generic(const DecodeParams& p, cudaStream_t st) {
-  int rc = SPX_OK;
-  if (p.nblk > 0) {
-    switch (p.RK) {
-      case 16: rc = launch_cold_generic<T, 16>(p, st); break;
-      case 32: rc = launch_cold_generic<T, 32>(p, st); break;
-      case 48: rc = launch_cold_generic<T, 48>(p, st); break;
-      case 64: rc = launch_cold_generic<T, 64>(p, st); break;
-      default: set_error("rank_k %d not in {16,32,48,64}", p.RK); return SPX_ERR_UNSUPPORTED;
-    }
-    if (rc != SPX_OK) return rc;
+static int launch_cold(const DecodeParams& p, cudaStream_t st) {
+  switch (p.RK) {
+    case 16: return launch_cold_generic<T, 16>(p, st);
+    case 32: return launch_cold_generic<T, 32>(p, st);
+    case 48: return launch_cold_generic<T, 48>(p, st);
+    case 64: return launch_cold_generic<T, 64>(p, st);
+    default: set_error("rank_k %d not in {16,32,48,64}", p.RK); return SPX_ERR_UNSUPPORTED;
   }
+}
+
+template <typename T>
+static int launch_hot_merge(const DecodeParams& p, cudaStream_t st) {
   const size_t smem = ((size_t)p.nrep * p.D + (size_t)p.nrep * p.hot + 2 * p.nrep + (size_t)p.nrep * (p.nblk + 1)) *
                       sizeof(float);
   SPX_REQUIRE(smem <= kMaxSmem, SPX_ERR_UNSUPPORTED,
@@ -333,21 +337,34 @@ static int make_params(const spx_decode_args* a, DecodeParams* p) {
   p->sinT = a->sin_table;
   p->mask = a->mask;
   p->out = a->out;
-  p->ws = reinterpret_cast<float*>(a->workspace);
+  p->ws = a->workspace ? reinterpret_cast<float*>(reinterpret_cast<char*>(a->workspace) + kWsHeader) : nullptr;
   return SPX_OK;
 }
 
 size_t decode_workspace_bytes(const DecodeParams& p) {
-  return (size_t)p.L * p.B * p.H * p.nparts * p.nrep * (p.D + 4) * sizeof(float);
+  return kWsHeader + (size_t)p.L * p.B * p.H * p.nparts * p.nrep * (p.D + 4) * sizeof(float);
+}
+
+// SPX_DECODE_PATH=generic forces the generic cold-tier kernel (used to cross-check the
+// fast kernel on identical inputs); the default picks the fast kernel when it covers
+// the configuration.
+static bool force_generic() {
+  const char* e = getenv("SPX_DECODE_PATH");
+  return e && strcmp(e, "generic") == 0;
 }
 
 int decode_dispatch(const DecodeParams& p, cudaStream_t st) {
-  if (decode_fast_supported(p)) return decode_fast_launch(p, st);
-  return SPX_DISPATCH_DTYPE(p.dtype, T, [&] { return launch_generic<T>(p, st); });
-}
-
-int decode_generic(const DecodeParams& p, cudaStream_t st) {
-  return SPX_DISPATCH_DTYPE(p.dtype, T, [&] { return launch_generic<T>(p, st); });
+  int rc = SPX_OK;
+  if (p.nblk > 0) {
+    const cudaError_t e = cudaMemsetAsync(reinterpret_cast<char*>(p.ws) - kWsHeader, 0, sizeof(int), st);
+    SPX_REQUIRE(e == cudaSuccess, SPX_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+    if (!force_generic() && decode_fast_supported(p))
+      rc = decode_fast_cold(p, st);
+    else
+      rc = SPX_DISPATCH_DTYPE(p.dtype, T, [&] { return launch_cold<T>(p, st); });
+    if (rc != SPX_OK) return rc;
+  }
+  return SPX_DISPATCH_DTYPE(p.dtype, T, [&] { return launch_hot_merge<T>(p, st); });
 }
 
 }  // namespace spx
@@ -372,6 +389,8 @@ int spx_decode_attn(const spx_decode_args* a, void* stream) {
   if (p.nblk > 0) {
     SPX_REQUIRE(a->workspace && a->workspace_bytes >= need, SPX_ERR_WORKSPACE,
                 "workspace of %zu bytes required, %zu given", need, a->workspace_bytes);
+    SPX_REQUIRE((reinterpret_cast<uintptr_t>(a->workspace) & 255u) == 0, SPX_ERR_ALIGN,
+                "workspace must be 256-byte aligned");
   }
   return decode_dispatch(p, (cudaStream_t)stream);
 }

@@ -24,15 +24,18 @@ struct DecodeParams {
   const float* sinT;
   const uint8_t* mask;
   void* out;
-  float* ws;  // cold partials: [L*B*H][nparts][nrep][D + 4] = (m, l, -, -, o[D])
+  float* ws;  // cold partials [L*B*H][nparts][nrep][D + 4] = (m, l, -, -, o[D]), after the header
 };
+
+// The workspace starts with a 256-byte header (word 0: set to 1 by a cold-tier kernel
+// whose bounded wait expired); the cold partials follow it.
+constexpr size_t kWsHeader = 256;
 
 size_t decode_workspace_bytes(const DecodeParams& p);
 int decode_dispatch(const DecodeParams& p, cudaStream_t st);
-int decode_generic(const DecodeParams& p, cudaStream_t st);
 
-// Fast cold-tier path (spx_decode_fast.cu): returns true when the shape is covered.
+// Fast cold-tier path (spx_decode_fast.cu): true when the configuration is covered.
 bool decode_fast_supported(const DecodeParams& p);
-int decode_fast_launch(const DecodeParams& p, cudaStream_t st);
+int decode_fast_cold(const DecodeParams& p, cudaStream_t st);
 
 }  // namespace spx
