@@ -2,23 +2,27 @@
 //
 // Work item: one CTA per (cold block j, chunk of units), a unit being one (layer,
 // sequence, KV head).  Every unit of the chunk shares block j's token positions, so the
-// block's RoPE rows are read once per CTA and parked in tensor memory (TMEM, used here as
-// an extension of the register file: each warp writes its own tokens' rows with
-// tcgen05.st and reads them back per unit with tcgen05.ld of the same shape).
+// block's RoPE rows are read once per CTA and parked in tensor memory (TMEM columns
+// 0..255, used as an extension of the register file: each warp writes its own tokens'
+// rows with tcgen05.st and reads them back per unit with tcgen05.ld of the same shape).
 //
 // Per unit the CTA streams, through a 3-stage TMA bulk-copy + mbarrier pipeline:
 //   INT8 key codes [T][RK] (token-major), INT8 value codes [RV][T] (rank-major),
 //   FP16 bases [RK][128] and [RV][128], and the unit's query rows (n_rep x 128 FP16).
-// A swizzle pass copies codes and key basis into bank-conflict-free layouts.  Each warp
-// owns 64 tokens (four 16-token m-tiles) and computes, with mma.sync m16n8k16:
-//   K~ = codes_K @ B_K (FP32 accumulate)   -> RoPE rotation in packed f16x2 registers
-//   scores = rot(K~) . Q                   -> online softmax (exp2, per-warp running max)
-//   v_lat += P^T-weighted codes_V          -> [RV x heads]
+// A conversion pass turns the key codes into FP16 UMMA operand tiles (K-major, no
+// swizzle) and the key basis into the MN-major operand; one thread then issues
+//   tcgen05.mma kind::f16  M=128 tokens x N=128 dims x K=16   (K~ = codes_K @ B_K)
+// into one of two TMEM accumulators (columns 256..511), per 128-token M-tile.  Warps
+// read K~ back with tcgen05.ld.16x256b, which lands in the mma.sync fragment layout:
+//   rotate K~ by the token's RoPE row in packed f16x2   -> A fragment
+//   scores = rot(K~) . Q          (mma.sync m16n8k16)   -> online softmax (exp2)
+//   v_lat += codes_V^T . P        (mma.sync m16n8k16)   -> [RV x heads]
 // Warps combine (m, l, v_lat) in shared memory; v_lat is expanded once through B_V and
 // written as the unit's partial (m, l, o[128]) for the hot-tier/merge kernel.
 //
-// Token order inside a 16-token m-tile is the permutation PI below, chosen so that the
-// value codes load with one ldmatrix per m-tile; softmax is order-invariant.
+// Token order inside each 16-token group is the permutation slot_to_token() below,
+// chosen so that value codes load with one ldmatrix per group; softmax is
+// order-invariant.
 #include <math.h>
 
 #include "spx_common.cuh"
@@ -96,6 +100,39 @@ __device__ __forceinline__ void tmem_ld16x256_x2(uint32_t taddr, uint32_t (&r)[8
       : "memory");
 }
 
+// ------------------------------------------------------------------- tcgen05.mma ----
+// Shared-memory matrix descriptor, no swizzle: start address, leading-dimension byte
+// offset and stride-dimension byte offset (all >> 4), version 1 (sm_100).
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+// Instruction descriptor: D f32, A/B f16, A K-major, B MN-major, N = 128, M = 128.
+constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | (0u << 15) | (1u << 16) | ((128u >> 3) << 17) |
+                            ((128u >> 4) << 24);
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+// Two 16x256b loads (columns c0.. and c1..) and the wait, in one statement.
+__device__ __forceinline__ void tmem_ld16x256_x2x2(uint32_t ta, uint32_t tb, uint32_t (&r)[8], uint32_t (&q)[8]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%16];\n\t"
+      "tcgen05.ld.sync.aligned.16x256b.x2.b32 {%8, %9, %10, %11, %12, %13, %14, %15}, [%17];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(q[0]), "=r"(q[1]), "=r"(q[2]), "=r"(q[3]), "=r"(q[4]), "=r"(q[5]), "=r"(q[6]), "=r"(q[7])
+      : "r"(ta), "r"(tb)
+      : "memory");
+}
+
 // ------------------------------------------------------------- warp MMA helpers -----
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
@@ -149,34 +186,51 @@ template <int RK, int RV, int NW>
 struct Cfg {
   static constexpr int NT = NW * 32;
   static constexpr int TB = NW * 64;
-  static constexpr int G = RK / 4;                      // key-code bytes per thread-row
+  static constexpr int MT = TB / 128;                   // 128-token UMMA M-tiles per unit
   static constexpr int CK = TB * RK;
   static constexpr int CV = RV * TB;
   static constexpr int BK = RK * FD * 2;
   static constexpr int BV = RV * FD * 2;
   static constexpr int QB = 8 * FD * 2;
   static constexpr int STAGE = CK + CV + BK + BV + QB;
-  static constexpr int OFF_CK = STAGES * STAGE;         // swizzled compute copies
-  static constexpr int OFF_CV = OFF_CK + CK;
-  static constexpr int OFF_BK = OFF_CV + CV;
-  static constexpr int OFF_SM = OFF_BK + BK;            // per-warp m [NW][8]
+  static constexpr int ATILE = 128 * RK * 2;            // one M-tile of FP16 key codes
+  static constexpr int OFF_A = STAGES * STAGE;          // UMMA A tiles [MT][RK/8][16][8 rows][16 B]
+  static constexpr int OFF_B = OFF_A + MT * ATILE;      // UMMA B tile  [16 n-chunks][RK rows][16 B]
+  static constexpr int OFF_CV = OFF_B + BK;             // value codes [T/16][RV][16 B], XOR-swizzled rows
+  static constexpr int OFF_Q = OFF_CV + CV;             // query [8][16 chunks], XOR-swizzled chunks
+  static constexpr int OFF_SM = OFF_Q + QB;             // per-warp m [NW][8]
   static constexpr int OFF_SL = OFF_SM + NW * 8 * 4;    // per-warp l [NW][8]
   static constexpr int OFF_SV = OFF_SL + NW * 8 * 4;    // per-warp v_lat [NW][RV][8]
   static constexpr int OFF_VL = OFF_SV + NW * RV * 8 * 4;   // combined v_lat [8][RV]
   static constexpr int OFF_ML = OFF_VL + 8 * RV * 4;    // combined (m, l) [8][2]
-  static constexpr int OFF_BAR = OFF_ML + 16 * 4;
-  static constexpr int OFF_TM = OFF_BAR + STAGES * 8;
+  static constexpr int OFF_BAR = OFF_ML + 16 * 4;       // STAGES load barriers + 2 MMA barriers
+  static constexpr int OFF_TM = OFF_BAR + (STAGES + 2) * 8;
   static constexpr int BYTES = OFF_TM + 16;
-  static_assert(STAGE % 16 == 0 && OFF_BAR % 8 == 0, "alignment");
+  static_assert(STAGE % 16 == 0 && OFF_BAR % 8 == 0 && OFF_A % 128 == 0, "alignment");
+  static_assert(BYTES <= 227 * 1024, "shared memory");
 };
 
-// Bank-conflict-free chunk index for row R of the key basis (see the loader below).
-template <int G>
-__device__ __forceinline__ int bk_swz(int R) { return (((R / G) & 3) << 1) | (R & 1); }
+template <int NW>
+struct Group {
+  int mt, lane_off, tcol;
+  __device__ __forceinline__ Group(int w, int i) {
+    if constexpr (NW == 8) {
+      mt = i;
+      lane_off = 32 * (w & 3) + 16 * (w >> 2);
+      tcol = 64 * i;
+    } else {
+      mt = i >> 1;
+      lane_off = 32 * w + 16 * (i & 1);
+      tcol = 64 * (i >> 1);
+    }
+  }
+  __device__ __forceinline__ int token0() const { return mt * 128 + lane_off; }
+};
 
 template <int RK, int RV, int NW>
 __global__ void __launch_bounds__(NW * 32, 1) cold_fast_kernel(DecodeParams p, int units_per_cta) {
   using C = Cfg<RK, RV, NW>;
+  static_assert(NW == 8 || NW == 4, "one or two warps per TMEM lane quadrant");
   extern __shared__ __align__(1024) uint8_t sm[];
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
@@ -185,16 +239,17 @@ __global__ void __launch_bounds__(NW * 32, 1) cold_fast_kernel(DecodeParams p, i
   const int u0 = blockIdx.y * units_per_cta;
   const int nu = min(units_per_cta, units - u0);
   const int nrep = p.nrep;
-  const uint32_t bar0 = smem_u32(sm + C::OFF_BAR);
+  const uint32_t bar0 = smem_u32(sm + C::OFF_BAR);      // TMA stage barriers
+  const uint32_t mbar0 = bar0 + 8 * STAGES;              // MMA-done barriers, one per accumulator
   uint32_t* tm_slot = reinterpret_cast<uint32_t*>(sm + C::OFF_TM);
   int* err = reinterpret_cast<int*>(p.ws) - 64;   // status word in the workspace header
 
   if (w == 0) {
-    tmem_alloc(smem_u32(tm_slot), 256);
+    tmem_alloc(smem_u32(tm_slot), 512);
     tmem_relinquish();
   }
   if (tid == 0) {
-    for (int s = 0; s < STAGES; ++s) mbar_init(bar0 + 8 * s, 1);
+    for (int s = 0; s < STAGES + 2; ++s) mbar_init(bar0 + 8 * s, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   tc_fence_before();
@@ -225,17 +280,13 @@ __global__ void __launch_bounds__(NW * 32, 1) cold_fast_kernel(DecodeParams p, i
 
   // ---- RoPE rows of this warp's 64 tokens -> TMEM (f16 pairs), once per CTA ----------
   const int64_t p0 = p.bpos[j];
-  const uint32_t lane_q = (uint32_t)(32 * (w & 3));
-  auto taddr = [&](int i) {  // TMEM address of m-tile i of this warp
-    return tbase + ((lane_q + 16u * (uint32_t)(i & 1)) << 16) + (uint32_t)(((w >> 2) * 2 + (i >> 1)) * 64);
-  };
 #pragma unroll 1
   for (int i = 0; i < 4; ++i) {
+    const Group<NW> G(w, i);
     int64_t a[2];
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
-      const int tok = w * 64 + i * 16 + slot_to_token(g + 8 * hh);
-      const int64_t pos = p0 + tok;
+      const int64_t pos = p0 + G.token0() + slot_to_token(g + 8 * hh);
       int64_t aa = p.mode == SPX_ROPE_DISTANCE ? (p.qpos - pos > 0 ? p.qpos - pos : 0) : pos;
       a[hh] = aa < 0 ? 0 : (aa >= p.rope_len ? p.rope_len - 1 : aa);
     }
@@ -253,7 +304,7 @@ __global__ void __launch_bounds__(NW * 32, 1) cold_fast_kernel(DecodeParams p, i
           r[4 * cc + 2 * hh + 1] = pack_f2(sv.x, sv.y);
         }
       }
-      tmem_st16x256_x2(taddr(i) + 16 * s, r);
+      tmem_st16x256_x2(tbase + ((uint32_t)G.lane_off << 16) + (uint32_t)(G.tcol + 16 * s), r);
     }
   }
   tmem_wait_st();
@@ -263,11 +314,25 @@ __global__ void __launch_bounds__(NW * 32, 1) cold_fast_kernel(DecodeParams p, i
   float* sV = reinterpret_cast<float*>(sm + C::OFF_SV);
   float* sVL = reinterpret_cast<float*>(sm + C::OFF_VL);
   float* sML = reinterpret_cast<float*>(sm + C::OFF_ML);
-  uint8_t* cK = sm + C::OFF_CK;
+  uint8_t* sA = sm + C::OFF_A;
+  uint8_t* sB = sm + C::OFF_B;
   uint8_t* cV = sm + C::OFF_CV;
-  uint8_t* bK = sm + C::OFF_BK;
-  const uint32_t cK_u = smem_u32(cK), cV_u = smem_u32(cV), bK_u = smem_u32(bK);
+  uint8_t* sQ = sm + C::OFF_Q;
+  const uint32_t sA_u = smem_u32(sA), sB_u = smem_u32(sB), cV_u = smem_u32(cV);
   int failed_at = -1;
+  uint32_t mma_uses[2] = {0u, 0u};   // completed waits per accumulator (phase parity)
+
+  auto issue_mma = [&](int mt) {   // one thread: K~ of M-tile mt into accumulator mt & 1
+    tc_fence_after();
+    const uint32_t d = tbase + 256u + 128u * (uint32_t)(mt & 1);
+#pragma unroll
+    for (int ks = 0; ks < RK / 16; ++ks) {
+      const uint64_t ad = umma_desc(sA_u + mt * C::ATILE + ks * 2 * 2048, 2048, 128);
+      const uint64_t bd = umma_desc(sB_u + ks * 256, 128, RK * 16);
+      umma_f16(d, ad, bd, ks > 0 ? 1u : 0u);
+    }
+    umma_commit(mbar0 + 8 * (mt & 1));
+  };
 
 #pragma unroll 1
   for (int u = 0; u < nu; ++u) {
@@ -278,108 +343,91 @@ __global__ void __launch_bounds__(NW * 32, 1) cold_fast_kernel(DecodeParams p, i
       failed_at = u;
       break;
     }
-    // ---- swizzle pass: codes and key basis into conflict-free layouts --------------
+    // ---- conversion pass -----------------------------------------------------------
     {
-      const uint4* src = reinterpret_cast<const uint4*>(st);
-      for (int e = tid; e < C::CK / 16; e += C::NT) {       // key codes -> slot order
-        const int tok = e / (RK / 16), ch = e % (RK / 16);
-        const int row = (tok & ~15) + token_to_slot(tok & 15);
-        reinterpret_cast<uint4*>(cK + row * RK)[ch] = src[e];
+      // key codes -> FP16 A tiles: row m of M-tile mt holds token mt*128 + (m & ~15) +
+      // slot_to_token(m & 15); 16-byte K-chunks of 8 codes, K-major, no swizzle
+      for (int e = tid; e < C::TB * (RK / 8); e += C::NT) {
+        const int tau = e % C::TB, kc = e / C::TB;
+        const uint2 v = *reinterpret_cast<const uint2*>(st + tau * RK + kc * 8);
+        const int mt = tau >> 7;
+        const int m = (tau & 127 & ~15) + token_to_slot(tau & 15);
+        uint4 o;
+        i8x4_to_h2(v.x, o.x, o.y);
+        i8x4_to_h2(v.y, o.z, o.w);
+        *reinterpret_cast<uint4*>(sA + mt * C::ATILE + kc * 2048 + (m >> 3) * 128 + (m & 7) * 16) = o;
       }
-      const uint4* srcv = reinterpret_cast<const uint4*>(st + C::CK);
-      for (int e = tid; e < C::CV / 16; e += C::NT) {       // value codes -> [T/16][RV][16]
-        const int r = e / (C::TB / 16), tt = e % (C::TB / 16);
-        reinterpret_cast<uint4*>(cV)[tt * RV + r] = srcv[e];
-      }
+      // key basis [RK][128] -> MN-major B tile [16 n-chunks][RK rows][16 B]
       const uint4* srcb = reinterpret_cast<const uint4*>(st + C::CK + C::CV);
-      for (int e = tid; e < C::BK / 16; e += C::NT) {       // key basis, XOR-swizzled chunks
-        const int R = e >> 4, n = e & 15;
-        reinterpret_cast<uint4*>(bK + R * 256)[n ^ bk_swz<C::G>(R)] = srcb[e];
+      for (int e = tid; e < RK * 16; e += C::NT) {
+        const int k = e % RK, nc = e / RK;
+        reinterpret_cast<uint4*>(sB)[nc * RK + k] = srcb[k * 16 + nc];
+      }
+      // value codes [RV][T] -> [T/16][RV][16 tokens], row index XOR (tile & 7)
+      const uint4* srcv = reinterpret_cast<const uint4*>(st + C::CK);
+      for (int e = tid; e < C::CV / 16; e += C::NT) {
+        const int r = e / (C::TB / 16), tt = e % (C::TB / 16);
+        reinterpret_cast<uint4*>(cV)[tt * RV + (r ^ (tt & 7))] = srcv[e];
+      }
+      // query rows, 16-byte chunk index XOR head
+      const uint4* srcq = reinterpret_cast<const uint4*>(st + C::CK + C::CV + C::BK + C::BV);
+      for (int e = tid; e < nrep * 16; e += C::NT) {
+        const int h = e >> 4, n = e & 15;
+        reinterpret_cast<uint4*>(sQ)[h * 16 + (n ^ h)] = srcq[e];
       }
     }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
+    if (tid == 0) {
+      issue_mma(0);
+      if (C::MT > 1) issue_mma(1);
+    }
     const int64_t unit = u0 + u;
     const int64_t slotid = unit * p.NBc + j;
     const float kscale = p.sk[slotid] * p.scale * LOG2E;
     const float vscale = p.sv[slotid];
 
     // ---- query fragments (B operand of the score MMA), padded heads zeroed ---------
-    const uint8_t* sq = st + C::CK + C::CV + C::BK + C::BV;
     uint32_t qf[8][2];
 #pragma unroll
     for (int ks = 0; ks < 8; ++ks) {
       if (g < nrep) {
-        qf[ks][0] = *reinterpret_cast<const uint32_t*>(sq + (g * FD + 16 * ks + 2 * t) * 2);
-        qf[ks][1] = *reinterpret_cast<const uint32_t*>(sq + (g * FD + 16 * ks + 2 * t + 8) * 2);
+        qf[ks][0] = *reinterpret_cast<const uint32_t*>(sQ + (g * 16 + ((2 * ks) ^ g)) * 16 + 4 * t);
+        qf[ks][1] = *reinterpret_cast<const uint32_t*>(sQ + (g * 16 + ((2 * ks + 1) ^ g)) * 16 + 4 * t);
       } else {
         qf[ks][0] = qf[ks][1] = 0u;
       }
     }
-    // ---- key-code A fragments of the warp's four m-tiles ---------------------------
-    uint32_t af[4][RK / 16][4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int row = w * 64 + i * 16 + g;
-      if constexpr (RK == 32) {
-        const uint2 v0 = *reinterpret_cast<const uint2*>(cK + row * 32 + 8 * t);
-        const uint2 v1 = *reinterpret_cast<const uint2*>(cK + (row + 8) * 32 + 8 * t);
-        i8x4_to_h2(v0.x, af[i][0][0], af[i][0][2]);
-        i8x4_to_h2(v1.x, af[i][0][1], af[i][0][3]);
-        i8x4_to_h2(v0.y, af[i][1][0], af[i][1][2]);
-        i8x4_to_h2(v1.y, af[i][1][1], af[i][1][3]);
-      } else {
-        const uint32_t v0 = *reinterpret_cast<const uint32_t*>(cK + row * 16 + 4 * t);
-        const uint32_t v1 = *reinterpret_cast<const uint32_t*>(cK + (row + 8) * 16 + 4 * t);
-        i8x4_to_h2(v0, af[i][0][0], af[i][0][2]);
-        i8x4_to_h2(v1, af[i][0][1], af[i][0][3]);
-      }
-    }
-    // ---- scores: reconstruct, rotate, dot ------------------------------------------
+    // ---- scores: K~ from TMEM, rotate, dot ----------------------------------------
     float sc[4][4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.f;
-    const int mrow = lane & 7, mid = lane >> 3;
 #pragma unroll
-    for (int s4 = 0; s4 < 4; ++s4) {
-      uint32_t bf[4][RK / 16][2];   // n-tiles {2s, 2s+1, 2s+8, 2s+9}
-      if constexpr (RK == 32) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int n = 2 * s4 + (q & 1) + 8 * (q >> 1);
-          const int ks = mid >> 1, h = mid & 1;
-          const int R = C::G * (mrow >> 1) + 4 * ks + 2 * h + (mrow & 1);
-          ldsm_x4_t(bK_u + R * 256 + ((n ^ bk_swz<C::G>(R)) << 4), bf[q][0][0], bf[q][0][1], bf[q][1][0],
-                    bf[q][1][1]);
-        }
-      } else {
-#pragma unroll
-        for (int q2 = 0; q2 < 2; ++q2) {
-          const int n = 2 * s4 + (mid >> 1) + 8 * q2;
-          const int h = mid & 1;
-          const int R = C::G * (mrow >> 1) + 2 * h + (mrow & 1);
-          ldsm_x4_t(bK_u + R * 256 + ((n ^ bk_swz<C::G>(R)) << 4), bf[2 * q2][0][0], bf[2 * q2][0][1],
-                    bf[2 * q2 + 1][0][0], bf[2 * q2 + 1][0][1]);
-        }
+    for (int i = 0; i < 4; ++i) {
+      const Group<NW> G(w, i);
+      const bool first_of_tile = (NW == 8) || ((i & 1) == 0);
+      const int b = G.mt & 1;
+      if (first_of_tile) {
+        const bool mok = mbar_wait(mbar0 + 8 * b, mma_uses[b] & 1u);
+        mma_uses[b]++;
+        if (!mok) atomicExch(err, 1);
+        tc_fence_after();
       }
+      const uint32_t lrow = (uint32_t)G.lane_off << 16;
+      const uint32_t dcol = tbase + lrow + 256u + 128u * (uint32_t)b;
+      const uint32_t tcol = tbase + lrow + (uint32_t)G.tcol;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float acc[4][4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
-#pragma unroll
-        for (int ks = 0; ks < RK / 16; ++ks)
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            mma16816(acc[q], af[i][ks][0], af[i][ks][1], af[i][ks][2], af[i][ks][3], bf[q][ks][0], bf[q][ks][1]);
-        uint32_t tr[8];
-        tmem_ld16x256_x2(taddr(i) + 16 * s4, tr);
+      for (int s4 = 0; s4 < 4; ++s4) {
+        uint32_t d1[8], d2[8], tr[8];
+        tmem_ld16x256_x2x2(dcol + 16 * s4, dcol + 64 + 16 * s4, d1, d2);
+        tmem_ld16x256_x2(tcol + 16 * s4, tr);
         uint32_t k1[4], k2[4];
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {   // hh: row g (0) or g+8 (1)
-            const __half2 a1 = u2h(pack_f2(acc[cc][2 * hh], acc[cc][2 * hh + 1]));
-            const __half2 a2 = u2h(pack_f2(acc[2 + cc][2 * hh], acc[2 + cc][2 * hh + 1]));
+            const __half2 a1 = u2h(pack_f2(__uint_as_float(d1[4 * cc + 2 * hh]), __uint_as_float(d1[4 * cc + 2 * hh + 1])));
+            const __half2 a2 = u2h(pack_f2(__uint_as_float(d2[4 * cc + 2 * hh]), __uint_as_float(d2[4 * cc + 2 * hh + 1])));
             const __half2 c = u2h(tr[4 * cc + 2 * hh]), sn = u2h(tr[4 * cc + 2 * hh + 1]);
             k1[2 * cc + hh] = h2u(__hfma2(c, a1, __hneg2(__hmul2(sn, a2))));   // c K1 - s K2
             k2[2 * cc + hh] = h2u(__hfma2(c, a2, __hmul2(sn, a1)));            // s K1 + c K2
@@ -387,6 +435,13 @@ __global__ void __launch_bounds__(NW * 32, 1) cold_fast_kernel(DecodeParams p, i
         }
         mma16816(sc[i], k1[0], k1[1], k1[2], k1[3], qf[s4][0], qf[s4][1]);
         mma16816(sc[i], k2[0], k2[1], k2[2], k2[3], qf[s4 + 4][0], qf[s4 + 4][1]);
+      }
+      // accumulator b is free once every warp has read this M-tile: refill it
+      const bool last_of_tile = (NW == 8) || ((i & 1) == 1);
+      if (last_of_tile && G.mt + 2 < C::MT) {
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0) issue_mma(G.mt + 2);
       }
     }
     // ---- per-warp softmax over 64 tokens (log2 domain) ----------------------------
@@ -416,13 +471,13 @@ __global__ void __launch_bounds__(NW * 32, 1) cold_fast_kernel(DecodeParams p, i
       sc[i][3] = live1 ? exp2f(sc[i][3] - mx1) : 0.f;
       l0 += sc[i][0] + sc[i][2];
       l1 += sc[i][1] + sc[i][3];
-      // ---- v_lat[rank][head] += codes_V^T . P  (one ldmatrix per m-tile) ------------
+      // ---- v_lat[rank][head] += codes_V^T . P  (one ldmatrix per 16 tokens) ---------
       const uint32_t b0 = movm_t(pack_f2(sc[i][0], sc[i][1]));
       const uint32_t b1 = movm_t(pack_f2(sc[i][2], sc[i][3]));
-      const int tt = w * 4 + i;
+      const int tt = Group<NW>(w, i).token0() >> 4;
       if constexpr (RV == 32) {
         uint32_t v0, v1, v2, v3;
-        ldsm_x4(cV_u + ((tt * RV + lane) << 4), v0, v1, v2, v3);
+        ldsm_x4(cV_u + ((tt * RV + (lane ^ (tt & 7))) << 4), v0, v1, v2, v3);
         uint32_t a0, a1, a2, a3;
         i8x4_to_h2(v0, a0, a2);
         i8x4_to_h2(v1, a1, a3);
@@ -432,7 +487,7 @@ __global__ void __launch_bounds__(NW * 32, 1) cold_fast_kernel(DecodeParams p, i
         mma16816(vacc[1], a0, a1, a2, a3, b0, b1);
       } else {
         uint32_t v0, v1;
-        ldsm_x2(cV_u + ((tt * RV + (lane & 15)) << 4), v0, v1);
+        ldsm_x2(cV_u + ((tt * RV + ((lane & 15) ^ (tt & 7))) << 4), v0, v1);
         uint32_t a0, a1, a2, a3;
         i8x4_to_h2(v0, a0, a2);
         i8x4_to_h2(v1, a1, a3);
@@ -515,7 +570,7 @@ __global__ void __launch_bounds__(NW * 32, 1) cold_fast_kernel(DecodeParams p, i
   }
   tc_fence_before();
   __syncthreads();
-  if (w == 0) tmem_dealloc(tbase, 256);
+  if (w == 0) tmem_dealloc(tbase, 512);
 }
 
 template <int RK, int RV, int NW>
@@ -538,7 +593,7 @@ bool decode_fast_supported(const DecodeParams& p) {
   if (p.nblk <= 0 || p.D != 128 || p.dtype != SPX_F16 || p.mask != nullptr) return false;
   if (!(p.tied || p.mode == SPX_ROPE_DISTANCE)) return false;
   if (!(p.RK == 16 || p.RK == 32) || !(p.RV == 16 || p.RV == 32)) return false;
-  if (!(p.Tb == 128 || p.Tb == 256 || p.Tb == 512)) return false;
+  if (!(p.Tb == 256 || p.Tb == 512)) return false;
   if (!(p.nrep == 1 || p.nrep == 2 || p.nrep == 4 || p.nrep == 8)) return false;
   if (reinterpret_cast<uintptr_t>(p.q) & 15) return false;
   return true;
@@ -546,11 +601,7 @@ bool decode_fast_supported(const DecodeParams& p) {
 
 template <int RK, int RV>
 static int launch_nw(const DecodeParams& p, cudaStream_t st) {
-  switch (p.Tb) {
-    case 128: return fastk::launch<RK, RV, 2>(p, st);
-    case 256: return fastk::launch<RK, RV, 4>(p, st);
-    default: return fastk::launch<RK, RV, 8>(p, st);
-  }
+  return p.Tb == 256 ? fastk::launch<RK, RV, 4>(p, st) : fastk::launch<RK, RV, 8>(p, st);
 }
 
 int decode_fast_cold(const DecodeParams& p, cudaStream_t st) {
