@@ -20,9 +20,9 @@
 // Warps combine (m, l, v_lat) in shared memory; v_lat is expanded once through B_V and
 // written as the unit's partial (m, l, o[128]) for the hot-tier/merge kernel.
 //
-// Token order inside each 16-token group is the permutation slot_to_token() below,
-// chosen so that value codes load with one ldmatrix per group; softmax is
-// order-invariant.
+// Value codes are stored in shared memory with the 16 tokens of each tile reordered
+// (0,1,8,9, 2,3,10,11, ...) so that one ldmatrix per 16 tokens yields mma.sync A
+// fragments directly.
 #include <math.h>
 
 #include "spx_common.cuh"
@@ -121,16 +121,20 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
-// Two 16x256b loads (columns c0.. and c1..) and the wait, in one statement.
-__device__ __forceinline__ void tmem_ld16x256_x2x2(uint32_t ta, uint32_t tb, uint32_t (&r)[8], uint32_t (&q)[8]) {
+// Three 16x256b.x2 loads (24 registers) issued without waiting.
+__device__ __forceinline__ void tmem_ld3(uint32_t ta, uint32_t tb, uint32_t tc, uint32_t (&r)[24]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%16];\n\t"
-      "tcgen05.ld.sync.aligned.16x256b.x2.b32 {%8, %9, %10, %11, %12, %13, %14, %15}, [%17];\n\t"
-      "tcgen05.wait::ld.sync.aligned;"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(q[0]), "=r"(q[1]), "=r"(q[2]), "=r"(q[3]), "=r"(q[4]), "=r"(q[5]), "=r"(q[6]), "=r"(q[7])
-      : "r"(ta), "r"(tb)
+      "tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%24];\n\t"
+      "tcgen05.ld.sync.aligned.16x256b.x2.b32 {%8, %9, %10, %11, %12, %13, %14, %15}, [%25];\n\t"
+      "tcgen05.ld.sync.aligned.16x256b.x2.b32 {%16, %17, %18, %19, %20, %21, %22, %23}, [%26];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23])
+      : "r"(ta), "r"(tb), "r"(tc)
       : "memory");
+}
+// Wait for this thread's TMEM loads; the registers are tied to the wait so that no use
+// of them can be scheduled before it.
+__device__ __forceinline__ void tmem_wait_ld_tied(uint32_t (&r)[24]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]) :: "memory");
 }
 
 // ------------------------------------------------------------- warp MMA helpers -----
@@ -155,6 +159,9 @@ __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r
 __device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
 }
+__device__ __forceinline__ void ldsm_x2_t(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
 __device__ __forceinline__ uint32_t movm_t(uint32_t x) {
   uint32_t y;
   asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
@@ -176,12 +183,6 @@ __device__ __forceinline__ void i8x4_to_h2(uint32_t w, uint32_t& lo, uint32_t& h
   hi = h2u(__hsub2(u2h(h), bias));
 }
 
-// Slot s of an m-tile holds token PI(s); PI_INV maps a token back to its slot.
-__host__ __device__ __forceinline__ int slot_to_token(int s) {
-  return s < 8 ? 4 * (s >> 1) + (s & 1) : 4 * ((s - 8) >> 1) + 2 + (s & 1);
-}
-__host__ __device__ __forceinline__ int token_to_slot(int tau) { return 2 * (tau >> 2) + (tau & 1) + 8 * ((tau & 3) >> 1); }
-
 template <int RK, int RV, int NW>
 struct Cfg {
   static constexpr int NT = NW * 32;
@@ -198,7 +199,8 @@ struct Cfg {
   static constexpr int OFF_B = OFF_A + MT * ATILE;      // UMMA B tile  [16 n-chunks][RK rows][16 B]
   static constexpr int OFF_CV = OFF_B + BK;             // value codes [T/16][RV][16 B], XOR-swizzled rows
   static constexpr int OFF_Q = OFF_CV + CV;             // query [8][16 chunks], XOR-swizzled chunks
-  static constexpr int OFF_SM = OFF_Q + QB;             // per-warp m [NW][8]
+  static constexpr int OFF_BV = OFF_Q + QB;             // value basis [RV][16 chunks], XOR-swizzled
+  static constexpr int OFF_SM = OFF_BV + BV;            // per-warp m [NW][8]
   static constexpr int OFF_SL = OFF_SM + NW * 8 * 4;    // per-warp l [NW][8]
   static constexpr int OFF_SV = OFF_SL + NW * 8 * 4;    // per-warp v_lat [NW][RV][8]
   static constexpr int OFF_VL = OFF_SV + NW * RV * 8 * 4;   // combined v_lat [8][RV]
@@ -286,7 +288,7 @@ __global__ void __launch_bounds__(NW * 32, 1) cold_fast_kernel(DecodeParams p, i
     int64_t a[2];
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
-      const int64_t pos = p0 + G.token0() + slot_to_token(g + 8 * hh);
+      const int64_t pos = p0 + G.token0() + g + 8 * hh;
       int64_t aa = p.mode == SPX_ROPE_DISTANCE ? (p.qpos - pos > 0 ? p.qpos - pos : 0) : pos;
       a[hh] = aa < 0 ? 0 : (aa >= p.rope_len ? p.rope_len - 1 : aa);
     }
@@ -345,17 +347,20 @@ __global__ void __launch_bounds__(NW * 32, 1) cold_fast_kernel(DecodeParams p, i
     }
     // ---- conversion pass -----------------------------------------------------------
     {
-      // key codes -> FP16 A tiles: row m of M-tile mt holds token mt*128 + (m & ~15) +
-      // slot_to_token(m & 15); 16-byte K-chunks of 8 codes, K-major, no swizzle
-      for (int e = tid; e < C::TB * (RK / 8); e += C::NT) {
-        const int tau = e % C::TB, kc = e / C::TB;
-        const uint2 v = *reinterpret_cast<const uint2*>(st + tau * RK + kc * 8);
-        const int mt = tau >> 7;
-        const int m = (tau & 127 & ~15) + token_to_slot(tau & 15);
-        uint4 o;
-        i8x4_to_h2(v.x, o.x, o.y);
-        i8x4_to_h2(v.y, o.z, o.w);
-        *reinterpret_cast<uint4*>(sA + mt * C::ATILE + kc * 2048 + (m >> 3) * 128 + (m & 7) * 16) = o;
+      // key codes -> FP16 A tiles (row m of M-tile mt = token mt*128 + m), 16-byte
+      // K-chunks of 8 codes, K-major, no swizzle; one item = 16 codes of one token
+      for (int e = tid; e < C::TB * (RK / 16); e += C::NT) {
+        const int tau = e % C::TB, hf = e / C::TB;
+        const uint4 v = *reinterpret_cast<const uint4*>(st + tau * RK + hf * 16);
+        const int m = tau & 127;
+        uint8_t* dst = sA + (tau >> 7) * C::ATILE + 2 * hf * 2048 + (m >> 3) * 128 + (m & 7) * 16;
+        uint4 o0, o1;
+        i8x4_to_h2(v.x, o0.x, o0.y);
+        i8x4_to_h2(v.y, o0.z, o0.w);
+        i8x4_to_h2(v.z, o1.x, o1.y);
+        i8x4_to_h2(v.w, o1.z, o1.w);
+        *reinterpret_cast<uint4*>(dst) = o0;
+        *reinterpret_cast<uint4*>(dst + 2048) = o1;
       }
       // key basis [RK][128] -> MN-major B tile [16 n-chunks][RK rows][16 B]
       const uint4* srcb = reinterpret_cast<const uint4*>(st + C::CK + C::CV);
@@ -363,11 +368,25 @@ __global__ void __launch_bounds__(NW * 32, 1) cold_fast_kernel(DecodeParams p, i
         const int k = e % RK, nc = e / RK;
         reinterpret_cast<uint4*>(sB)[nc * RK + k] = srcb[k * 16 + nc];
       }
-      // value codes [RV][T] -> [T/16][RV][16 tokens], row index XOR (tile & 7)
+      // value codes [RV][T] -> [T/16][RV][16 tokens], row index XOR (tile & 7); the
+      // tokens of a row are reordered (0,1,8,9, 2,3,10,11, 4,5,12,13, 6,7,14,15) so that
+      // word t of an ldmatrix row holds tokens 2t, 2t+1, 2t+8, 2t+9
       const uint4* srcv = reinterpret_cast<const uint4*>(st + C::CK);
       for (int e = tid; e < C::CV / 16; e += C::NT) {
         const int r = e / (C::TB / 16), tt = e % (C::TB / 16);
-        reinterpret_cast<uint4*>(cV)[tt * RV + (r ^ (tt & 7))] = srcv[e];
+        const uint4 v = srcv[e];
+        uint4 o;
+        o.x = __byte_perm(v.x, v.z, 0x5410);
+        o.y = __byte_perm(v.x, v.z, 0x7632);
+        o.z = __byte_perm(v.y, v.w, 0x5410);
+        o.w = __byte_perm(v.y, v.w, 0x7632);
+        reinterpret_cast<uint4*>(cV)[tt * RV + (r ^ (tt & 7))] = o;
+      }
+      // value basis [RV][128] -> chunk index XOR (rank & 7) (conflict-free ldmatrix)
+      const uint4* srcbv = reinterpret_cast<const uint4*>(st + C::CK + C::CV + C::BK);
+      for (int e = tid; e < RV * 16; e += C::NT) {
+        const int R = e >> 4, n = e & 15;
+        reinterpret_cast<uint4*>(sm + C::OFF_BV)[R * 16 + (n ^ (R & 7))] = srcbv[e];
       }
       // query rows, 16-byte chunk index XOR head
       const uint4* srcq = reinterpret_cast<const uint4*>(st + C::CK + C::CV + C::BK + C::BV);
@@ -401,8 +420,6 @@ __global__ void __launch_bounds__(NW * 32, 1) cold_fast_kernel(DecodeParams p, i
     // ---- scores: K~ from TMEM, rotate, dot ----------------------------------------
     float sc[4][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.f;
-#pragma unroll
     for (int i = 0; i < 4; ++i) {
       const Group<NW> G(w, i);
       const bool first_of_tile = (NW == 8) || ((i & 1) == 0);
@@ -416,26 +433,37 @@ __global__ void __launch_bounds__(NW * 32, 1) cold_fast_kernel(DecodeParams p, i
       const uint32_t lrow = (uint32_t)G.lane_off << 16;
       const uint32_t dcol = tbase + lrow + 256u + 128u * (uint32_t)b;
       const uint32_t tcol = tbase + lrow + (uint32_t)G.tcol;
+      float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t cur[24];
+      tmem_ld3(dcol, dcol + 64, tcol, cur);
+      tmem_wait_ld_tied(cur);
 #pragma unroll
       for (int s4 = 0; s4 < 4; ++s4) {
-        uint32_t d1[8], d2[8], tr[8];
-        tmem_ld16x256_x2x2(dcol + 16 * s4, dcol + 64 + 16 * s4, d1, d2);
-        tmem_ld16x256_x2(tcol + 16 * s4, tr);
+        uint32_t nxt[24];
+        if (s4 < 3) tmem_ld3(dcol + 16 * (s4 + 1), dcol + 64 + 16 * (s4 + 1), tcol + 16 * (s4 + 1), nxt);
         uint32_t k1[4], k2[4];
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {   // hh: row g (0) or g+8 (1)
-            const __half2 a1 = u2h(pack_f2(__uint_as_float(d1[4 * cc + 2 * hh]), __uint_as_float(d1[4 * cc + 2 * hh + 1])));
-            const __half2 a2 = u2h(pack_f2(__uint_as_float(d2[4 * cc + 2 * hh]), __uint_as_float(d2[4 * cc + 2 * hh + 1])));
-            const __half2 c = u2h(tr[4 * cc + 2 * hh]), sn = u2h(tr[4 * cc + 2 * hh + 1]);
+            const int e = 4 * cc + 2 * hh;
+            const __half2 a1 = u2h(pack_f2(__uint_as_float(cur[e]), __uint_as_float(cur[e + 1])));
+            const __half2 a2 = u2h(pack_f2(__uint_as_float(cur[8 + e]), __uint_as_float(cur[8 + e + 1])));
+            const __half2 c = u2h(cur[16 + e]), sn = u2h(cur[16 + e + 1]);
             k1[2 * cc + hh] = h2u(__hfma2(c, a1, __hneg2(__hmul2(sn, a2))));   // c K1 - s K2
             k2[2 * cc + hh] = h2u(__hfma2(c, a2, __hmul2(sn, a1)));            // s K1 + c K2
           }
         }
-        mma16816(sc[i], k1[0], k1[1], k1[2], k1[3], qf[s4][0], qf[s4][1]);
-        mma16816(sc[i], k2[0], k2[1], k2[2], k2[3], qf[s4 + 4][0], qf[s4 + 4][1]);
+        mma16816(sa, k1[0], k1[1], k1[2], k1[3], qf[s4][0], qf[s4][1]);
+        mma16816(sb, k2[0], k2[1], k2[2], k2[3], qf[s4 + 4][0], qf[s4 + 4][1]);
+        if (s4 < 3) {
+          tmem_wait_ld_tied(nxt);
+#pragma unroll
+          for (int q = 0; q < 24; ++q) cur[q] = nxt[q];
+        }
       }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[i][e] = sa[e] + sb[e];
       // accumulator b is free once every warp has read this M-tile: refill it
       const bool last_of_tile = (NW == 8) || ((i & 1) == 1);
       if (last_of_tile && G.mt + 2 < C::MT) {
@@ -445,19 +473,23 @@ __global__ void __launch_bounds__(NW * 32, 1) cold_fast_kernel(DecodeParams p, i
       }
     }
     // ---- per-warp softmax over 64 tokens (log2 domain) ----------------------------
+    // raw scores times kscale (> 0) are the logits in log2 units; fold the scale into
+    // the exp2 argument instead of scaling every score
+    // (the max of the scaled logits is max*k for k >= 0 and min*k for k < 0)
+    const bool kpos = kscale >= 0.f;
     float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) sc[i][e] *= kscale;
-      mx0 = fmaxf(mx0, fmaxf(sc[i][0], sc[i][2]));
-      mx1 = fmaxf(mx1, fmaxf(sc[i][1], sc[i][3]));
+      mx0 = fmaxf(mx0, kpos ? fmaxf(sc[i][0], sc[i][2]) : -fminf(sc[i][0], sc[i][2]));
+      mx1 = fmaxf(mx1, kpos ? fmaxf(sc[i][1], sc[i][3]) : -fminf(sc[i][1], sc[i][3]));
     }
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) {
       mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
       mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
     }
+    mx0 = kpos ? mx0 * kscale : -mx0 * kscale;
+    mx1 = kpos ? mx1 * kscale : -mx1 * kscale;
     const bool live0 = 2 * t < nrep, live1 = 2 * t + 1 < nrep;
     float l0 = 0.f, l1 = 0.f;
     float vacc[RV / 16][4];
@@ -465,10 +497,10 @@ __global__ void __launch_bounds__(NW * 32, 1) cold_fast_kernel(DecodeParams p, i
     for (int rt = 0; rt < RV / 16; ++rt) vacc[rt][0] = vacc[rt][1] = vacc[rt][2] = vacc[rt][3] = 0.f;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      sc[i][0] = live0 ? exp2f(sc[i][0] - mx0) : 0.f;
-      sc[i][2] = live0 ? exp2f(sc[i][2] - mx0) : 0.f;
-      sc[i][1] = live1 ? exp2f(sc[i][1] - mx1) : 0.f;
-      sc[i][3] = live1 ? exp2f(sc[i][3] - mx1) : 0.f;
+      sc[i][0] = live0 ? exp2f(fmaf(sc[i][0], kscale, -mx0)) : 0.f;
+      sc[i][2] = live0 ? exp2f(fmaf(sc[i][2], kscale, -mx0)) : 0.f;
+      sc[i][1] = live1 ? exp2f(fmaf(sc[i][1], kscale, -mx1)) : 0.f;
+      sc[i][3] = live1 ? exp2f(fmaf(sc[i][3], kscale, -mx1)) : 0.f;
       l0 += sc[i][0] + sc[i][2];
       l1 += sc[i][1] + sc[i][3];
       // ---- v_lat[rank][head] += codes_V^T . P  (one ldmatrix per 16 tokens) ---------
@@ -534,21 +566,44 @@ __global__ void __launch_bounds__(NW * 32, 1) cold_fast_kernel(DecodeParams p, i
       }
     }
     __syncthreads();
-    // ---- expand once through B_V and write the partial ----------------------------
+    // ---- expand once through B_V (mma.sync) and write the partial -----------------
+    // o[h][d] = l_h * sum_r (v_lat[h][r] / l_h) B_V[r][d]: the normalised v_lat is a
+    // weighted mean of INT8 codes (|.| <= 127), safe as an f16 operand.
     {
-      const __half* bv = reinterpret_cast<const __half*>(st + C::CK + C::CV + C::BK);
       float* rec = p.ws + (unit * p.nparts + j) * (int64_t)nrep * (FD + 4);
-      for (int e = tid; e < nrep * (FD / 2); e += C::NT) {
-        const int h = e / (FD / 2), d = 2 * (e % (FD / 2));
-        float o0 = 0.f, o1 = 0.f;
-#pragma unroll 8
-        for (int r = 0; r < RV; ++r) {
-          const float2 bb = __half22float2(*reinterpret_cast<const __half2*>(bv + r * FD + d));
-          const float vl = sVL[h * RV + r];
-          o0 = fmaf(vl, bb.x, o0);
-          o1 = fmaf(vl, bb.y, o1);
+      const uint32_t bv_u = smem_u32(sm + C::OFF_BV);
+      const bool hl = g < nrep;
+      const float inv_l = hl ? 1.f / sML[2 * g + 1] : 0.f;
+      uint32_t va[RV / 16][2];
+#pragma unroll
+      for (int ks = 0; ks < RV / 16; ++ks) {
+        const float2 x0 = *reinterpret_cast<const float2*>(sVL + g * RV + 16 * ks + 2 * t);
+        const float2 x1 = *reinterpret_cast<const float2*>(sVL + g * RV + 16 * ks + 2 * t + 8);
+        va[ks][0] = hl ? pack_f2(x0.x * inv_l, x0.y * inv_l) : 0u;
+        va[ks][1] = hl ? pack_f2(x1.x * inv_l, x1.y * inv_l) : 0u;
+      }
+      const float oscale = hl ? sML[2 * g + 1] * vscale : 0.f;
+      constexpr int NTW = 16 / NW;   // n-tiles (8 dims each) per warp
+#pragma unroll
+      for (int q = 0; q < NTW; ++q) {
+        const int n = w * NTW + q;
+        float o[4] = {0.f, 0.f, 0.f, 0.f};
+        const int mi = lane >> 3, rr = lane & 7;
+        if constexpr (RV == 32) {
+          const int R = 16 * (mi >> 1) + 8 * (mi & 1) + rr;
+          uint32_t b00, b01, b10, b11;
+          ldsm_x4_t(bv_u + R * 256 + ((n ^ (R & 7)) << 4), b00, b01, b10, b11);
+          mma16816(o, va[0][0], 0u, va[0][1], 0u, b00, b01);
+          mma16816(o, va[1][0], 0u, va[1][1], 0u, b10, b11);
+        } else {
+          const int R = 8 * (mi & 1) + rr;
+          uint32_t b00, b01;
+          ldsm_x2_t(bv_u + R * 256 + ((n ^ (R & 7)) << 4), b00, b01);
+          mma16816(o, va[0][0], 0u, va[0][1], 0u, b00, b01);
         }
-        *reinterpret_cast<float2*>(rec + h * (FD + 4) + 4 + d) = make_float2(o0 * vscale, o1 * vscale);
+        if (hl)
+          *reinterpret_cast<float2*>(rec + g * (FD + 4) + 4 + 8 * n + 2 * t) =
+              make_float2(o[0] * oscale, o[1] * oscale);
       }
       if (tid < nrep) {
         rec[tid * (FD + 4) + 0] = sML[2 * tid] * LN2;
