@@ -124,6 +124,24 @@ typedef struct spx_decode_args {
 SPX_API size_t spx_decode_workspace_size(const spx_decode_args* args);
 SPX_API int spx_decode_attn(const spx_decode_args* args, void* stream);
 
+/* Decode attention for callers that cannot allocate device memory.  This entry point has
+ * no counterpart in the reference; it exists for hosts with no device allocator on the
+ * decode path -- for example a runtime embedding this library through cgo, JNI or
+ * another FFI that owns no CUDA allocator, or a serving loop that may not call
+ * cudaMalloc/cudaFree there because those calls can synchronise the device or fail under
+ * a fixed memory budget.  It computes exactly what spx_decode_attn computes; the caller
+ * still passes every input and the output, but args->workspace and
+ * args->workspace_bytes are ignored: the scratch is a fixed array of
+ * SPX_NOALLOC_SCRATCH_BYTES built into the library, which every device that loads this
+ * part of the library holds until the process exits.  Calls needing more scratch than
+ * that (spx_decode_workspace_size) fail with SPX_ERR_WORKSPACE before launching anything.
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress,
+ * with that device current); make that first call before any stream capture.  All calls
+ * on a device share the one array and it keeps the last call's contents, so calls whose
+ * GPU work overlaps (other streams, other host threads) race: serialise them. */
+#define SPX_NOALLOC_SCRATCH_BYTES (64u << 20)
+SPX_API int spx_decode_attn_noalloc(const spx_decode_args* args, void* stream);
+
 /* ---------------------------------------------------------------------------------
  * Batched randomized SVD + block compression.  Replaces rsvd.py:28-157 and
  * spectral_cache.py:345-407.  Computes, per matrix M_i [m, n], a rank-k factorisation

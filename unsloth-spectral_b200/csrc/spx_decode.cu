@@ -367,6 +367,12 @@ int decode_dispatch(const DecodeParams& p, cudaStream_t st) {
   return SPX_DISPATCH_DTYPE(p.dtype, T, [&] { return launch_hot_merge<T>(p, st); });
 }
 
+int decode_params(const spx_decode_args* a, DecodeParams* p) {
+  const int rc = make_params(a, p);
+  if (rc == SPX_OK) p->dtype = a->dtype;
+  return rc;
+}
+
 }  // namespace spx
 
 using namespace spx;

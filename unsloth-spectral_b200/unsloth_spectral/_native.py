@@ -15,7 +15,9 @@ import torch
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libspx.so")
 
 SPX_OK = 0
+SPX_ERR_WORKSPACE = 5
 SPX_ERR_EMPTY = 6
+NOALLOC_SCRATCH_BYTES = 64 << 20
 SPX_F32, SPX_F16, SPX_BF16 = 0, 1, 2
 SPX_ROPE_DISTANCE, SPX_ROPE_ABSOLUTE = 0, 1
 
@@ -82,6 +84,7 @@ class BlockValueArgs(C.Structure):
 EXPORTS = {
     "spx_decode_workspace_size": (C.c_size_t, [C.POINTER(DecodeArgs)]),
     "spx_decode_attn": (C.c_int, [C.POINTER(DecodeArgs), C.c_void_p]),
+    "spx_decode_attn_noalloc": (C.c_int, [C.POINTER(DecodeArgs), C.c_void_p]),
     "spx_rsvd_workspace_size": (C.c_size_t, [C.POINTER(RsvdArgs)]),
     "spx_rsvd_compress": (C.c_int, [C.POINTER(RsvdArgs), C.c_void_p]),
     "spx_quantize_int8": (C.c_int, [C.POINTER(QuantArgs), C.c_void_p]),

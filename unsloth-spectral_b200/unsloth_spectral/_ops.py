@@ -94,13 +94,13 @@ def rsvd(M: torch.Tensor, omega: torch.Tensor, k: int, n_iter: int, *, want_fact
     return U, S, Vh
 
 
-def decode(q: torch.Tensor, tiers, cos: torch.Tensor, sin: torch.Tensor, query_position: int, *,
-           rope_mode: int, mask: Optional[torch.Tensor] = None, scale: Optional[float] = None,
-           out: Optional[torch.Tensor] = None, tied: Optional[bool] = None) -> torch.Tensor:
-    """Run ``spx_decode_attn`` over ``tiers`` (a ``DeviceTiers``).  ``q`` is
-    ``[L, B, H_q, D]`` in the tiers' dtype; returns ``[L, B, H_q, D]``."""
+def decode_args(q: torch.Tensor, tiers, cos: torch.Tensor, sin: torch.Tensor, query_position: int, *,
+                rope_mode: int, mask: Optional[torch.Tensor] = None, scale: Optional[float] = None,
+                out: Optional[torch.Tensor] = None, tied: Optional[bool] = None):
+    """Build the ``spx_decode_args`` of a decode over ``tiers`` (no workspace set).
+    Returns ``(args, out, keepalive)``; ``keepalive`` holds the temporaries the pointers
+    refer to and must outlive the call."""
     dev = q.device
-    lib = N.lib_for(dev)
     L, B, Hq, D = q.shape
     t = tiers
     if scale is None:
@@ -133,10 +133,23 @@ def decode(q: torch.Tensor, tiers, cos: torch.Tensor, sin: torch.Tensor, query_p
         scale_v=N.ptr(t.scale_v), basis_k=N.ptr(t.basis_k), basis_v=N.ptr(t.basis_v),
         block_pos=N.ptr(t.block_pos), hot_k=N.ptr(t.hot_k), hot_v=N.ptr(t.hot_v), hot_pos=N.ptr(t.hot_pos),
         cos_table=N.ptr(cos32), sin_table=N.ptr(sin32), mask=N.ptr(mask_u8), out=N.ptr(out))
+    return a, out, (q, cos32, sin32, mask_u8)
+
+
+def decode(q: torch.Tensor, tiers, cos: torch.Tensor, sin: torch.Tensor, query_position: int, *,
+           rope_mode: int, mask: Optional[torch.Tensor] = None, scale: Optional[float] = None,
+           out: Optional[torch.Tensor] = None, tied: Optional[bool] = None) -> torch.Tensor:
+    """Run ``spx_decode_attn`` over ``tiers`` (a ``DeviceTiers``).  ``q`` is
+    ``[L, B, H_q, D]`` in the tiers' dtype; returns ``[L, B, H_q, D]``."""
+    dev = q.device
+    lib = N.lib_for(dev)
+    a, out, keep = decode_args(q, tiers, cos, sin, query_position, rope_mode=rope_mode, mask=mask, scale=scale,
+                               out=out, tied=tied)
     need = lib.spx_decode_workspace_size(a)
     ws = N.workspace(dev, need)
     a.workspace, a.workspace_bytes = N.ptr(ws), ws.numel()
     N.check(lib, lib.spx_decode_attn(a, N.stream_handle(dev)), "spx_decode_attn")
+    del keep
     return out
 
 
