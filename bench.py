@@ -54,6 +54,18 @@ def algorithmic_bytes_per_step(c, kv_heads_local):
     return per_head * c["layers"] * c["batch"] * kv_heads_local
 
 
+def measured_traffic():
+    """Per-launch DRAM bytes of the decode call from the committed ncu summary, if any."""
+    p = os.path.join(REPO, "profiles", "decode_cold_fast_config2.md")
+    try:
+        for line in open(p):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
 def read_peaks():
     p = os.path.join(REPO, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -397,7 +409,10 @@ def run_ours(args, c):
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": qs_host[0].numel() * 2,
                     "d2h_bytes_per_step": out_host.numel() * 2},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
+                         "frac": achieved / peak,
+                         "traffic": measured_traffic() if (world == 1 and c["layers"] == CFG["layers"]) else None,
+                         "traffic_source": "profiles/decode_cold_fast_config2.md (ncu launch list, same command)",
+                         "peak_kind": peak_kind,
                          "kernel": "spx_decode_attn (cold partials + hot/merge)",
                          "algorithmic_bytes_per_launch": bytes_launch, "launch_ms": kern_ms},
             "rsvd": {"blocks_per_s": nb_rs * world / (rs_ms / 1e3), "blocks": 4096, "k": 32, "n_iter": 2,

@@ -1,0 +1,92 @@
+"""KV-head sharding of decode across ranks (the multi-GPU layout of bench.py), checked
+on CPU with gloo ranks: each rank computes its head slice with the oracle and one
+all-gather reassembles the single-rank output exactly."""
+import math
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import spectral_oracle as so
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _case(seed=0, H=4, nrep=2, D=32, T=32, nblk=3, k=8, hot=5):
+    rng = np.random.default_rng(seed)
+    codes_K = rng.integers(-127, 128, size=(nblk, H, T, k), dtype=np.int8)
+    codes_V = rng.integers(-127, 128, size=(nblk, H, T, k), dtype=np.int8)
+    scale = (rng.random((nblk, H)) * 0.01 + 0.01).astype(np.float32)
+    basis = rng.standard_normal((nblk, H, k, D)).astype(np.float32) / math.sqrt(D)
+    hot_K = rng.standard_normal((1, H, hot, D)).astype(np.float32)
+    hot_V = rng.standard_normal((1, H, hot, D)).astype(np.float32)
+    Q = rng.standard_normal((1, H * nrep, 1, D)).astype(np.float32)
+    qpos = nblk * T + hot
+    cos, sin = so.rope_tables(qpos + 4, D, 1e4)
+    return dict(codes_K=codes_K, codes_V=codes_V, scale=scale, basis=basis, hot_K=hot_K, hot_V=hot_V, Q=Q,
+                qpos=qpos, cos=cos, sin=sin, H=H, nrep=nrep, T=T, nblk=nblk, hot=hot)
+
+
+def _decode_slice(c, h0, h1):
+    """Oracle decode of KV heads [h0, h1) and their query heads."""
+    nrep = c["nrep"]
+    sl = slice(h0, h1)
+    blocks = so.blocks_from_codes(c["codes_K"][:, sl], c["scale"][:, sl], c["basis"][:, sl], c["codes_V"][:, sl],
+                                  c["scale"][:, sl], c["basis"][:, sl], np.arange(c["nblk"]) * c["T"])
+    Q = c["Q"][:, h0 * nrep:h1 * nrep]
+    hp = np.arange(c["nblk"] * c["T"], c["nblk"] * c["T"] + c["hot"])
+    return so.spectral_attention_decode(Q, blocks, c["hot_K"][:, sl], c["hot_V"][:, sl], hp, c["cos"], c["sin"],
+                                        c["qpos"])
+
+
+def _worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        c = _case()
+        Hl = c["H"] // world
+        part = torch.from_numpy(_decode_slice(c, rank * Hl, (rank + 1) * Hl)).contiguous()   # [1, Hl*nrep, 1, D]
+        gathered = [torch.empty_like(part) for _ in range(world)]
+        dist.all_gather(gathered, part)
+        if rank == 0:
+            q.put(torch.cat(gathered, dim=1).numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_head_sharded_decode_reassembles_single_rank_output(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    c = _case()
+    ref = _decode_slice(c, 0, c["H"])
+    np.testing.assert_array_equal(out, ref.astype(np.float32))
+
+
+def test_bench_shard_byte_accounting():
+    """The per-rank algorithmic bytes of bench.py add up to the single-GPU figure."""
+    import bench
+    c = dict(bench.CFG)
+    total = bench.algorithmic_bytes_per_step(c, c["kv_heads"])
+    for world in (2, 4, 8):
+        assert bench.algorithmic_bytes_per_step(c, c["kv_heads"] // world) * world == total
+    assert abs(total - 26.06e9) < 0.01e9
