@@ -75,7 +75,7 @@ def read_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi samples (200 ms) during the timed region."""
+    """nvidia-smi samples (every 50 ms) from the warm-up through the timed region."""
 
     def __init__(self, index):
         self.index = index
@@ -88,7 +88,7 @@ class ClockSampler:
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -210,9 +210,18 @@ def decode_args(c, t, q, out, cos, sin, qpos, ws, Hl):
 # -------------------------------------------------------------------- CPU baseline
 def cpu_sample_decode(c, n_calls, seed=0):
     """Time the CPU oracle port on ``n_calls`` (sequence, layer) decodes of the
-    workload's shape; returns (seconds per call, threads)."""
+    workload's shape with every host core this process may use; returns (seconds per
+    call, threads)."""
     sys.path.insert(0, REPO)
     from oracle import spectral_oracle as so
+    from threadpoolctl import threadpool_limits
+    ncores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(ncores)
+    with threadpool_limits(limits=ncores):
+        return _cpu_sample_decode(so, c, n_calls, seed), ncores
+
+
+def _cpu_sample_decode(so, c, n_calls, seed):
     rng = np.random.default_rng(seed)
     H, D, T, NB, R, hot, Hq = (c["kv_heads"], c["head_dim"], c["block"], c["blocks"], c["rank"], c["hot"],
                                c["q_heads"])
@@ -232,7 +241,7 @@ def cpu_sample_decode(c, n_calls, seed=0):
     t0 = time.perf_counter()
     for _ in range(n_calls):
         so.spectral_attention_decode(Q, blocks, hk, hv, hp, cos, sin, qpos)
-    return (time.perf_counter() - t0) / n_calls, torch.get_num_threads()
+    return (time.perf_counter() - t0) / n_calls
 
 
 def cpu_tokens_per_s(c, per_call_s):
@@ -314,11 +323,11 @@ def run_ours(args, c):
         torch.cuda.synchronize(dev)
 
     # ---- device-resident timing (value)
-    for i in range(args.warmup):
-        step(i, qs_dev[i % nq])
-    barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
+        for i in range(args.warmup):
+            step(i, qs_dev[i % nq])
+        barrier()
         ev0.record(stream)
         for i in range(args.steps):
             step(i, qs_dev[(args.warmup + i) % nq])
