@@ -138,7 +138,7 @@ def build_tiers(c, rank_id, world, dev):
     h0 = rank_id * Hl
     t = dict(
         codes_k=torch.empty(L, B, Hl, NB, T, R, dtype=torch.int8, device=dev),
-        codes_v=torch.empty(L, B, Hl, NB, R, T, dtype=torch.int8, device=dev),
+        codes_v=torch.empty(L, B, Hl, NB, R * T, dtype=torch.int8, device=dev),   # value-tile layout
         scale_k=torch.empty(L, B, Hl, NB, dtype=torch.float32, device=dev),
         scale_v=torch.empty(L, B, Hl, NB, dtype=torch.float32, device=dev),
         basis_k=torch.empty(L, B, Hl, NB, R, D, dtype=torch.float16, device=dev),
@@ -159,15 +159,12 @@ def build_tiers(c, rank_id, world, dev):
             cold = Xl[:, :, :NB * T]
             g = torch.Generator(device=dev).manual_seed(10_000 + 2 * l + (name == "v"))
             omega = torch.randn(nm, D, r, generator=g, device=dev)
-            if name == "k":
-                cs = (T * R, R, 1)
-            else:
-                cs = (R * T, 1, T)
+            cs = (T * R, R, 1) if name == "k" else (R * T, 0, 0)
             torch.cuda.synchronize()
             t0 = time.perf_counter()
             _ops.rsvd(cold, omega, R, c["n_iter"], want_factors=False, codes=t[f"codes_{name}"][l], codes_strides=cs,
                       rank_pad=R, qscale=t[f"scale_{name}"][l], scale_stride=1, basis=t[f"basis_{name}"][l],
-                      basis_stride=R * D, M_mat_stride=T * D, num_mats=nm, m=T, n=D)
+                      basis_stride=R * D, M_mat_stride=T * D, num_mats=nm, m=T, n=D, codes_tiled=(name == "v"))
             torch.cuda.synchronize()
             rs += time.perf_counter() - t0
             del Xl, cold, omega

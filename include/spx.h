@@ -26,7 +26,11 @@
  *
  * Cold-tier layout (one cache = L layers x B sequences x H KV heads, NBc block slots):
  *   codes_k  int8   [L][B][H][NBc][T_blk][RK]   token-major INT8 key coefficients
- *   codes_v  int8   [L][B][H][NBc][RV][T_blk]   rank-major  INT8 value coefficients
+ *   codes_v  int8   [L][B][H][NBc][T_blk*RV]    INT8 value coefficients, value-tile layout:
+ *            code (r, t) of a block at byte ((t/16)*RV + (r ^ ((t/16) & 7)))*16 + pos(t%16),
+ *            pos(x) = 4*((x%8)/2) + x%2 + 2*(x/8)  (16-token tiles of [RV][16] bytes,
+ *            rows XOR-swizzled, tokens ordered 0,1,8,9,2,3,10,11,...: the layout the tensor
+ *            cores read directly)
  *   scale_k  f32    [L][B][H][NBc]              dequantisation scale (coeff = code*scale)
  *   scale_v  f32    [L][B][H][NBc]
  *   basis_k  dtype  [L][B][H][NBc][RK][D]        FP16/BF16/FP32 key basis (Vh rows)
@@ -171,6 +175,8 @@ typedef struct spx_rsvd_args {
   int64_t codes_t_stride;
   int64_t codes_j_stride;
   int32_t codes_rank_pad;  /* write zero codes for j in [k, codes_rank_pad) (>= k) */
+  int32_t codes_tiled;     /* 1: ignore the t/j strides and write each matrix in the value-tile
+                              layout of codes_v (m % 16 == 0, codes_rank_pad % 8 == 0) */
   float* qscale;           /* with codes: scale of matrix i at qscale[i*scale_mat_stride] */
   int64_t scale_mat_stride;
   float* qminmax;          /* optional: (min, max) of C_i at qminmax[i*minmax_mat_stride + {0,1}] */
@@ -211,7 +217,7 @@ SPX_API int spx_quantize_int8(const spx_quant_args* args, void* stream);
 typedef struct spx_reconstruct_args {
   int32_t batch, num_kv_heads, head_dim, block_size, num_blocks, block_capacity;
   int32_t rank;            /* stored (padded) rank */
-  int32_t rank_major;      /* 0: codes [..][T_blk][rank] (keys); 1: [..][rank][T_blk] (values) */
+  int32_t rank_major;      /* 0: codes [..][T_blk][rank] (keys); 1: value-tile layout (values) */
   int32_t dtype;           /* dtype of basis and out */
   int32_t out_tokens;      /* token capacity of out per (b, h) */
   const int8_t* codes;

@@ -333,6 +333,15 @@ def test_cache_compression_codes_bit_exact_and_error_parity():
     assert (t.codes_k[0, :, 0, :, 16:] == 0).all()
     np.testing.assert_array_equal(t.scale_k[0, :, 0].cpu().numpy(), scale)
     np.testing.assert_array_equal(t.minmax_k[0, :, 0].cpu().numpy(), mm)
+    # value codes are stored in the value-tile layout; untile and compare the same way
+    Uv, Sv, _ = _ops.rsvd(V[0, :, :T].half().cuda(), om_v, 32, 2)
+    _, mm_v, codes_v, scale_v = so.quantize_int8_batched((Uv * Sv[:, None, :]).cpu().numpy())
+    nat = torch.empty_like(t.codes_v[0, :, 0])
+    nat[:, _ops.vtile_index(T, t.rank_v_pad, nat.device)] = t.codes_v[0, :, 0]
+    nat = nat.view(H, t.rank_v_pad, T).cpu().numpy()
+    np.testing.assert_array_equal(nat[:, :32].transpose(0, 2, 1), codes_v)
+    assert (nat[:, 32:] == 0).all()
+    np.testing.assert_array_equal(t.scale_v[0, :, 0].cpu().numpy(), scale_v)
     # reconstruction error of the stored block vs the oracle on the same sketches
     Kr, Vr = cache.get_kv()
     for X, Xr, om, k in ((K, Kr, om_k, 16), (V, Vr, om_v, 32)):

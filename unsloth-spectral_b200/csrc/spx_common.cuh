@@ -52,6 +52,16 @@ __device__ __forceinline__ __half from_f<__half>(float x) { return __float2half_
 template <>
 __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
 
+// Byte offset of the value code (rank r, token t) inside one block stored in the
+// value-tile layout: 16-token tiles, each an [R][16] byte matrix whose row index is XORed
+// with (tile & 7) and whose 16 tokens are stored in the order 0,1,8,9,2,3,10,11,4,5,12,13,
+// 6,7,14,15.  R must be a multiple of 8 and the block length a multiple of 16.
+__host__ __device__ __forceinline__ int vtile_offset(int r, int t, int R) {
+  const int tt = t >> 4, x = t & 15;
+  const int pos = 4 * ((x & 7) >> 1) + (x & 1) + 2 * (x >> 3);
+  return (tt * R + (r ^ (tt & 7))) * 16 + pos;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -119,7 +119,7 @@ __global__ void __launch_bounds__(256) cold_generic_kernel(DecodeParams p) {
   for (int pr = warp; pr < nrep * RV; pr += nwarps) {
     const int h = pr / RV, r = pr - h * RV;
     float acc = 0.f;
-    for (int t = lane; t < Tb; t += 32) acc = fmaf(ssc[h * Tb + t], (float)cvb[(int64_t)r * Tb + t], acc);
+    for (int t = lane; t < Tb; t += 32) acc = fmaf(ssc[h * Tb + t], (float)cvb[vtile_offset(r, t, RV)], acc);
     acc = warp_sum(acc);
     if (lane == 0) svl[pr] = acc;
   }

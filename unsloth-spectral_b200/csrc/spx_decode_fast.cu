@@ -7,7 +7,7 @@
 // rows with tcgen05.st and reads them back per unit with tcgen05.ld of the same shape).
 //
 // Per unit the CTA streams, through a 3-stage TMA bulk-copy + mbarrier pipeline:
-//   INT8 key codes [T][RK] (token-major), INT8 value codes [RV][T] (rank-major),
+//   INT8 key codes [T][RK] (token-major), INT8 value codes (value-tile layout),
 //   FP16 bases [RK][128] and [RV][128], and the unit's query rows (n_rep x 128 FP16).
 // A conversion pass turns the key codes into FP16 UMMA operand tiles (K-major, no
 // swizzle) and the key basis into the MN-major operand; one thread then issues
@@ -20,8 +20,8 @@
 // Warps combine (m, l, v_lat) in shared memory; v_lat is expanded once through B_V and
 // written as the unit's partial (m, l, o[128]) for the hot-tier/merge kernel.
 //
-// Value codes are stored in shared memory with the 16 tokens of each tile reordered
-// (0,1,8,9, 2,3,10,11, ...) so that one ldmatrix per 16 tokens yields mma.sync A
+// Value codes arrive in the value-tile layout (16-token tiles, XOR-swizzled rows, tokens
+// ordered 0,1,8,9, 2,3,10,11, ...), so one ldmatrix per 16 tokens yields mma.sync A
 // fragments directly.
 #include <math.h>
 
@@ -368,20 +368,9 @@ __global__ void __launch_bounds__(NW * 32, 1) cold_fast_kernel(DecodeParams p, i
         const int k = e % RK, nc = e / RK;
         reinterpret_cast<uint4*>(sB)[nc * RK + k] = srcb[k * 16 + nc];
       }
-      // value codes [RV][T] -> [T/16][RV][16 tokens], row index XOR (tile & 7); the
-      // tokens of a row are reordered (0,1,8,9, 2,3,10,11, 4,5,12,13, 6,7,14,15) so that
-      // word t of an ldmatrix row holds tokens 2t, 2t+1, 2t+8, 2t+9
+      // value codes are stored in the value-tile layout the ldmatrix below reads
       const uint4* srcv = reinterpret_cast<const uint4*>(st + C::CK);
-      for (int e = tid; e < C::CV / 16; e += C::NT) {
-        const int r = e / (C::TB / 16), tt = e % (C::TB / 16);
-        const uint4 v = srcv[e];
-        uint4 o;
-        o.x = __byte_perm(v.x, v.z, 0x5410);
-        o.y = __byte_perm(v.x, v.z, 0x7632);
-        o.z = __byte_perm(v.y, v.w, 0x5410);
-        o.w = __byte_perm(v.y, v.w, 0x7632);
-        reinterpret_cast<uint4*>(cV)[tt * RV + (r ^ (tt & 7))] = o;
-      }
+      for (int e = tid; e < C::CV / 16; e += C::NT) reinterpret_cast<uint4*>(cV)[e] = srcv[e];
       // value basis [RV][128] -> chunk index XOR (rank & 7) (conflict-free ldmatrix)
       const uint4* srcbv = reinterpret_cast<const uint4*>(st + C::CK + C::CV + C::BK);
       for (int e = tid; e < RV * 16; e += C::NT) {

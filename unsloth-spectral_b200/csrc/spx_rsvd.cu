@@ -349,10 +349,13 @@ __global__ void __launch_bounds__(256) lift_quant_kernel(LiftParams p) {
     int8_t* ci = p.codes + (int64_t)i * p.codes_mat_stride;
     for (int e = threadIdx.x; e < m * kp; e += blockDim.x) {
       int t, j;
-      if (p.codes_j_stride == 1) { t = e / kp; j = e - t * kp; }   // walk the contiguous index fastest
+      if (p.codes_j_stride == 1 || p.codes_tiled) { t = e / kp; j = e - t * kp; }
       else { j = e / m; t = e - j * m; }
       const int8_t v = j < k ? (int8_t)(int)rintf(__fdiv_rn(sc[t * k + j], scale)) : (int8_t)0;
-      ci[(int64_t)t * p.codes_t_stride + (int64_t)j * p.codes_j_stride] = v;
+      if (p.codes_tiled)
+        ci[vtile_offset(j, t, kp)] = v;
+      else
+        ci[(int64_t)t * p.codes_t_stride + (int64_t)j * p.codes_j_stride] = v;
     }
   }
   if (p.S && threadIdx.x < k) p.S[(int64_t)i * k + threadIdx.x] = ss[threadIdx.x];
@@ -416,8 +419,11 @@ static int validate(const spx_rsvd_args* a) {
   if (a->codes) {
     SPX_REQUIRE(a->qscale, SPX_ERR_NULL, "qscale is required with codes");
     SPX_REQUIRE(a->codes_rank_pad >= a->k, SPX_ERR_SHAPE, "codes_rank_pad < k");
-    SPX_REQUIRE(a->codes_j_stride == 1 || a->codes_t_stride == 1, SPX_ERR_SHAPE,
-                "codes must be token-major or rank-major");
+    SPX_REQUIRE(a->codes_tiled || a->codes_j_stride == 1 || a->codes_t_stride == 1, SPX_ERR_SHAPE,
+                "codes must be token-major, rank-major or tiled");
+    if (a->codes_tiled)
+      SPX_REQUIRE(a->m % 16 == 0 && a->codes_rank_pad % 8 == 0, SPX_ERR_SHAPE,
+                  "tiled codes need m %% 16 == 0 and codes_rank_pad %% 8 == 0");
   }
   if (a->basis) {
     SPX_REQUIRE(dtype_ok(a->basis_dtype), SPX_ERR_UNSUPPORTED, "bad basis dtype");
@@ -463,6 +469,7 @@ static int run_chain(const spx_rsvd_args* a, const RsvdWs& w, cudaStream_t st) {
   lp.codes_mat_stride = a->codes_mat_stride;
   lp.codes_t_stride = a->codes_t_stride;
   lp.codes_j_stride = a->codes_j_stride;
+  lp.codes_tiled = a->codes_tiled;
   lp.rank_pad = a->codes_rank_pad > k ? a->codes_rank_pad : k;
   lp.qscale = a->qscale; lp.scale_mat_stride = a->scale_mat_stride;
   lp.qminmax = a->qminmax; lp.minmax_mat_stride = a->minmax_mat_stride;

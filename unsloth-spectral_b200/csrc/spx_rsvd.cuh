@@ -15,6 +15,7 @@ struct LiftParams {
   float* Vh;
   int8_t* codes;
   int64_t codes_mat_stride, codes_t_stride, codes_j_stride;
+  int codes_tiled;
   float* qscale;
   int64_t scale_mat_stride;
   float* qminmax;

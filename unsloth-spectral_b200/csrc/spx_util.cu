@@ -96,7 +96,7 @@ __global__ void reconstruct_kernel(spx_reconstruct_args a) {
     const int t = e / D, d = e - t * D;
     float acc = 0.f;
     for (int r = 0; r < R; ++r) {
-      const int8_t c = a.rank_major ? codes[(int64_t)r * Tb + t] : codes[(int64_t)t * R + r];
+      const int8_t c = a.rank_major ? codes[vtile_offset(r, t, R)] : codes[(int64_t)t * R + r];
       acc = fmaf((float)c, sm_basis[r * D + d], acc);
     }
     out[(int64_t)t * D + d] = from_f<T>(acc * sc);
@@ -223,6 +223,8 @@ int spx_reconstruct(const spx_reconstruct_args* a, void* stream) {
                   a->num_blocks >= 0 && a->num_blocks <= a->block_capacity && a->batch > 0 && a->num_kv_heads > 0 &&
                   a->out_tokens >= a->num_blocks * a->block_size,
               SPX_ERR_SHAPE, "bad reconstruct shape");
+  SPX_REQUIRE(!a->rank_major || (a->rank % 8 == 0 && a->block_size % 16 == 0), SPX_ERR_SHAPE,
+              "value-tile codes need rank %% 8 == 0 and block_size %% 16 == 0");
   if (a->num_blocks == 0) return SPX_OK;
   dim3 grid(a->num_blocks, a->num_kv_heads, a->batch);
   const size_t smem = (size_t)a->rank * a->head_dim * sizeof(float);

@@ -50,7 +50,8 @@ class RsvdArgs(C.Structure):
     _fields_ = [(n, C.c_int32) for n in ("num_mats", "m", "n", "k", "r", "n_iter", "in_dtype")] + [
         ("M", C.c_void_p), ("omega", C.c_void_p), ("U", C.c_void_p), ("S", C.c_void_p), ("Vh", C.c_void_p),
         ("M_mat_stride", C.c_int64), ("codes", C.c_void_p), ("codes_mat_stride", C.c_int64), ("codes_t_stride", C.c_int64),
-        ("codes_j_stride", C.c_int64), ("codes_rank_pad", C.c_int32), ("qscale", C.c_void_p),
+        ("codes_j_stride", C.c_int64), ("codes_rank_pad", C.c_int32), ("codes_tiled", C.c_int32),
+        ("qscale", C.c_void_p),
         ("scale_mat_stride", C.c_int64), ("qminmax", C.c_void_p), ("minmax_mat_stride", C.c_int64),
         ("basis", C.c_void_p), ("basis_dtype", C.c_int32), ("basis_mat_stride", C.c_int64),
         ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t)]

@@ -16,6 +16,29 @@ def _key(t: torch.Tensor):
     return (t.data_ptr(), tuple(t.shape), tuple(t.stride()), t.dtype, t._version)
 
 
+_vtile_cache = {}
+
+
+def vtile_index(T: int, R: int, device) -> torch.Tensor:
+    """``idx`` with ``stored[..., p] = natural[..., idx[p]]`` for one block of value codes:
+    natural = rank-major ``[R][T]`` flattened, stored = the value-tile layout of
+    ``include/spx.h`` (16-token tiles of ``[R][16]`` bytes, rows XOR (tile & 7), tokens
+    ordered 0,1,8,9,2,3,10,11,...)."""
+    key = (T, R, str(device))
+    idx = _vtile_cache.get(key)
+    if idx is None:
+        r = torch.arange(R).view(R, 1).expand(R, T)
+        t = torch.arange(T).view(1, T).expand(R, T)
+        tt, x = t // 16, t % 16
+        pos = 4 * ((x % 8) // 2) + (x % 2) + 2 * (x // 8)
+        stored = (tt * R + (r ^ (tt % 8))) * 16 + pos
+        idx = torch.empty(R * T, dtype=torch.long)
+        idx[stored.reshape(-1)] = (r * T + t).reshape(-1)
+        idx = idx.to(device)
+        _vtile_cache[key] = idx
+    return idx
+
+
 def rope_table_f32(t: torch.Tensor, device) -> torch.Tensor:
     """``t`` as a contiguous float32 ``[rope_len, D]`` table on ``device``."""
     if t.dim() == 3 and t.shape[0] == 1:
@@ -61,7 +84,7 @@ def rsvd(M: torch.Tensor, omega: torch.Tensor, k: int, n_iter: int, *, want_fact
          qscale: Optional[torch.Tensor] = None, scale_stride: int = 1, qminmax: Optional[torch.Tensor] = None,
          minmax_stride: int = 2, basis: Optional[torch.Tensor] = None, basis_stride: int = 0,
          M_mat_stride: int = 0, num_mats: Optional[int] = None, m: Optional[int] = None,
-         n: Optional[int] = None):
+         n: Optional[int] = None, codes_tiled: bool = False):
     """Run ``spx_rsvd_compress``.  ``M`` is ``[Nb, m, n]`` (or a strided view described by
     ``num_mats``/``m``/``n``/``M_mat_stride``); ``omega`` is ``[Nb, n, r]`` float32.
     Returns (U, S, Vh) float32 when ``want_factors``; compressed outputs are written in
@@ -81,7 +104,8 @@ def rsvd(M: torch.Tensor, omega: torch.Tensor, k: int, n_iter: int, *, want_fact
     a = N.RsvdArgs(num_mats=num_mats, m=m, n=n, k=k, r=r, n_iter=n_iter, in_dtype=N.dtype_code(M.dtype),
                    M=N.ptr(M), omega=N.ptr(omega), U=N.ptr(U), S=N.ptr(S), Vh=N.ptr(Vh),
                    M_mat_stride=M_mat_stride, codes=N.ptr(codes), codes_mat_stride=cs[0], codes_t_stride=cs[1],
-                   codes_j_stride=cs[2], codes_rank_pad=rank_pad or k, qscale=N.ptr(qscale),
+                   codes_j_stride=cs[2], codes_rank_pad=rank_pad or k, codes_tiled=int(bool(codes_tiled)),
+                   qscale=N.ptr(qscale),
                    scale_mat_stride=scale_stride, qminmax=N.ptr(qminmax), minmax_mat_stride=minmax_stride,
                    basis=N.ptr(basis), basis_dtype=N.dtype_code(basis.dtype) if basis is not None else 0,
                    basis_mat_stride=basis_stride)

@@ -5,8 +5,8 @@ Same constructor, attributes and methods as the reference's ``SpectralCache``
 
 * hot tier: preallocated ``[B, H, HC, D]`` K/V buffers in the cache dtype plus an int64
   position buffer; ``append`` copies into them (no ``torch.cat`` reallocation);
-* cold tier: preallocated INT8 codes (keys token-major ``[B, H, NBc, T, RK]``, values
-  rank-major ``[B, H, NBc, RV, T]``), one float32 scale and (min, max) per
+* cold tier: preallocated INT8 codes (keys token-major ``[B, H, NBc, T, RK]``, values in
+  the value-tile layout ``[B, H, NBc, RV*T]`` of ``include/spx.h``), one float32 scale and (min, max) per
   (sequence, head, block), bases ``[B, H, NBc, R, D]`` in the cache dtype, and the
   blocks' start positions.  Stored ranks are padded to multiples of 16 with zeros;
 * compression runs the batched rSVD + INT8 kernels of ``libspx`` and writes straight
@@ -71,7 +71,7 @@ class DeviceTiers:
         dev, dt = self.device, self.dtype
         new = dict(
             codes_k=torch.zeros(B, H, cap, T, self.rank_k_pad, dtype=torch.int8, device=dev),
-            codes_v=torch.zeros(B, H, cap, self.rank_v_pad, T, dtype=torch.int8, device=dev),
+            codes_v=torch.zeros(B, H, cap, self.rank_v_pad * T, dtype=torch.int8, device=dev),
             scale_k=torch.zeros(B, H, cap, dtype=torch.float32, device=dev),
             scale_v=torch.zeros(B, H, cap, dtype=torch.float32, device=dev),
             minmax_k=torch.zeros(B, H, cap, 2, dtype=torch.float32, device=dev),
@@ -267,7 +267,7 @@ class SpectralCache:
             basis, scale, mm = t.basis_k, t.scale_k, t.minmax_k
         else:
             codes, kp = t.codes_v, t.rank_v_pad
-            cstr = (t.block_capacity * kp * T, 1, T)      # rank-major
+            cstr = (t.block_capacity * kp * T, 0, 0)      # value-tile layout
             basis, scale, mm = t.basis_v, t.scale_v, t.minmax_v
         if r >= min(T, D) - 1:
             raise ValueError(f"rank {k} + oversampling {self.oversampling} too large for {T}x{D} blocks")
@@ -276,7 +276,7 @@ class SpectralCache:
                   qscale=scale[:, :, j], scale_stride=t.block_capacity,
                   qminmax=mm[:, :, j], minmax_stride=2 * t.block_capacity,
                   basis=basis[:, :, j], basis_stride=t.block_capacity * kp * D,
-                  M_mat_stride=HC * D, num_mats=nm, m=T, n=D)
+                  M_mat_stride=HC * D, num_mats=nm, m=T, n=D, codes_tiled=not keys)
 
     # -- reference-layout views -------------------------------------------------------
     @property
@@ -328,7 +328,9 @@ class SpectralCache:
         t.basis_k.zero_()
         t.basis_v.zero_()
         t.codes_k[:, :, :nb, :, :kK] = codes_K
-        t.codes_v[:, :, :nb, :kV, :] = codes_V.transpose(-1, -2)
+        nat = torch.zeros(B, H, nb, t.rank_v_pad, T, dtype=torch.int8, device=t.device)
+        nat[:, :, :, :kV, :] = codes_V.transpose(-1, -2)
+        t.codes_v[:, :, :nb] = nat.reshape(B, H, nb, -1)[..., _ops.vtile_index(T, t.rank_v_pad, t.device)]
         t.scale_k[:, :, :nb] = scale_K
         t.scale_v[:, :, :nb] = scale_V
         t.basis_k[:, :, :nb, :kK] = basis_K.to(self.dtype)
@@ -382,7 +384,10 @@ class SpectralCache:
             kK, kV = self.k_rank_keys, self.k_rank_values
             for j in range(t.num_blocks):
                 ck = (t.codes_k[:, :, j, :, :kK].float() * t.scale_k[:, :, j, None, None]).to(self.dtype)
-                cv = (t.codes_v[:, :, j, :kV, :].transpose(-1, -2).float()
+                nat = torch.empty_like(t.codes_v[:, :, j])
+                nat[..., _ops.vtile_index(self.block_size, t.rank_v_pad, t.device)] = t.codes_v[:, :, j]
+                nat = nat.view(t.batch, t.num_heads, t.rank_v_pad, self.block_size)
+                cv = (nat[:, :, :kV, :].transpose(-1, -2).float()
                       * t.scale_v[:, :, j, None, None]).to(self.dtype)
                 bk = t.basis_k[:, :, j, :kK]
                 bv = t.basis_v[:, :, j, :kV]
