@@ -97,7 +97,8 @@ def test_decode_host_validation_without_gpu():
     a = _decode_args(num_blocks=2, codes_k=32, codes_v=32, scale_k=32, scale_v=32, basis_k=32, basis_v=32,
                      block_pos=32, workspace=256, workspace_bytes=8)
     assert lib.spx_decode_attn(a, None) == 5
-    assert lib.spx_decode_workspace_size(a) == 256 + 1 * 1 * 8 * 2 * 4 * (128 + 4) * 4
+    # header + partial records [units][blocks][heads][D + 4] + packed RoPE words [blocks][T][64]
+    assert lib.spx_decode_workspace_size(a) == 256 + 1 * 1 * 8 * 2 * 4 * (128 + 4) * 4 + 2 * 512 * 256
     assert b"workspace" in lib.spx_last_error()
 
 

@@ -142,13 +142,13 @@ template <typename T>
 __global__ void __launch_bounds__(256) hot_merge_kernel(DecodeParams p) {
   const int g = blockIdx.x, lb = blockIdx.y;
   const int b = lb % p.B;
-  const int D = p.D, half = D / 2, nrep = p.nrep, hot = p.hot, nb = p.nblk;
+  const int D = p.D, half = D / 2, nrep = p.nrep, hot = p.hot, nb = p.nblk, nc = p.ncold;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   extern __shared__ float sm[];
   float* sq = sm;                   // [nrep][D]
   float* ssc = sq + nrep * D;       // [nrep][hot]
   float* sml = ssc + nrep * hot;    // [nrep][2]
-  float* swt = sml + 2 * nrep;      // [nrep][nb + 1] merge weights, then 1/L
+  float* swt = sml + 2 * nrep;      // [nrep][nc + 1] merge weights, then 1/L
   const int64_t lbg = (int64_t)lb * p.H + g;
   const T* q = reinterpret_cast<const T*>(p.q) + ((int64_t)lb * p.Hq + (int64_t)g * nrep) * D;
   for (int i = tid; i < nrep * D; i += blockDim.x) sq[i] = to_f(q[i]);
@@ -203,13 +203,13 @@ __global__ void __launch_bounds__(256) hot_merge_kernel(DecodeParams p) {
     // merge weights over the cold partials and the hot partial
     const float* recs = p.ws + (lbg * p.nparts) * nrep * (int64_t)(D + 4);
     float M = m;
-    for (int jj = lane; jj < nb; jj += 32) M = fmaxf(M, recs[((int64_t)jj * nrep + h) * (D + 4)]);
+    for (int jj = lane; jj < nc; jj += 32) M = fmaxf(M, recs[((int64_t)jj * nrep + h) * (D + 4)]);
     M = warp_max(M);
     float L = 0.f;
-    for (int jj = lane; jj < nb; jj += 32) {
+    for (int jj = lane; jj < nc; jj += 32) {
       const float* r = recs + ((int64_t)jj * nrep + h) * (D + 4);
       const float w = M == -INFINITY ? 0.f : __expf(r[0] - M);
-      swt[h * (nb + 1) + jj] = w;
+      swt[h * (nc + 1) + jj] = w;
       L += w * r[1];
     }
     L = warp_sum(L);
@@ -228,7 +228,7 @@ __global__ void __launch_bounds__(256) hot_merge_kernel(DecodeParams p) {
     float acc = 0.f;
     for (int t = 0; t < hot; ++t) acc = fmaf(ssc[h * hot + t], to_f(hv[(int64_t)t * D + d]), acc);
     acc *= sml[2 * h];
-    for (int jj = 0; jj < nb; ++jj) acc = fmaf(swt[h * (nb + 1) + jj], recs[((int64_t)jj * nrep + h) * (D + 4) + 4 + d], acc);
+    for (int jj = 0; jj < nc; ++jj) acc = fmaf(swt[h * (nc + 1) + jj], recs[((int64_t)jj * nrep + h) * (D + 4) + 4 + d], acc);
     out[(int64_t)h * D + d] = from_f<T>(cold_failed ? NAN : acc * sml[2 * h + 1]);
   }
 }
@@ -268,6 +268,15 @@ static int launch_hot_merge(const DecodeParams& p, cudaStream_t st) {
 }
 
 // ------------------------------------------------------------------- host side ---
+static size_t partial_bytes(const DecodeParams& p) {
+  return (size_t)p.L * p.B * p.H * p.nparts * p.nrep * (p.D + 4) * sizeof(float);
+}
+
+void decode_set_workspace(DecodeParams* p, void* base) {
+  p->ws = base ? reinterpret_cast<float*>(reinterpret_cast<char*>(base) + kWsHeader) : nullptr;
+  p->rope = base ? reinterpret_cast<char*>(base) + kWsHeader + partial_bytes(*p) : nullptr;
+}
+
 static int make_params(const spx_decode_args* a, DecodeParams* p) {
   SPX_REQUIRE(a, SPX_ERR_NULL, "args is NULL");
   SPX_REQUIRE(a->num_layers >= 1 && a->batch >= 1 && a->num_kv_heads >= 1 && a->num_q_heads >= 1,
@@ -320,6 +329,7 @@ static int make_params(const spx_decode_args* a, DecodeParams* p) {
   p->rope_len = a->rope_len;
   p->mask_stride = a->mask_stride;
   p->nparts = a->num_blocks > 0 ? a->num_blocks : 1;
+  p->ncold = a->num_blocks;
   p->qpos = a->query_position;
   p->scale = a->scale;
   p->q = a->q;
@@ -337,12 +347,12 @@ static int make_params(const spx_decode_args* a, DecodeParams* p) {
   p->sinT = a->sin_table;
   p->mask = a->mask;
   p->out = a->out;
-  p->ws = a->workspace ? reinterpret_cast<float*>(reinterpret_cast<char*>(a->workspace) + kWsHeader) : nullptr;
+  decode_set_workspace(p, a->workspace);
   return SPX_OK;
 }
 
 size_t decode_workspace_bytes(const DecodeParams& p) {
-  return kWsHeader + (size_t)p.L * p.B * p.H * p.nparts * p.nrep * (p.D + 4) * sizeof(float);
+  return kWsHeader + partial_bytes(p) + (size_t)p.nblk * p.Tb * 256;
 }
 
 // SPX_DECODE_PATH=generic forces the generic cold-tier kernel (used to cross-check the
@@ -353,15 +363,20 @@ static bool force_generic() {
   return e && strcmp(e, "generic") == 0;
 }
 
-int decode_dispatch(const DecodeParams& p, cudaStream_t st) {
+int decode_dispatch(const DecodeParams& p0, cudaStream_t st) {
+  DecodeParams p = p0;
   int rc = SPX_OK;
   if (p.nblk > 0) {
+    SPX_REQUIRE(p.ws && p.rope, SPX_ERR_WORKSPACE, "decode workspace pointers are not set");
     const cudaError_t e = cudaMemsetAsync(reinterpret_cast<char*>(p.ws) - kWsHeader, 0, sizeof(int), st);
     SPX_REQUIRE(e == cudaSuccess, SPX_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
-    if (!force_generic() && decode_fast_supported(p))
+    if (!force_generic() && decode_fast_supported(p)) {
+      p.ncold = decode_fast_ncold(p);
       rc = decode_fast_cold(p, st);
-    else
+    } else {
+      p.ncold = p.nblk;
       rc = SPX_DISPATCH_DTYPE(p.dtype, T, [&] { return launch_cold<T>(p, st); });
+    }
     if (rc != SPX_OK) return rc;
   }
   return SPX_DISPATCH_DTYPE(p.dtype, T, [&] { return launch_hot_merge<T>(p, st); });

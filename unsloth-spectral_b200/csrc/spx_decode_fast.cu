@@ -1,28 +1,31 @@
-// Fast cold-tier decode kernel for sm_100a (FP16 cache, D = 128, tied RoPE tables).
+// Fast cold-tier decode kernel for sm_100a (FP16 cache, D = 128, tied or distance RoPE).
 //
-// Work item: one CTA per (cold block j, chunk of units), a unit being one (layer,
-// sequence, KV head).  Every unit of the chunk shares block j's token positions, so the
-// block's RoPE rows are read once per CTA and parked in tensor memory (TMEM columns
-// 0..255, used as an extension of the register file: each warp writes its own tokens'
-// rows with tcgen05.st and reads them back per unit with tcgen05.ld of the same shape).
+// Work decomposition.  A unit is one (layer, sequence, KV head); a unit-block is one unit
+// restricted to one cold block j.  The launch covers items = (group of G units) x (range
+// of JR blocks); a persistent CTA per SM walks its items block-major (for j in range:
+// for u in group), so block j's RoPE rows are parked in tensor memory once per j and the
+// unit's softmax state (m, l, o) is merged across the j of the range inside the CTA: one
+// partial record per (unit, range) is written for the hot-tier/merge kernel.
 //
-// Per unit the CTA streams, through a 3-stage TMA bulk-copy + mbarrier pipeline:
-//   INT8 key codes [T][RK] (token-major), INT8 value codes (value-tile layout),
-//   FP16 bases [RK][128] and [RV][128], and the unit's query rows (n_rep x 128 FP16).
-// A conversion pass turns the key codes into FP16 UMMA operand tiles (K-major, no
-// swizzle) and the key basis into the MN-major operand; one thread then issues
-//   tcgen05.mma kind::f16  M=128 tokens x N=128 dims x K=16   (K~ = codes_K @ B_K)
-// into one of two TMEM accumulators (columns 256..511), per 128-token M-tile.  Warps
-// read K~ back with tcgen05.ld.16x256b, which lands in the mma.sync fragment layout:
-//   rotate K~ by the token's RoPE row in packed f16x2   -> A fragment
-//   scores = rot(K~) . Q          (mma.sync m16n8k16)   -> online softmax (exp2)
-//   v_lat += codes_V^T . P        (mma.sync m16n8k16)   -> [RV x heads]
-// Warps combine (m, l, v_lat) in shared memory; v_lat is expanded once through B_V and
-// written as the unit's partial (m, l, o[128]) for the hot-tier/merge kernel.
-//
-// Value codes arrive in the value-tile layout (16-token tiles, XOR-swizzled rows, tokens
-// ordered 0,1,8,9, 2,3,10,11, ...), so one ldmatrix per 16 tokens yields mma.sync A
-// fragments directly.
+// Warp roles (4 warpgroups, 512 threads, one CTA per SM; registers rebalanced with
+// setmaxnreg: 160 for the consumers, 96 for the others):
+//   warpgroup 2  converters: ring A (INT8 key codes [T][RK], FP16 key basis [RK][128],
+//                bulk-copied 3 stages ahead by thread 256) -> FP16 UMMA A tiles
+//                (K-major, no swizzle) and the MN-major B tile; thread 256 issues
+//                  tcgen05.mma kind::f16  M=128 tokens x N=128 dims x K=16, D = f16
+//                (K~ = codes_K @ B_K) into one of two TMEM accumulators per M-tile.
+//   warpgroups 0-1  consumers, two warps per TMEM lane quadrant, 16 tokens of each
+//                M-tile: K~ via tcgen05.ld 16x256b.pack::16b (already f16 pairs; the next
+//                M-tile loads while this one computes), RoPE rows via tcgen05.ld 16x256b,
+//                rotate in f16x2, scores = rot(K~) . Q (mma.sync m16n8k16), softmax
+//                (exp2), v_lat += codes_V^T P (mma.sync) with the value codes of ring B
+//                (value-tile layout); each warp hands (m, l, v_lat) to the epilogue.
+//   warpgroup 3  epilogue: combines the 8 warps, expands v_lat once through B_V, merges
+//                into the unit's running (m, l, o); thread 384 bulk-copies ring B (value
+//                codes, value basis, query rows at a padded pitch) 3 stages ahead.
+// Every wait is bounded in time; a wait that expires raises the CTA's abort flag and the
+// workspace error word, after which all waits return at once and no new copies or MMAs
+// are issued, so every role still reaches each named barrier and the CTA exits.
 #include <math.h>
 
 #include "spx_common.cuh"
@@ -33,12 +36,31 @@ namespace fastk {
 
 constexpr int FD = 128;
 constexpr int STAGES = 3;
+constexpr int NA = 3;                      // A-tile slots (one M-tile each)
+constexpr int NCW = 8;                     // consumer warps (warpgroups 0, 1)
+constexpr int NPW = 4;                     // converter warps (warpgroup 2)
+constexpr int NEW = 4;                     // epilogue warps (warpgroup 3)
+constexpr int NT = (NCW + NPW + NEW) * 32;
+constexpr int PT0 = NCW * 32;              // first converter thread
+constexpr int NPT = NPW * 32;
+constexpr int ET0 = (NCW + NPW) * 32;      // first epilogue thread
+constexpr int NEP = NEW * 32;
+constexpr int GMAX = 32;                   // units per item at most
+constexpr int BAR_CONV = 2, BAR_EPI = 3;   // named barriers
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LN2 = 0.6931471805599453f;
-constexpr unsigned kWaitLimit = 1u << 22;
+constexpr uint64_t kWaitNs = 2000000000ull;   // 2 s
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void named_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
 // ------------------------------------------------------------------ mbarrier / TMA --
@@ -47,6 +69,9 @@ __device__ __forceinline__ void mbar_init(uint32_t a, uint32_t cnt) {
 }
 __device__ __forceinline__ void mbar_expect_tx(uint32_t a, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t a) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(a) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait(uint32_t a, uint32_t parity) {
   uint32_t ok;
@@ -59,16 +84,77 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t a, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait: false when the phase did not complete within the iteration limit.
-__device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity) {
-  for (unsigned it = 0; it < kWaitLimit; ++it)
-    if (mbar_try_wait(a, parity)) return true;
-  return false;
-}
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
                "l"(src), "r"(bytes), "r"(bar)
                : "memory");
+}
+
+// Streaming copies are marked evict-first in L2 so that the data reused across CTAs
+// (query rows, packed RoPE words, partial records) stays resident.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ void bulk_g2s_hint(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
+                                              uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar), "l"(pol)
+      : "memory");
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+struct Abort {
+  volatile int* flag;   // shared: set once any wait of the CTA expired
+  int* err;             // workspace error word
+};
+
+// Single-thread bounded wait.  Returns false when aborted (now or earlier).
+__device__ __forceinline__ bool wait1(uint32_t bar, uint32_t parity, const Abort& ab) {
+  if (mbar_try_wait(bar, parity)) return true;
+  if (*ab.flag) return false;
+  const uint64_t t0 = gtimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 15u) == 0) {
+      if (*ab.flag) return false;
+      if (gtimer() - t0 > kWaitNs) {
+        *ab.flag = 1;
+        atomicExch(ab.err, 1);
+        return false;
+      }
+    }
+  }
+}
+// Warp-wide bounded wait with a warp-uniform result (all 32 lanes call it).
+__device__ __forceinline__ bool waitw(uint32_t bar, uint32_t parity, const Abort& ab) {
+  int r = 0;
+  if ((threadIdx.x & 31) == 0) r = wait1(bar, parity, ab) ? 1 : 0;
+  r = __shfl_sync(0xffffffffu, r, 0);
+  if (r) {   // every lane observes the completed phase itself (acquire)
+    for (int k = 0; k < (1 << 20) && !mbar_try_wait(bar, parity); ++k) {
+    }
+  }
+  return r != 0;
+}
+
+// After an abort: let the copies of the last `issued` iterations of a ring land (bounded)
+// before the shared memory goes away.
+__device__ __forceinline__ void drain(uint32_t full0, int issued) {
+  for (int k = (issued > STAGES ? issued - STAGES : 0); k < issued; ++k) {
+    const uint64_t t0 = gtimer();
+    while (!mbar_try_wait(full0 + 8 * (k % STAGES), (uint32_t)((k / STAGES) & 1)) && gtimer() - t0 < kWaitNs) {
+    }
+  }
 }
 
 // ------------------------------------------------------------------------- TMEM -----
@@ -84,21 +170,48 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tmem_st16x256_x2(uint32_t taddr, const uint32_t (&r)[8]) {
-  asm volatile("tcgen05.st.sync.aligned.16x256b.x2.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
-               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
-               : "memory");
-}
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-// Load + wait in one statement so no use of the registers can be scheduled early.
-__device__ __forceinline__ void tmem_ld16x256_x2(uint32_t taddr, uint32_t (&r)[8]) {
+
+#define SPX_R8(r, o) "=r"(r[o + 0]), "=r"(r[o + 1]), "=r"(r[o + 2]), "=r"(r[o + 3]), "=r"(r[o + 4]), "=r"(r[o + 5]), \
+                     "=r"(r[o + 6]), "=r"(r[o + 7])
+#define SPX_I8(r, o) "r"(r[o + 0]), "r"(r[o + 1]), "r"(r[o + 2]), "r"(r[o + 3]), "r"(r[o + 4]), "r"(r[o + 5]), \
+                     "r"(r[o + 6]), "r"(r[o + 7])
+
+// 32 registers of RoPE words (16x256b.x8, 64 columns) -> TMEM, then wait for the store.
+__device__ __forceinline__ void tmem_st_rope(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n\t"
-      "tcgen05.wait::ld.sync.aligned;"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-      : "r"(taddr)
+      "tcgen05.st.sync.aligned.16x256b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};\n\t"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+      SPX_I8(r, 0), SPX_I8(r, 8), SPX_I8(r, 16), SPX_I8(r, 24)
       : "memory");
 }
+// K~ (f16 accumulator, 128 columns, packed pairs) and the RoPE words (64 columns) of one
+// 16-lane slab, without the wait: the registers are valid only after tmem_wait_ld_64.
+__device__ __forceinline__ void tmem_ld_k_rope_nowait(uint32_t tk, uint32_t tr, uint32_t (&k)[32], uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x8.pack::16b.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+      "%13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%64];\n\t"
+      "tcgen05.ld.sync.aligned.16x256b.x8.b32 {%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, "
+      "%45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%65];"
+      : SPX_R8(k, 0), SPX_R8(k, 8), SPX_R8(k, 16), SPX_R8(k, 24), SPX_R8(r, 0), SPX_R8(r, 8), SPX_R8(r, 16),
+        SPX_R8(r, 24)
+      : "r"(tk), "r"(tr)
+      : "memory");
+}
+#define SPX_T8(r, o) "+r"(r[o + 0]), "+r"(r[o + 1]), "+r"(r[o + 2]), "+r"(r[o + 3]), "+r"(r[o + 4]), "+r"(r[o + 5]), \
+                     "+r"(r[o + 6]), "+r"(r[o + 7])
+// Wait for this thread's TMEM loads; the registers are tied to the wait so that no use
+// of them can be scheduled before it.
+__device__ __forceinline__ void tmem_wait_ld_64(uint32_t (&k)[32], uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : SPX_T8(k, 0), SPX_T8(k, 8), SPX_T8(k, 16), SPX_T8(k, 24), SPX_T8(r, 0), SPX_T8(r, 8), SPX_T8(r, 16),
+                 SPX_T8(r, 24)
+               :
+               : "memory");
+}
+#undef SPX_T8
+#undef SPX_R8
+#undef SPX_I8
 
 // ------------------------------------------------------------------- tcgen05.mma ----
 // Shared-memory matrix descriptor, no swizzle: start address, leading-dimension byte
@@ -107,8 +220,8 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint
   return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
          ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
 }
-// Instruction descriptor: D f32, A/B f16, A K-major, B MN-major, N = 128, M = 128.
-constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | (0u << 15) | (1u << 16) | ((128u >> 3) << 17) |
+// Instruction descriptor: D f16, A/B f16, A K-major, B MN-major, N = 128, M = 128.
+constexpr uint32_t kIdesc = (0u << 4) | (0u << 7) | (0u << 10) | (0u << 15) | (1u << 16) | ((128u >> 3) << 17) |
                             ((128u >> 4) << 24);
 __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
   asm volatile(
@@ -120,21 +233,6 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64
 }
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-// Three 16x256b.x2 loads (24 registers) issued without waiting.
-__device__ __forceinline__ void tmem_ld3(uint32_t ta, uint32_t tb, uint32_t tc, uint32_t (&r)[24]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%24];\n\t"
-      "tcgen05.ld.sync.aligned.16x256b.x2.b32 {%8, %9, %10, %11, %12, %13, %14, %15}, [%25];\n\t"
-      "tcgen05.ld.sync.aligned.16x256b.x2.b32 {%16, %17, %18, %19, %20, %21, %22, %23}, [%26];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23])
-      : "r"(ta), "r"(tb), "r"(tc)
-      : "memory");
-}
-// Wait for this thread's TMEM loads; the registers are tied to the wait so that no use
-// of them can be scheduled before it.
-__device__ __forceinline__ void tmem_wait_ld_tied(uint32_t (&r)[24]) {
-  asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]) :: "memory");
 }
 
 // ------------------------------------------------------------- warp MMA helpers -----
@@ -183,75 +281,103 @@ __device__ __forceinline__ void i8x4_to_h2(uint32_t w, uint32_t& lo, uint32_t& h
   hi = h2u(__hsub2(u2h(h), bias));
 }
 
-template <int RK, int RV, int NW>
+// ------------------------------------------------------------------ configuration ---
+template <int RK, int RV, int MT>
 struct Cfg {
-  static constexpr int NT = NW * 32;
-  static constexpr int TB = NW * 64;
-  static constexpr int MT = TB / 128;                   // 128-token UMMA M-tiles per unit
-  static constexpr int CK = TB * RK;
-  static constexpr int CV = RV * TB;
-  static constexpr int BK = RK * FD * 2;
-  static constexpr int BV = RV * FD * 2;
-  static constexpr int QB = 8 * FD * 2;
-  static constexpr int STAGE = CK + CV + BK + BV + QB;
-  static constexpr int ATILE = 128 * RK * 2;            // one M-tile of FP16 key codes
-  static constexpr int OFF_A = STAGES * STAGE;          // UMMA A tiles [MT][RK/8][16][8 rows][16 B]
-  static constexpr int OFF_B = OFF_A + MT * ATILE;      // UMMA B tile  [16 n-chunks][RK rows][16 B]
-  static constexpr int OFF_CV = OFF_B + BK;             // value codes [T/16][RV][16 B], XOR-swizzled rows
-  static constexpr int OFF_Q = OFF_CV + CV;             // query [8][16 chunks], XOR-swizzled chunks
-  static constexpr int OFF_BV = OFF_Q + QB;             // value basis [RV][16 chunks], XOR-swizzled
-  static constexpr int OFF_SM = OFF_BV + BV;            // per-warp m [NW][8]
-  static constexpr int OFF_SL = OFF_SM + NW * 8 * 4;    // per-warp l [NW][8]
-  static constexpr int OFF_SV = OFF_SL + NW * 8 * 4;    // per-warp v_lat [NW][RV][8]
-  static constexpr int OFF_VL = OFF_SV + NW * RV * 8 * 4;   // combined v_lat [8][RV]
-  static constexpr int OFF_ML = OFF_VL + 8 * RV * 4;    // combined (m, l) [8][2]
-  static constexpr int OFF_BAR = OFF_ML + 16 * 4;       // STAGES load barriers + 2 MMA barriers
-  static constexpr int OFF_TM = OFF_BAR + (STAGES + 2) * 8;
+  static constexpr int TB = MT * 128;                  // tokens per block
+  static constexpr int CK = TB * RK;                   // INT8 key codes
+  static constexpr int CV = RV * TB;                   // INT8 value codes (value-tile layout)
+  static constexpr int BK = RK * FD * 2;               // FP16 key basis
+  static constexpr int BV = RV * FD * 2;               // FP16 value basis
+  static constexpr int QP = FD * 2 + 16;               // padded query row pitch (conflict-free reads)
+  static constexpr int QB = 8 * QP;                    // query rows (up to 8 heads)
+  // ring A (keys: converters) and ring B (values, queries: consumers and epilogue)
+  static constexpr int A_CK = 0, A_BK = CK, STAGE_A = CK + BK;
+  static constexpr int B_CV = 0, B_BV = CV, B_Q = CV + BV, STAGE_B = B_Q + QB;
+  static constexpr int OFF_RA = 0;
+  static constexpr int OFF_RB = OFF_RA + STAGES * STAGE_A;
+  static constexpr int ATILE = 128 * RK * 2;           // one M-tile of FP16 key codes
+  static constexpr int OFF_A = OFF_RB + STAGES * STAGE_B;   // [NA] x [RK/8 chunks][16 groups][8 rows][16 B]
+  static constexpr int OFF_B = OFF_A + NA * ATILE;     // [2] x [16 n-chunks][RK rows][16 B]
+  // consumer -> epilogue partials, double-buffered: m [8][8], l [8][8], v_lat [8][RV][8]
+  static constexpr int PART = NCW * 8 * 4 * 2 + NCW * RV * 8 * 4;
+  static constexpr int OFF_P = OFF_B + 2 * BK;
+  static constexpr int OFF_BVP = OFF_P + 2 * PART;     // value basis, rows padded to QP bytes
+  static constexpr int OFF_VL = OFF_BVP + RV * QP;     // combined v_lat [8][RV]
+  static constexpr int OFF_ML = OFF_VL + 8 * RV * 4;   // per head (l_j, a_old, a_new, -) [8][4]
+  static constexpr int OFF_ST = OFF_ML + 8 * 4 * 4;    // running (m, l) per unit of the item [GMAX][8][2]
+  static constexpr int OFF_BAR = OFF_ST + GMAX * 8 * 2 * 4;
+  // barriers: fullA[S], fullB[S], aslot[NA], bslot[2], accf[2], acce[2], pready[2], pfree[2]
+  static constexpr int NBAR = 2 * STAGES + NA + 8;
+  static constexpr int OFF_TM = OFF_BAR + NBAR * 8;    // TMEM base address, abort flag
   static constexpr int BYTES = OFF_TM + 16;
-  static_assert(STAGE % 16 == 0 && OFF_BAR % 8 == 0 && OFF_A % 128 == 0, "alignment");
+  static_assert(STAGE_A % 128 == 0 && STAGE_B % 128 == 0 && OFF_A % 128 == 0 && OFF_BAR % 8 == 0, "alignment");
   static_assert(BYTES <= 227 * 1024, "shared memory");
 };
 
-template <int NW>
-struct Group {
-  int mt, lane_off, tcol;
-  __device__ __forceinline__ Group(int w, int i) {
-    if constexpr (NW == 8) {
-      mt = i;
-      lane_off = 32 * (w & 3) + 16 * (w >> 2);
-      tcol = 64 * i;
-    } else {
-      mt = i >> 1;
-      lane_off = 32 * w + 16 * (i & 1);
-      tcol = 64 * (i >> 1);
-    }
-  }
-  __device__ __forceinline__ int token0() const { return mt * 128 + lane_off; }
+// Launch-wide item geometry (kernel parameters, uniform across the CTA).
+struct Items {
+  int G, JR, ngroups, nitems, nblk, units;
 };
 
-template <int RK, int RV, int NW>
-__global__ void __launch_bounds__(NW * 32, 1) cold_fast_kernel(DecodeParams p, int units_per_cta) {
-  using C = Cfg<RK, RV, NW>;
-  static_assert(NW == 8 || NW == 4, "one or two warps per TMEM lane quadrant");
+// The CTA's walk over its items: for j in range: for u in group.
+struct Seq {
+  int x;          // item id
+  int j0, jn, u0, un;
+  int jj, uu;     // position inside the item
+  __device__ __forceinline__ void load_item(const Items& I) {
+    const int jr = x / I.ngroups, ug = x - jr * I.ngroups;
+    j0 = jr * I.JR;
+    jn = min(I.JR, I.nblk - j0);
+    u0 = ug * I.G;
+    un = min(I.G, I.units - u0);
+    jj = 0;
+    uu = 0;
+  }
+  __device__ __forceinline__ bool valid(const Items& I) const { return x < I.nitems; }
+  __device__ __forceinline__ void next(const Items& I) {
+    if (++uu < un) return;
+    uu = 0;
+    if (++jj < jn) return;
+    x += gridDim.x;
+    if (x < I.nitems) load_item(I);
+  }
+  __device__ __forceinline__ int j() const { return j0 + jj; }
+  __device__ __forceinline__ int unit() const { return u0 + uu; }
+};
+
+template <int RK, int RV, int MT>
+__global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items I) {
+  using C = Cfg<RK, RV, MT>;
   extern __shared__ __align__(1024) uint8_t sm[];
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
-  const int j = blockIdx.x;
-  const int units = p.L * p.B * p.H;
-  const int u0 = blockIdx.y * units_per_cta;
-  const int nu = min(units_per_cta, units - u0);
   const int nrep = p.nrep;
-  const uint32_t bar0 = smem_u32(sm + C::OFF_BAR);      // TMA stage barriers
-  const uint32_t mbar0 = bar0 + 8 * STAGES;              // MMA-done barriers, one per accumulator
+  const uint32_t bar0 = smem_u32(sm + C::OFF_BAR);
+  const uint32_t b_fullA = bar0, b_fullB = bar0 + 8 * STAGES, b_aslot = bar0 + 16 * STAGES;
+  const uint32_t b_bslot = b_aslot + 8 * NA, b_accf = b_bslot + 16, b_acce = b_accf + 16, b_pready = b_acce + 16,
+                 b_pfree = b_pready + 16;
   uint32_t* tm_slot = reinterpret_cast<uint32_t*>(sm + C::OFF_TM);
-  int* err = reinterpret_cast<int*>(p.ws) - 64;   // status word in the workspace header
+  Abort ab{reinterpret_cast<volatile int*>(sm + C::OFF_TM + 4), reinterpret_cast<int*>(p.ws) - 64};
 
   if (w == 0) {
     tmem_alloc(smem_u32(tm_slot), 512);
     tmem_relinquish();
   }
   if (tid == 0) {
-    for (int s = 0; s < STAGES + 2; ++s) mbar_init(bar0 + 8 * s, 1);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(b_fullA + 8 * s, 1);
+      mbar_init(b_fullB + 8 * s, 1);
+    }
+    for (int a = 0; a < NA; ++a) mbar_init(b_aslot + 8 * a, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(b_bslot + 8 * b, 1);
+      mbar_init(b_accf + 8 * b, 1);
+      mbar_init(b_acce + 8 * b, NCW);
+      mbar_init(b_pready + 8 * b, NCW);
+      mbar_init(b_pfree + 8 * b, 1);
+    }
+    *ab.flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   tc_fence_before();
@@ -259,375 +385,524 @@ __global__ void __launch_bounds__(NW * 32, 1) cold_fast_kernel(DecodeParams p, i
   tc_fence_after();
   const uint32_t tbase = *tm_slot;
 
-  auto issue = [&](int u) {  // one thread: TMA bulk loads of unit u into stage u % STAGES
-    const int s = u % STAGES;
-    const int64_t unit = u0 + u;
-    const int64_t slot = unit * p.NBc + j;
-    const int64_t lb = unit / p.H, gg = unit % p.H;
-    uint8_t* st = sm + s * C::STAGE;
-    const uint32_t bar = bar0 + 8 * s;
-    const uint32_t qbytes = nrep * FD * 2;
-    mbar_expect_tx(bar, C::CK + C::CV + C::BK + C::BV + qbytes);
-    bulk_g2s(smem_u32(st), p.ck + slot * C::CK, C::CK, bar);
-    bulk_g2s(smem_u32(st + C::CK), p.cv + slot * C::CV, C::CV, bar);
-    bulk_g2s(smem_u32(st + C::CK + C::CV), reinterpret_cast<const uint8_t*>(p.bk) + slot * C::BK, C::BK, bar);
-    bulk_g2s(smem_u32(st + C::CK + C::CV + C::BK), reinterpret_cast<const uint8_t*>(p.bv) + slot * C::BV, C::BV, bar);
-    bulk_g2s(smem_u32(st + C::CK + C::CV + C::BK + C::BV),
-             reinterpret_cast<const uint8_t*>(p.q) + ((lb * p.Hq) + gg * nrep) * FD * 2, qbytes, bar);
-  };
-  if (tid == 0) {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    for (int u = 0; u < min(STAGES, nu); ++u) issue(u);
-  }
+  Seq sq;
+  sq.x = blockIdx.x;
+  if (sq.valid(I)) sq.load_item(I);
+  const uint64_t stream_policy = l2_evict_first_policy();
 
-  // ---- RoPE rows of this warp's 64 tokens -> TMEM (f16 pairs), once per CTA ----------
-  const int64_t p0 = p.bpos[j];
-#pragma unroll 1
-  for (int i = 0; i < 4; ++i) {
-    const Group<NW> G(w, i);
-    int64_t a[2];
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const int64_t pos = p0 + G.token0() + g + 8 * hh;
-      int64_t aa = p.mode == SPX_ROPE_DISTANCE ? (p.qpos - pos > 0 ? p.qpos - pos : 0) : pos;
-      a[hh] = aa < 0 ? 0 : (aa >= p.rope_len ? p.rope_len - 1 : aa);
+  if (w >= NCW + NPW) {
+    // ============================================================== epilogue warps ===
+    // combine the consumer warps' partials, expand v_lat through B_V, merge into the
+    // unit's running (m, l, o); thread 384 also streams ring B (values, queries).
+    setmaxnreg_dec<96>();
+    const int et = tid - ET0, ew = et >> 5;
+    Seq sqB = sq;   // ring-B copies run STAGES iterations ahead
+    int issuedB = 0;
+    auto issueB = [&]() {
+      const int s = issuedB % STAGES;
+      const int64_t unit = sqB.unit();
+      const int64_t slot = unit * p.NBc + sqB.j();
+      const int64_t lb = unit / p.H, gg = unit % p.H;
+      uint8_t* st = sm + C::OFF_RB + s * C::STAGE_B;
+      const uint32_t bar = b_fullB + 8 * s;
+      mbar_expect_tx(bar, C::CV + C::BV + nrep * FD * 2);
+      bulk_g2s_hint(smem_u32(st + C::B_CV), p.cv + slot * C::CV, C::CV, bar, stream_policy);
+      bulk_g2s_hint(smem_u32(st + C::B_BV), reinterpret_cast<const uint8_t*>(p.bv) + slot * C::BV, C::BV, bar,
+                    stream_policy);
+      const uint8_t* q = reinterpret_cast<const uint8_t*>(p.q) + ((lb * p.Hq) + gg * nrep) * FD * 2;
+      for (int h = 0; h < nrep; ++h) bulk_g2s(smem_u32(st + C::B_Q + h * C::QP), q + h * FD * 2, FD * 2, bar);
+      ++issuedB;
+      sqB.next(I);
+    };
+    if (et == 0) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      for (int k = 0; k < STAGES && sqB.valid(I); ++k) issueB();
     }
-#pragma unroll 1
-    for (int s = 0; s < 4; ++s) {
-      uint32_t r[8];
+    float* sVL = reinterpret_cast<float*>(sm + C::OFF_VL);
+    float* sML = reinterpret_cast<float*>(sm + C::OFF_ML);
+    float* sST = reinterpret_cast<float*>(sm + C::OFF_ST);
+    const uint32_t bvp_u = smem_u32(sm + C::OFF_BVP);
+    const bool hl = g < nrep;
+    int it = 0;
+    for (; sq.valid(I); sq.next(I), ++it) {
+      const int s = it % STAGES, b2 = it & 1;
+      const uint8_t* st = sm + C::OFF_RB + s * C::STAGE_B;
+      const int64_t unit = sq.unit();
+      const bool first_j = sq.jj == 0, last_j = sq.jj == sq.jn - 1;
+      const float vscale = __ldg(p.sv + unit * p.NBc + sq.j());
+      float* rec = p.ws + (unit * p.nparts + (sq.j0 / I.JR)) * (int64_t)nrep * (FD + 4);
+      float2 oold[4];
 #pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        const int f = 8 * (2 * s + cc) + 2 * t;
+      for (int q = 0; q < 4; ++q) {
+        oold[q] = make_float2(0.f, 0.f);
+        if (!first_j && hl)
+          oold[q] = *reinterpret_cast<const float2*>(rec + g * (FD + 4) + 4 + 8 * (4 * ew + q) + 2 * t);
+      }
+      waitw(b_fullB + 8 * s, (uint32_t)((it / STAGES) & 1), ab);
+      waitw(b_pready + 8 * b2, (uint32_t)((it / 2) & 1), ab);
+      const float* sM = reinterpret_cast<const float*>(sm + C::OFF_P + b2 * C::PART);
+      const float* sL = sM + NCW * 8;
+      const float* sV = sL + NCW * 8;
+      // ---- combine the warps: v_lat[h][r], block (m_j, l_j); merge into the state ----
+      for (int e = et; e < nrep * RV; e += NEP) {
+        const int h = e / RV, r = e - h * RV;
+        float M = -INFINITY;
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const float2 cv = *reinterpret_cast<const float2*>(p.cosT + a[hh] * FD + f);
-          const float2 sv = *reinterpret_cast<const float2*>(p.sinT + a[hh] * FD + f);
-          r[4 * cc + 2 * hh + 0] = pack_f2(cv.x, cv.y);
-          r[4 * cc + 2 * hh + 1] = pack_f2(sv.x, sv.y);
+        for (int ww = 0; ww < NCW; ++ww) M = fmaxf(M, sM[ww * 8 + h]);
+        float v = 0.f, l = 0.f;
+#pragma unroll
+        for (int ww = 0; ww < NCW; ++ww) {
+          const float wt = exp2f(sM[ww * 8 + h] - M);
+          v = fmaf(sV[(ww * RV + r) * 8 + h], wt, v);
+          l = fmaf(sL[ww * 8 + h], wt, l);
+        }
+        sVL[h * RV + r] = v;
+        if (r == 0) {
+          float* stt = sST + (sq.uu * 8 + h) * 2;
+          const float mo = first_j ? -INFINITY : stt[0], lo = first_j ? 0.f : stt[1];
+          const float Mn = fmaxf(mo, M);
+          const float ao = exp2f(mo - Mn), an = exp2f(M - Mn);
+          sML[4 * h + 0] = l;
+          sML[4 * h + 1] = ao;
+          sML[4 * h + 2] = an;
+          stt[0] = Mn;
+          stt[1] = fmaf(lo, ao, l * an);
         }
       }
-      tmem_st16x256_x2(tbase + ((uint32_t)G.lane_off << 16) + (uint32_t)(G.tcol + 16 * s), r);
-    }
-  }
-  tmem_wait_st();
-
-  float* sM = reinterpret_cast<float*>(sm + C::OFF_SM);
-  float* sL = reinterpret_cast<float*>(sm + C::OFF_SL);
-  float* sV = reinterpret_cast<float*>(sm + C::OFF_SV);
-  float* sVL = reinterpret_cast<float*>(sm + C::OFF_VL);
-  float* sML = reinterpret_cast<float*>(sm + C::OFF_ML);
-  uint8_t* sA = sm + C::OFF_A;
-  uint8_t* sB = sm + C::OFF_B;
-  uint8_t* cV = sm + C::OFF_CV;
-  uint8_t* sQ = sm + C::OFF_Q;
-  const uint32_t sA_u = smem_u32(sA), sB_u = smem_u32(sB), cV_u = smem_u32(cV);
-  int failed_at = -1;
-  uint32_t mma_uses[2] = {0u, 0u};   // completed waits per accumulator (phase parity)
-
-  auto issue_mma = [&](int mt) {   // one thread: K~ of M-tile mt into accumulator mt & 1
-    tc_fence_after();
-    const uint32_t d = tbase + 256u + 128u * (uint32_t)(mt & 1);
+      // ---- value basis -> rows padded to QP bytes (conflict-free ldmatrix.trans) -----
+      {
+        const uint4* src = reinterpret_cast<const uint4*>(st + C::B_BV);
+        for (int e = et; e < RV * 16; e += NEP)
+          *reinterpret_cast<uint4*>(sm + C::OFF_BVP + (e >> 4) * C::QP + (e & 15) * 16) = src[e];
+      }
+      named_sync(BAR_EPI, NEP);
+      // partials and stage s are consumed: hand them back, refill the stage
+      if (et == 0) {
+        mbar_arrive(b_pfree + 8 * b2);
+        if (sqB.valid(I) && !*ab.flag) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          issueB();
+        }
+      }
+      // ---- expand once through B_V (mma.sync), merge with the running o --------------
+      // o_j[h][d] = l_j * vscale * sum_r (v_lat[h][r] / l_j) B_V[r][d]: the normalised
+      // v_lat is a weighted mean of INT8 codes (|.| <= 127), safe as an f16 operand.
+      {
+        const float lj = hl ? sML[4 * g] : 1.f;
+        const float inv_l = hl ? 1.f / lj : 0.f;
+        uint32_t va[RV / 16][2];
 #pragma unroll
-    for (int ks = 0; ks < RK / 16; ++ks) {
-      const uint64_t ad = umma_desc(sA_u + mt * C::ATILE + ks * 2 * 2048, 2048, 128);
-      const uint64_t bd = umma_desc(sB_u + ks * 256, 128, RK * 16);
-      umma_f16(d, ad, bd, ks > 0 ? 1u : 0u);
+        for (int ks = 0; ks < RV / 16; ++ks) {
+          const float2 x0 = *reinterpret_cast<const float2*>(sVL + g * RV + 16 * ks + 2 * t);
+          const float2 x1 = *reinterpret_cast<const float2*>(sVL + g * RV + 16 * ks + 2 * t + 8);
+          va[ks][0] = hl ? pack_f2(x0.x * inv_l, x0.y * inv_l) : 0u;
+          va[ks][1] = hl ? pack_f2(x1.x * inv_l, x1.y * inv_l) : 0u;
+        }
+        const float an = hl ? sML[4 * g + 2] * lj * vscale : 0.f;
+        const float ao = hl ? sML[4 * g + 1] : 0.f;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int n = 4 * ew + q;
+          float o[4] = {0.f, 0.f, 0.f, 0.f};
+          const int mi = lane >> 3, rr = lane & 7;
+          if constexpr (RV == 32) {
+            const int R = 16 * (mi >> 1) + 8 * (mi & 1) + rr;
+            uint32_t b00, b01, b10, b11;
+            ldsm_x4_t(bvp_u + R * C::QP + n * 16, b00, b01, b10, b11);
+            mma16816(o, va[0][0], 0u, va[0][1], 0u, b00, b01);
+            mma16816(o, va[1][0], 0u, va[1][1], 0u, b10, b11);
+          } else {
+            const int R = 8 * (mi & 1) + rr;
+            uint32_t b00, b01;
+            ldsm_x2_t(bvp_u + R * C::QP + n * 16, b00, b01);
+            mma16816(o, va[0][0], 0u, va[0][1], 0u, b00, b01);
+          }
+          if (hl)
+            *reinterpret_cast<float2*>(rec + g * (FD + 4) + 4 + 8 * n + 2 * t) =
+                make_float2(fmaf(oold[q].x, ao, o[0] * an), fmaf(oold[q].y, ao, o[1] * an));
+        }
+        if (last_j && et < nrep) {
+          const float* stt = sST + (sq.uu * 8 + et) * 2;
+          rec[et * (FD + 4) + 0] = stt[0] * LN2;
+          rec[et * (FD + 4) + 1] = stt[1];
+        }
+      }
+      named_sync(BAR_EPI, NEP);
     }
-    umma_commit(mbar0 + 8 * (mt & 1));
-  };
-
+    if (et == 0 && *ab.flag) drain(b_fullB, issuedB);
+    __syncwarp();
+  } else if (w >= NCW) {
+    // ============================================================= converter warps ===
+    setmaxnreg_dec<96>();
+    const int pt = tid - PT0;
+    const uint32_t sA_u = smem_u32(sm + C::OFF_A), sB_u = smem_u32(sm + C::OFF_B);
+    Seq sqA = sq;   // ring-A copies run STAGES iterations ahead
+    int issuedA = 0;
+    auto issueA = [&]() {
+      const int s = issuedA % STAGES;
+      const int64_t slot = (int64_t)sqA.unit() * p.NBc + sqA.j();
+      uint8_t* st = sm + C::OFF_RA + s * C::STAGE_A;
+      const uint32_t bar = b_fullA + 8 * s;
+      mbar_expect_tx(bar, C::CK + C::BK);
+      bulk_g2s_hint(smem_u32(st + C::A_CK), p.ck + slot * C::CK, C::CK, bar, stream_policy);
+      bulk_g2s_hint(smem_u32(st + C::A_BK), reinterpret_cast<const uint8_t*>(p.bk) + slot * C::BK, C::BK, bar,
+                    stream_policy);
+      ++issuedA;
+      sqA.next(I);
+    };
+    if (pt == 0) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      for (int k = 0; k < STAGES && sqA.valid(I); ++k) issueA();
+    }
+    int it = 0;
+    int64_t n_issued = 0;   // M-tiles handed to the tensor core
+    for (; sq.valid(I); sq.next(I), ++it) {
+      const int s = it % STAGES;
+      const uint8_t* st = sm + C::OFF_RA + s * C::STAGE_A;
+      const bool ok = waitw(b_fullA + 8 * s, (uint32_t)((it / STAGES) & 1), ab);
+      // key basis [RK][16 chunks] -> B tile [16 n-chunks][RK rows] (conflict-free walk)
+      const int bs = it & 1;
+      bool okb = ok;
+      if (it >= 2) okb = waitw(b_bslot + 8 * bs, (uint32_t)((it / 2 - 1) & 1), ab) && okb;
+      if (okb) {
+        const uint4* srcb = reinterpret_cast<const uint4*>(st + C::A_BK);
+        uint4* dstb = reinterpret_cast<uint4*>(sm + C::OFF_B + bs * C::BK);
+#pragma unroll
+        for (int q = 0; q < RK * 16 / NPT; ++q) {
+          const int idx = q * NPT + pt;
+          const int l = idx & 31, W = idx >> 5, a = l & 7, b = l >> 3;
+          int k, nc;
+          if (RK == 32) {
+            nc = a + 8 * (W & 1);
+            k = 8 * b + ((a + (W >> 1)) & 7);
+          } else {
+            nc = a + 8 * (b >> 1);
+            k = 8 * (b & 1) + ((a + W) & 7);
+          }
+          dstb[nc * RK + k] = srcb[k * 16 + nc];
+        }
+      }
+      // key codes -> FP16 A tiles, one M-tile at a time
 #pragma unroll 1
-  for (int u = 0; u < nu; ++u) {
-    const int s = u % STAGES;
-    uint8_t* st = sm + s * C::STAGE;
-    const bool ok = mbar_wait(bar0 + 8 * s, (uint32_t)((u / STAGES) & 1));
-    if (__syncthreads_or(!ok)) {   // every thread takes the same decision
-      failed_at = u;
-      break;
-    }
-    // ---- conversion pass -----------------------------------------------------------
-    {
-      // key codes -> FP16 A tiles (row m of M-tile mt = token mt*128 + m), 16-byte
-      // K-chunks of 8 codes, K-major, no swizzle; one item = 16 codes of one token
-      for (int e = tid; e < C::TB * (RK / 16); e += C::NT) {
-        const int tau = e % C::TB, hf = e / C::TB;
-        const uint4 v = *reinterpret_cast<const uint4*>(st + tau * RK + hf * 16);
-        const int m = tau & 127;
-        uint8_t* dst = sA + (tau >> 7) * C::ATILE + 2 * hf * 2048 + (m >> 3) * 128 + (m & 7) * 16;
-        uint4 o0, o1;
-        i8x4_to_h2(v.x, o0.x, o0.y);
-        i8x4_to_h2(v.y, o0.z, o0.w);
-        i8x4_to_h2(v.z, o1.x, o1.y);
-        i8x4_to_h2(v.w, o1.z, o1.w);
-        *reinterpret_cast<uint4*>(dst) = o0;
-        *reinterpret_cast<uint4*>(dst + 2048) = o1;
-      }
-      // key basis [RK][128] -> MN-major B tile [16 n-chunks][RK rows][16 B]
-      const uint4* srcb = reinterpret_cast<const uint4*>(st + C::CK + C::CV);
-      for (int e = tid; e < RK * 16; e += C::NT) {
-        const int k = e % RK, nc = e / RK;
-        reinterpret_cast<uint4*>(sB)[nc * RK + k] = srcb[k * 16 + nc];
-      }
-      // value codes are stored in the value-tile layout the ldmatrix below reads
-      const uint4* srcv = reinterpret_cast<const uint4*>(st + C::CK);
-      for (int e = tid; e < C::CV / 16; e += C::NT) reinterpret_cast<uint4*>(cV)[e] = srcv[e];
-      // value basis [RV][128] -> chunk index XOR (rank & 7) (conflict-free ldmatrix)
-      const uint4* srcbv = reinterpret_cast<const uint4*>(st + C::CK + C::CV + C::BK);
-      for (int e = tid; e < RV * 16; e += C::NT) {
-        const int R = e >> 4, n = e & 15;
-        reinterpret_cast<uint4*>(sm + C::OFF_BV)[R * 16 + (n ^ (R & 7))] = srcbv[e];
-      }
-      // query rows, 16-byte chunk index XOR head
-      const uint4* srcq = reinterpret_cast<const uint4*>(st + C::CK + C::CV + C::BK + C::BV);
-      for (int e = tid; e < nrep * 16; e += C::NT) {
-        const int h = e >> 4, n = e & 15;
-        reinterpret_cast<uint4*>(sQ)[h * 16 + (n ^ h)] = srcq[e];
-      }
-    }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncthreads();
-    if (tid == 0) {
-      issue_mma(0);
-      if (C::MT > 1) issue_mma(1);
-    }
-    const int64_t unit = u0 + u;
-    const int64_t slotid = unit * p.NBc + j;
-    const float kscale = p.sk[slotid] * p.scale * LOG2E;
-    const float vscale = p.sv[slotid];
-
-    // ---- query fragments (B operand of the score MMA), padded heads zeroed ---------
-    uint32_t qf[8][2];
+      for (int mt = 0; mt < MT; ++mt) {
+        const int64_t n = (int64_t)it * MT + mt;
+        const int as = (int)(n % NA);
+        bool oka = okb;
+        if (n >= NA) oka = waitw(b_aslot + 8 * as, (uint32_t)((n / NA - 1) & 1), ab) && oka;
+        if (oka) {
+          const uint8_t* src = st + C::A_CK + mt * 128 * RK;
+          uint8_t* dst = sm + C::OFF_A + as * C::ATILE;
 #pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      if (g < nrep) {
-        qf[ks][0] = *reinterpret_cast<const uint32_t*>(sQ + (g * 16 + ((2 * ks) ^ g)) * 16 + 4 * t);
-        qf[ks][1] = *reinterpret_cast<const uint32_t*>(sQ + (g * 16 + ((2 * ks + 1) ^ g)) * 16 + 4 * t);
-      } else {
-        qf[ks][0] = qf[ks][1] = 0u;
-      }
-    }
-    // ---- scores: K~ from TMEM, rotate, dot ----------------------------------------
-    float sc[4][4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const Group<NW> G(w, i);
-      const bool first_of_tile = (NW == 8) || ((i & 1) == 0);
-      const int b = G.mt & 1;
-      if (first_of_tile) {
-        const bool mok = mbar_wait(mbar0 + 8 * b, mma_uses[b] & 1u);
-        mma_uses[b]++;
-        if (!mok) atomicExch(err, 1);
-        tc_fence_after();
-      }
-      const uint32_t lrow = (uint32_t)G.lane_off << 16;
-      const uint32_t dcol = tbase + lrow + 256u + 128u * (uint32_t)b;
-      const uint32_t tcol = tbase + lrow + (uint32_t)G.tcol;
-      float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
-      uint32_t cur[24];
-      tmem_ld3(dcol, dcol + 64, tcol, cur);
-      tmem_wait_ld_tied(cur);
-#pragma unroll
-      for (int s4 = 0; s4 < 4; ++s4) {
-        uint32_t nxt[24];
-        if (s4 < 3) tmem_ld3(dcol + 16 * (s4 + 1), dcol + 64 + 16 * (s4 + 1), tcol + 16 * (s4 + 1), nxt);
-        uint32_t k1[4], k2[4];
-#pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {   // hh: row g (0) or g+8 (1)
-            const int e = 4 * cc + 2 * hh;
-            const __half2 a1 = u2h(pack_f2(__uint_as_float(cur[e]), __uint_as_float(cur[e + 1])));
-            const __half2 a2 = u2h(pack_f2(__uint_as_float(cur[8 + e]), __uint_as_float(cur[8 + e + 1])));
-            const __half2 c = u2h(cur[16 + e]), sn = u2h(cur[16 + e + 1]);
-            k1[2 * cc + hh] = h2u(__hfma2(c, a1, __hneg2(__hmul2(sn, a2))));   // c K1 - s K2
-            k2[2 * cc + hh] = h2u(__hfma2(c, a2, __hmul2(sn, a1)));            // s K1 + c K2
+          for (int q = 0; q < 128 * (RK / 16) / NPT; ++q) {
+            const int e = q * NPT + pt;
+            const int tau = RK == 32 ? (e >> 1) : e, hf = RK == 32 ? (e & 1) : 0;
+            const uint4 v = *reinterpret_cast<const uint4*>(src + tau * RK + hf * 16);
+            uint4 o0, o1;
+            i8x4_to_h2(v.x, o0.x, o0.y);
+            i8x4_to_h2(v.y, o0.z, o0.w);
+            i8x4_to_h2(v.z, o1.x, o1.y);
+            i8x4_to_h2(v.w, o1.z, o1.w);
+            uint8_t* d = dst + 2 * hf * 2048 + (tau >> 3) * 128 + (tau & 7) * 16;
+            *reinterpret_cast<uint4*>(d) = o0;
+            *reinterpret_cast<uint4*>(d + 2048) = o1;
           }
         }
-        mma16816(sa, k1[0], k1[1], k1[2], k1[3], qf[s4][0], qf[s4][1]);
-        mma16816(sb, k2[0], k2[1], k2[2], k2[3], qf[s4 + 4][0], qf[s4 + 4][1]);
-        if (s4 < 3) {
-          tmem_wait_ld_tied(nxt);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        named_sync(BAR_CONV, NPT);
+        if (pt == 0 && oka && !*ab.flag) {
+          const int b = (int)(n & 1);
+          bool oke = true;
+          if (n >= 2) oke = wait1(b_acce + 8 * b, (uint32_t)((n / 2 - 1) & 1), ab);
+          if (oke) {
+            tc_fence_after();
+            const uint32_t d = tbase + 256u + 128u * (uint32_t)b;
+            const uint32_t a_u = sA_u + as * C::ATILE, b_u = sB_u + bs * C::BK;
 #pragma unroll
-          for (int q = 0; q < 24; ++q) cur[q] = nxt[q];
+            for (int ks = 0; ks < RK / 16; ++ks) {
+              const uint64_t ad = umma_desc(a_u + ks * 2 * 2048, 2048, 128);
+              const uint64_t bd = umma_desc(b_u + ks * 256, 128, RK * 16);
+              umma_f16(d, ad, bd, ks > 0 ? 1u : 0u);
+            }
+            umma_commit(b_accf + 8 * b);
+            umma_commit(b_aslot + 8 * as);
+            if (mt == MT - 1) umma_commit(b_bslot + 8 * bs);
+            n_issued = n + 1;
+          }
+        }
+        __syncwarp();
+      }
+      // stage s of ring A is converted: refill it
+      if (pt == 0 && sqA.valid(I) && !*ab.flag) issueA();
+      __syncwarp();
+    }
+    if (pt == 0 && *ab.flag) {
+      drain(b_fullA, issuedA);
+      if (n_issued > 0) {   // the last MMAs handed to the tensor core
+        const int64_t n = n_issued - 1;
+        const uint64_t t0 = gtimer();
+        while (!mbar_try_wait(b_accf + 8 * (n & 1), (uint32_t)((n / 2) & 1)) && gtimer() - t0 < kWaitNs) {
         }
       }
+    }
+    __syncwarp();
+  } else {
+    // ============================================================== consumer warps ===
+    setmaxnreg_inc<160>();
+    const int lane_off = 32 * (w & 3) + 16 * (w >> 2);
+    const uint4* rope_tab = reinterpret_cast<const uint4*>(p.rope);
+    const bool live0 = 2 * t < nrep, live1 = 2 * t + 1 < nrep, hl = g < nrep;
+    const uint32_t lrow = (uint32_t)lane_off << 16;
+    int prev_j = -1;
+    Seq sqn = sq;   // one iteration ahead: scale prefetch
+    float ks_next = sq.valid(I) ? __ldg(p.sk + (int64_t)sq.unit() * p.NBc + sq.j()) : 0.f;
+    sqn.next(I);
+    int it = 0;
+    for (; sq.valid(I); sq.next(I), ++it) {
+      const int s = it % STAGES, b2 = it & 1;
+      const uint8_t* st = sm + C::OFF_RB + s * C::STAGE_B;
+      const int j = sq.j();
+      // ---- RoPE rows of block j for this warp's 16-lane slabs -> TMEM --------------
+      if (j != prev_j) {
+        prev_j = j;
+        uint32_t r[MT][32];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) sc[i][e] = sa[e] + sb[e];
-      // accumulator b is free once every warp has read this M-tile: refill it
-      const bool last_of_tile = (NW == 8) || ((i & 1) == 1);
-      if (last_of_tile && G.mt + 2 < C::MT) {
+        for (int i = 0; i < MT; ++i) {
+          const int tile16 = (i * 128 + lane_off) >> 4;
+          const uint4* src = rope_tab + (((int64_t)j * (C::TB / 16) + tile16) * 32 + lane) * 8;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const uint4 v = __ldg(src + q);
+            r[i][4 * q] = v.x;
+            r[i][4 * q + 1] = v.y;
+            r[i][4 * q + 2] = v.z;
+            r[i][4 * q + 3] = v.w;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < MT; ++i) tmem_st_rope(tbase + lrow + (uint32_t)(64 * i), r[i]);
+      }
+      const float kscale = ks_next * p.scale * LOG2E;
+      if (sqn.valid(I)) ks_next = __ldg(p.sk + (int64_t)sqn.unit() * p.NBc + sqn.j());
+      sqn.next(I);
+      waitw(b_fullB + 8 * s, (uint32_t)((it / STAGES) & 1), ab);
+      // ---- query fragments: dims 16k + 4t .. +3 of head g ----------------------------
+      uint2 qf[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        qf[k] = hl ? *reinterpret_cast<const uint2*>(st + C::B_Q + g * C::QP + 32 * k + 8 * t) : make_uint2(0u, 0u);
+      // ---- scores: K~ from TMEM (next M-tile loading while this one computes) --------
+      float sc[MT][4];
+      uint32_t kr[2][32], ro[2][32];
+      {
+        const int64_t n = (int64_t)it * MT;
+        waitw(b_accf + 8 * (int)(n & 1), (uint32_t)((n / 2) & 1), ab);
+        tc_fence_after();
+        tmem_ld_k_rope_nowait(tbase + lrow + 256u + 128u * (uint32_t)(n & 1), tbase + lrow, kr[0], ro[0]);
+        tmem_wait_ld_64(kr[0], ro[0]);
         tc_fence_before();
-        __syncthreads();
-        if (tid == 0) issue_mma(G.mt + 2);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(b_acce + 8 * (int)(n & 1));
       }
-    }
-    // ---- per-warp softmax over 64 tokens (log2 domain) ----------------------------
-    // raw scores times kscale (> 0) are the logits in log2 units; fold the scale into
-    // the exp2 argument instead of scaling every score
-    // (the max of the scaled logits is max*k for k >= 0 and min*k for k < 0)
-    const bool kpos = kscale >= 0.f;
-    float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      mx0 = fmaxf(mx0, kpos ? fmaxf(sc[i][0], sc[i][2]) : -fminf(sc[i][0], sc[i][2]));
-      mx1 = fmaxf(mx1, kpos ? fmaxf(sc[i][1], sc[i][3]) : -fminf(sc[i][1], sc[i][3]));
-    }
-#pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-    }
-    mx0 = kpos ? mx0 * kscale : -mx0 * kscale;
-    mx1 = kpos ? mx1 * kscale : -mx1 * kscale;
-    const bool live0 = 2 * t < nrep, live1 = 2 * t + 1 < nrep;
-    float l0 = 0.f, l1 = 0.f;
-    float vacc[RV / 16][4];
-#pragma unroll
-    for (int rt = 0; rt < RV / 16; ++rt) vacc[rt][0] = vacc[rt][1] = vacc[rt][2] = vacc[rt][3] = 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      sc[i][0] = live0 ? exp2f(fmaf(sc[i][0], kscale, -mx0)) : 0.f;
-      sc[i][2] = live0 ? exp2f(fmaf(sc[i][2], kscale, -mx0)) : 0.f;
-      sc[i][1] = live1 ? exp2f(fmaf(sc[i][1], kscale, -mx1)) : 0.f;
-      sc[i][3] = live1 ? exp2f(fmaf(sc[i][3], kscale, -mx1)) : 0.f;
-      l0 += sc[i][0] + sc[i][2];
-      l1 += sc[i][1] + sc[i][3];
-      // ---- v_lat[rank][head] += codes_V^T . P  (one ldmatrix per 16 tokens) ---------
-      const uint32_t b0 = movm_t(pack_f2(sc[i][0], sc[i][1]));
-      const uint32_t b1 = movm_t(pack_f2(sc[i][2], sc[i][3]));
-      const int tt = Group<NW>(w, i).token0() >> 4;
-      if constexpr (RV == 32) {
-        uint32_t v0, v1, v2, v3;
-        ldsm_x4(cV_u + ((tt * RV + (lane ^ (tt & 7))) << 4), v0, v1, v2, v3);
-        uint32_t a0, a1, a2, a3;
-        i8x4_to_h2(v0, a0, a2);
-        i8x4_to_h2(v1, a1, a3);
-        mma16816(vacc[0], a0, a1, a2, a3, b0, b1);
-        i8x4_to_h2(v2, a0, a2);
-        i8x4_to_h2(v3, a1, a3);
-        mma16816(vacc[1], a0, a1, a2, a3, b0, b1);
-      } else {
-        uint32_t v0, v1;
-        ldsm_x2(cV_u + ((tt * RV + ((lane & 15) ^ (tt & 7))) << 4), v0, v1);
-        uint32_t a0, a1, a2, a3;
-        i8x4_to_h2(v0, a0, a2);
-        i8x4_to_h2(v1, a1, a3);
-        mma16816(vacc[0], a0, a1, a2, a3, b0, b1);
-      }
-    }
-#pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-      l0 += __shfl_xor_sync(0xffffffffu, l0, o);
-      l1 += __shfl_xor_sync(0xffffffffu, l1, o);
-    }
-    if (g == 0) {
-      sM[w * 8 + 2 * t] = mx0;
-      sM[w * 8 + 2 * t + 1] = mx1;
-      sL[w * 8 + 2 * t] = l0;
-      sL[w * 8 + 2 * t + 1] = l1;
-    }
-#pragma unroll
-    for (int rt = 0; rt < RV / 16; ++rt) {
-      float* base = sV + (w * RV + rt * 16) * 8;
-      base[g * 8 + 2 * t] = vacc[rt][0];
-      base[g * 8 + 2 * t + 1] = vacc[rt][1];
-      base[(g + 8) * 8 + 2 * t] = vacc[rt][2];
-      base[(g + 8) * 8 + 2 * t + 1] = vacc[rt][3];
-    }
-    __syncthreads();
-    // ---- combine warps: v_lat[h][r], m, l ------------------------------------------
-    for (int e = tid; e < nrep * RV; e += C::NT) {
-      const int h = e / RV, r = e % RV;
-      float M = -INFINITY;
-#pragma unroll
-      for (int ww = 0; ww < NW; ++ww) M = fmaxf(M, sM[ww * 8 + h]);
-      float v = 0.f, l = 0.f;
-#pragma unroll
-      for (int ww = 0; ww < NW; ++ww) {
-        const float wt = exp2f(sM[ww * 8 + h] - M);
-        v = fmaf(sV[(ww * RV + r) * 8 + h], wt, v);
-        l = fmaf(sL[ww * 8 + h], wt, l);
-      }
-      sVL[h * RV + r] = v;
-      if (r == 0) {
-        sML[2 * h] = M;
-        sML[2 * h + 1] = l;
-      }
-    }
-    __syncthreads();
-    // ---- expand once through B_V (mma.sync) and write the partial -----------------
-    // o[h][d] = l_h * sum_r (v_lat[h][r] / l_h) B_V[r][d]: the normalised v_lat is a
-    // weighted mean of INT8 codes (|.| <= 127), safe as an f16 operand.
-    {
-      float* rec = p.ws + (unit * p.nparts + j) * (int64_t)nrep * (FD + 4);
-      const uint32_t bv_u = smem_u32(sm + C::OFF_BV);
-      const bool hl = g < nrep;
-      const float inv_l = hl ? 1.f / sML[2 * g + 1] : 0.f;
-      uint32_t va[RV / 16][2];
-#pragma unroll
-      for (int ks = 0; ks < RV / 16; ++ks) {
-        const float2 x0 = *reinterpret_cast<const float2*>(sVL + g * RV + 16 * ks + 2 * t);
-        const float2 x1 = *reinterpret_cast<const float2*>(sVL + g * RV + 16 * ks + 2 * t + 8);
-        va[ks][0] = hl ? pack_f2(x0.x * inv_l, x0.y * inv_l) : 0u;
-        va[ks][1] = hl ? pack_f2(x1.x * inv_l, x1.y * inv_l) : 0u;
-      }
-      const float oscale = hl ? sML[2 * g + 1] * vscale : 0.f;
-      constexpr int NTW = 16 / NW;   // n-tiles (8 dims each) per warp
-#pragma unroll
-      for (int q = 0; q < NTW; ++q) {
-        const int n = w * NTW + q;
-        float o[4] = {0.f, 0.f, 0.f, 0.f};
-        const int mi = lane >> 3, rr = lane & 7;
-        if constexpr (RV == 32) {
-          const int R = 16 * (mi >> 1) + 8 * (mi & 1) + rr;
-          uint32_t b00, b01, b10, b11;
-          ldsm_x4_t(bv_u + R * 256 + ((n ^ (R & 7)) << 4), b00, b01, b10, b11);
-          mma16816(o, va[0][0], 0u, va[0][1], 0u, b00, b01);
-          mma16816(o, va[1][0], 0u, va[1][1], 0u, b10, b11);
-        } else {
-          const int R = 8 * (mi & 1) + rr;
-          uint32_t b00, b01;
-          ldsm_x2_t(bv_u + R * 256 + ((n ^ (R & 7)) << 4), b00, b01);
-          mma16816(o, va[0][0], 0u, va[0][1], 0u, b00, b01);
+      for (int i = 0; i < MT; ++i) {
+        const int cb = i & 1, nb = cb ^ 1;
+        const int64_t n1 = (int64_t)it * MT + i + 1;
+        if (i + 1 < MT) {
+          waitw(b_accf + 8 * (int)(n1 & 1), (uint32_t)((n1 / 2) & 1), ab);
+          tc_fence_after();
+          tmem_ld_k_rope_nowait(tbase + lrow + 256u + 128u * (uint32_t)(n1 & 1), tbase + lrow + (uint32_t)(64 * (i + 1)),
+                                kr[nb], ro[nb]);
         }
-        if (hl)
-          *reinterpret_cast<float2*>(rec + g * (FD + 4) + 4 + 8 * n + 2 * t) =
-              make_float2(o[0] * oscale, o[1] * oscale);
+        float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          uint32_t k1[4], k2[4];   // [2hh + c]
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int hh = q >> 1, c = q & 1;
+            const __half2 x = u2h(kr[cb][4 * k + q]), y = u2h(kr[cb][16 + 4 * k + q]);
+            const __half2 cs = u2h(ro[cb][8 * k + 4 * c + 2 * hh]), sn = u2h(ro[cb][8 * k + 4 * c + 2 * hh + 1]);
+            k1[q] = h2u(__hfma2(cs, x, __hneg2(__hmul2(sn, y))));   // c K1 - s K2
+            k2[q] = h2u(__hfma2(cs, y, __hmul2(sn, x)));            // s K1 + c K2
+          }
+          mma16816(sa, k1[0], k1[2], k1[1], k1[3], qf[k].x, qf[k].y);
+          mma16816(sb, k2[0], k2[2], k2[1], k2[3], qf[k + 4].x, qf[k + 4].y);
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[i][e] = sa[e] + sb[e];
+        if (i + 1 < MT) {
+          tmem_wait_ld_64(kr[nb], ro[nb]);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(b_acce + 8 * (int)(n1 & 1));
+        }
       }
-      if (tid < nrep) {
-        rec[tid * (FD + 4) + 0] = sML[2 * tid] * LN2;
-        rec[tid * (FD + 4) + 1] = sML[2 * tid + 1];
+      // ---- per-warp softmax over its tokens (log2 domain) ------------------------------
+      // raw scores times kscale are the logits in log2 units; the max of the scaled
+      // logits is max*k for k >= 0 and min*k for k < 0
+      const bool kpos = kscale >= 0.f;
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < MT; ++i) {
+        mx0 = fmaxf(mx0, kpos ? fmaxf(sc[i][0], sc[i][2]) : -fminf(sc[i][0], sc[i][2]));
+        mx1 = fmaxf(mx1, kpos ? fmaxf(sc[i][1], sc[i][3]) : -fminf(sc[i][1], sc[i][3]));
       }
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+      }
+      mx0 = kpos ? mx0 * kscale : -mx0 * kscale;
+      mx1 = kpos ? mx1 * kscale : -mx1 * kscale;
+      float l0 = 0.f, l1 = 0.f;
+      float vacc[RV / 16][4];
+#pragma unroll
+      for (int rt = 0; rt < RV / 16; ++rt) vacc[rt][0] = vacc[rt][1] = vacc[rt][2] = vacc[rt][3] = 0.f;
+      const uint32_t cV_u = smem_u32(st + C::B_CV);
+#pragma unroll
+      for (int i = 0; i < MT; ++i) {
+        sc[i][0] = live0 ? exp2f(fmaf(sc[i][0], kscale, -mx0)) : 0.f;
+        sc[i][2] = live0 ? exp2f(fmaf(sc[i][2], kscale, -mx0)) : 0.f;
+        sc[i][1] = live1 ? exp2f(fmaf(sc[i][1], kscale, -mx1)) : 0.f;
+        sc[i][3] = live1 ? exp2f(fmaf(sc[i][3], kscale, -mx1)) : 0.f;
+        l0 += sc[i][0] + sc[i][2];
+        l1 += sc[i][1] + sc[i][3];
+        // ---- v_lat[rank][head] += codes_V^T . P  (one ldmatrix per 16 tokens) ---------
+        const uint32_t b0 = movm_t(pack_f2(sc[i][0], sc[i][1]));
+        const uint32_t b1 = movm_t(pack_f2(sc[i][2], sc[i][3]));
+        const int tt = (i * 128 + lane_off) >> 4;
+        if constexpr (RV == 32) {
+          uint32_t v0, v1, v2, v3;
+          ldsm_x4(cV_u + ((tt * RV + (lane ^ (tt & 7))) << 4), v0, v1, v2, v3);
+          uint32_t a0, a1, a2, a3;
+          i8x4_to_h2(v0, a0, a2);
+          i8x4_to_h2(v1, a1, a3);
+          mma16816(vacc[0], a0, a1, a2, a3, b0, b1);
+          i8x4_to_h2(v2, a0, a2);
+          i8x4_to_h2(v3, a1, a3);
+          mma16816(vacc[1], a0, a1, a2, a3, b0, b1);
+        } else {
+          uint32_t v0, v1;
+          ldsm_x2(cV_u + ((tt * RV + ((lane & 15) ^ (tt & 7))) << 4), v0, v1);
+          uint32_t a0, a1, a2, a3;
+          i8x4_to_h2(v0, a0, a2);
+          i8x4_to_h2(v1, a1, a3);
+          mma16816(vacc[0], a0, a1, a2, a3, b0, b1);
+        }
+      }
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+      }
+      // ---- hand (m, l, v_lat) of this warp to the epilogue ----------------------------
+      if (it >= 2) waitw(b_pfree + 8 * b2, (uint32_t)((it / 2 - 1) & 1), ab);
+      float* sM = reinterpret_cast<float*>(sm + C::OFF_P + b2 * C::PART);
+      float* sL = sM + NCW * 8;
+      float* sV = sL + NCW * 8;
+      if (g == 0) {
+        sM[w * 8 + 2 * t] = mx0;
+        sM[w * 8 + 2 * t + 1] = mx1;
+        sL[w * 8 + 2 * t] = l0;
+        sL[w * 8 + 2 * t + 1] = l1;
+      }
+#pragma unroll
+      for (int rt = 0; rt < RV / 16; ++rt) {
+        float* base = sV + (w * RV + rt * 16) * 8;
+        base[g * 8 + 2 * t] = vacc[rt][0];
+        base[g * 8 + 2 * t + 1] = vacc[rt][1];
+        base[(g + 8) * 8 + 2 * t] = vacc[rt][2];
+        base[(g + 8) * 8 + 2 * t + 1] = vacc[rt][3];
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(b_pready + 8 * b2);
     }
-    __syncthreads();
-    if (tid == 0 && u + STAGES < nu) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(u + STAGES);
-    }
-  }
-  if (failed_at >= 0 && tid == 0) {
-    atomicExch(err, 1);
-    // drain the copies still in flight (bounded) before the shared memory goes away:
-    // units failed_at .. failed_at + STAGES - 1 were issued and not yet consumed
-    for (int u = failed_at; u < min(failed_at + STAGES, nu); ++u)
-      mbar_wait(bar0 + 8 * (u % STAGES), (uint32_t)((u / STAGES) & 1));
   }
   tc_fence_before();
   __syncthreads();
   if (w == 0) tmem_dealloc(tbase, 512);
 }
 
-template <int RK, int RV, int NW>
-int launch(const DecodeParams& p, cudaStream_t st) {
-  using C = Cfg<RK, RV, NW>;
+// RoPE words of every cold block, in the per-lane register order the consumers store to
+// TMEM: [block][token/16][lane][32 words]; word 4e + 2hh + cc of lane (g, t) is the f16
+// pair (f0, f0 + 1) of cos (cc = 0) or sin (cc = 1) for token 16*tile + g + 8hh, with
+// f0 = 16*(e/2) + 4t + 2*(e%2).  First-half table entries (tied or distance RoPE).
+__global__ void __launch_bounds__(128) rope_pack_kernel(DecodeParams p) {
+  const int j = blockIdx.x, tile = blockIdx.y * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (tile >= p.Tb / 16) return;
+  const int g = lane >> 2, t = lane & 3;
+  uint32_t r[32];
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    const int64_t pos = p.bpos[j] + tile * 16 + g + 8 * hh;
+    int64_t a = p.mode == SPX_ROPE_DISTANCE ? (p.qpos - pos > 0 ? p.qpos - pos : 0) : pos;
+    a = a < 0 ? 0 : (a >= p.rope_len ? p.rope_len - 1 : a);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int f0 = 16 * (e >> 1) + 4 * t + 2 * (e & 1);
+      const float2 c = *reinterpret_cast<const float2*>(p.cosT + a * FD + f0);
+      const float2 s = *reinterpret_cast<const float2*>(p.sinT + a * FD + f0);
+      r[4 * e + 2 * hh + 0] = pack_f2(c.x, c.y);
+      r[4 * e + 2 * hh + 1] = pack_f2(s.x, s.y);
+    }
+  }
+  uint4* dst = reinterpret_cast<uint4*>(p.rope) + (((int64_t)j * (p.Tb / 16) + tile) * 32 + lane) * 8;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) dst[q] = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+}
+
+static int num_sms() {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (cache[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+// Items of G units x JR blocks: pick the split whose slowest CTA does the least work
+// (rounds of items x item size), preferring longer block ranges (fewer partial records).
+struct Plan {
+  int G, JR, ngroups, nranges, nitems, grid;
+};
+static Plan plan(int units, int nblk, int sms) {
+  Plan best{};
+  long best_cost = -1;
+  for (int G : {32, 16, 8}) {
+    const int Gu = G < units ? G : units;
+    const int ngroups = (units + Gu - 1) / Gu;
+    for (int nr = 1; nr <= nblk; ++nr) {
+      const int JR = (nblk + nr - 1) / nr;
+      const int nranges = (nblk + JR - 1) / JR;
+      if (nranges != nr) continue;
+      const long items = (long)ngroups * nranges;
+      const long rounds = (items + sms - 1) / sms;
+      const long cost = rounds * Gu * JR;
+      if (best_cost < 0 || cost < best_cost) {
+        best_cost = cost;
+        best = Plan{Gu, JR, ngroups, nranges, (int)items, (int)(items < sms ? items : sms)};
+      }
+    }
+  }
+  return best;
+}
+
+template <int RK, int RV, int MT>
+int launch(DecodeParams p, cudaStream_t st) {
+  using C = Cfg<RK, RV, MT>;
   const int units = p.L * p.B * p.H;
-  long want = (long)units * p.nblk / (148L * 4);
-  int upc = (int)(want < 1 ? 1 : (want > 64 ? 64 : want));
-  const int chunks = (units + upc - 1) / upc;
-  SPX_REQUIRE(chunks <= 65535, SPX_ERR_UNSUPPORTED, "too many units for one launch");
-  cudaFuncSetAttribute(cold_fast_kernel<RK, RV, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::BYTES);
-  dim3 grid(p.nblk, chunks);
-  cold_fast_kernel<RK, RV, NW><<<grid, C::NT, C::BYTES, st>>>(p, upc);
+  const Plan pl = plan(units, p.nblk, num_sms());
+  dim3 rg(p.nblk, (p.Tb / 16 + 3) / 4);
+  rope_pack_kernel<<<rg, 128, 0, st>>>(p);
+  int rc = launch_status("rope_pack_kernel");
+  if (rc != SPX_OK) return rc;
+  cudaFuncSetAttribute(cold_fast_kernel<RK, RV, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::BYTES);
+  const Items items{pl.G, pl.JR, pl.ngroups, pl.nitems, p.nblk, units};
+  cold_fast_kernel<RK, RV, MT><<<pl.grid, NT, C::BYTES, st>>>(p, items);
   return launch_status("cold_fast_kernel");
 }
 
@@ -643,14 +918,18 @@ bool decode_fast_supported(const DecodeParams& p) {
   return true;
 }
 
+int decode_fast_ncold(const DecodeParams& p) {
+  return fastk::plan(p.L * p.B * p.H, p.nblk, fastk::num_sms()).nranges;
+}
+
 template <int RK, int RV>
-static int launch_nw(const DecodeParams& p, cudaStream_t st) {
-  return p.Tb == 256 ? fastk::launch<RK, RV, 4>(p, st) : fastk::launch<RK, RV, 8>(p, st);
+static int launch_mt(const DecodeParams& p, cudaStream_t st) {
+  return p.Tb == 256 ? fastk::launch<RK, RV, 2>(p, st) : fastk::launch<RK, RV, 4>(p, st);
 }
 
 int decode_fast_cold(const DecodeParams& p, cudaStream_t st) {
-  if (p.RK == 32) return p.RV == 32 ? launch_nw<32, 32>(p, st) : launch_nw<32, 16>(p, st);
-  return p.RV == 32 ? launch_nw<16, 32>(p, st) : launch_nw<16, 16>(p, st);
+  if (p.RK == 32) return p.RV == 32 ? launch_mt<32, 32>(p, st) : launch_mt<32, 16>(p, st);
+  return p.RV == 32 ? launch_mt<16, 32>(p, st) : launch_mt<16, 16>(p, st);
 }
 
 }  // namespace spx

@@ -55,7 +55,7 @@ int spx_decode_attn_noalloc(const spx_decode_args* a, void* stream) {
   void* base = nullptr;
   rc = noalloc_scratch(&base);
   if (rc != SPX_OK) return rc;
-  p.ws = reinterpret_cast<float*>(reinterpret_cast<char*>(base) + kWsHeader);
+  decode_set_workspace(&p, base);
   return decode_dispatch(p, (cudaStream_t)stream);
 }
 
