@@ -9,9 +9,10 @@
 //
 // Warp roles (4 warpgroups, 512 threads, one CTA per SM; registers rebalanced with
 // setmaxnreg: 160 for the consumers, 96 for the others):
-//   warpgroup 2  converters: ring A (INT8 key codes [T][RK], FP16 key basis [RK][128],
-//                bulk-copied 3 stages ahead by thread 256) -> FP16 UMMA A tiles
-//                (K-major, no swizzle) and the MN-major B tile; thread 256 issues
+//   warpgroup 2  warps 8-10 convert ring A (INT8 key codes [T][RK], FP16 key basis
+//                [RK][128]) -> FP16 UMMA A tiles (K-major, no swizzle) and the MN-major B
+//                tile, signalling each tile on an mbarrier; lane 0 of warp 11 bulk-copies
+//                ring A 3 stages ahead and issues
 //                  tcgen05.mma kind::f16  M=128 tokens x N=128 dims x K=16, D = f16
 //                (K~ = codes_K @ B_K) into one of two TMEM accumulators per M-tile.
 //   warpgroups 0-1  consumers, two warps per TMEM lane quadrant, 16 tokens of each
@@ -46,7 +47,8 @@ constexpr int NPT = NPW * 32;
 constexpr int ET0 = (NCW + NPW) * 32;      // first epilogue thread
 constexpr int NEP = NEW * 32;
 constexpr int GMAX = 32;                   // units per item at most
-constexpr int BAR_CONV = 2, BAR_EPI = 3;   // named barriers
+constexpr int NCV = NPW - 1;               // converter warps that convert; the last one issues MMAs
+constexpr int BAR_EPI = 3;                 // named barrier of the epilogue warps
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LN2 = 0.6931471805599453f;
 constexpr uint64_t kWaitNs = 2000000000ull;   // 2 s
@@ -59,8 +61,9 @@ __device__ __forceinline__ uint64_t gtimer() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+// Named barrier over n threads, non-aligned form: threads of a warp may arrive separately.
 __device__ __forceinline__ void named_sync(int id, int n) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+  asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
 // ------------------------------------------------------------------ mbarrier / TMA --
@@ -81,6 +84,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t a, uint32_t parity) {
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(a), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// The same test, but the thread may sleep in hardware (up to kSuspendNs) until the phase
+// completes instead of spinning on issue slots the working warps need.
+constexpr uint32_t kSuspendNs = 200000;
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t a, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(a), "r"(parity), "n"(kSuspendNs)
       : "memory");
   return ok != 0;
 }
@@ -121,30 +138,36 @@ struct Abort {
 // Single-thread bounded wait.  Returns false when aborted (now or earlier).
 __device__ __forceinline__ bool wait1(uint32_t bar, uint32_t parity, const Abort& ab) {
   if (mbar_try_wait(bar, parity)) return true;
-  if (*ab.flag) return false;
   const uint64_t t0 = gtimer();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 15u) == 0) {
-      if (*ab.flag) return false;
-      if (gtimer() - t0 > kWaitNs) {
-        *ab.flag = 1;
-        atomicExch(ab.err, 1);
-        return false;
-      }
+  for (;;) {
+    if (*ab.flag) return false;
+    if (mbar_try_wait_sleep(bar, parity)) return true;
+    if (gtimer() - t0 > kWaitNs) {
+      *ab.flag = 1;
+      atomicExch(ab.err, 1);
+      return false;
     }
   }
 }
-// Warp-wide bounded wait with a warp-uniform result (all 32 lanes call it).
-__device__ __forceinline__ bool waitw(uint32_t bar, uint32_t parity, const Abort& ab) {
+// Slow path of waitw: lane 0 sleeps on the barrier (bounded), then every lane observes
+// the completed phase itself (acquire); the warp is reconverged before returning.
+__device__ __forceinline__ bool waitw_slow(uint32_t bar, uint32_t parity, const Abort& ab) {
   int r = 0;
   if ((threadIdx.x & 31) == 0) r = wait1(bar, parity, ab) ? 1 : 0;
   r = __shfl_sync(0xffffffffu, r, 0);
-  if (r) {   // every lane observes the completed phase itself (acquire)
-    for (int k = 0; k < (1 << 20) && !mbar_try_wait(bar, parity); ++k) {
+  if (r) {
+    const uint64_t t0 = gtimer();
+    while (!mbar_try_wait(bar, parity) && gtimer() - t0 < kWaitNs) {
     }
   }
+  __syncwarp();
   return r != 0;
+}
+// Warp-wide bounded wait with a warp-uniform result (all 32 lanes call it).  The common
+// case - the phase has already completed - costs one barrier test per lane.
+__device__ __forceinline__ bool waitw(uint32_t bar, uint32_t parity, const Abort& ab) {
+  if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+  return waitw_slow(bar, parity, ab);
 }
 
 // After an abort: let the copies of the last `issued` iterations of a ring land (bounded)
@@ -152,7 +175,7 @@ __device__ __forceinline__ bool waitw(uint32_t bar, uint32_t parity, const Abort
 __device__ __forceinline__ void drain(uint32_t full0, int issued) {
   for (int k = (issued > STAGES ? issued - STAGES : 0); k < issued; ++k) {
     const uint64_t t0 = gtimer();
-    while (!mbar_try_wait(full0 + 8 * (k % STAGES), (uint32_t)((k / STAGES) & 1)) && gtimer() - t0 < kWaitNs) {
+    while (!mbar_try_wait_sleep(full0 + 8 * (k % STAGES), (uint32_t)((k / STAGES) & 1)) && gtimer() - t0 < kWaitNs) {
     }
   }
 }
@@ -307,8 +330,8 @@ struct Cfg {
   static constexpr int OFF_ML = OFF_VL + 8 * RV * 4;   // per head (l_j, a_old, a_new, -) [8][4]
   static constexpr int OFF_ST = OFF_ML + 8 * 4 * 4;    // running (m, l) per unit of the item [GMAX][8][2]
   static constexpr int OFF_BAR = OFF_ST + GMAX * 8 * 2 * 4;
-  // barriers: fullA[S], fullB[S], aslot[NA], bslot[2], accf[2], acce[2], pready[2], pfree[2]
-  static constexpr int NBAR = 2 * STAGES + NA + 8;
+  // barriers: fullA[S], fullB[S], aslot[NA], bslot[2], accf[2], acce[2], pready[2], pfree[2], aready[NA]
+  static constexpr int NBAR = 2 * STAGES + 2 * NA + 8;
   static constexpr int OFF_TM = OFF_BAR + NBAR * 8;    // TMEM base address, abort flag
   static constexpr int BYTES = OFF_TM + 16;
   static_assert(STAGE_A % 128 == 0 && STAGE_B % 128 == 0 && OFF_A % 128 == 0 && OFF_BAR % 8 == 0, "alignment");
@@ -357,6 +380,7 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
   const uint32_t b_fullA = bar0, b_fullB = bar0 + 8 * STAGES, b_aslot = bar0 + 16 * STAGES;
   const uint32_t b_bslot = b_aslot + 8 * NA, b_accf = b_bslot + 16, b_acce = b_accf + 16, b_pready = b_acce + 16,
                  b_pfree = b_pready + 16;
+  const uint32_t b_aready = b_pfree + 16;   // A tile (and, for the first, the B tile) converted
   uint32_t* tm_slot = reinterpret_cast<uint32_t*>(sm + C::OFF_TM);
   Abort ab{reinterpret_cast<volatile int*>(sm + C::OFF_TM + 4), reinterpret_cast<int*>(p.ws) - 64};
 
@@ -369,7 +393,10 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
       mbar_init(b_fullA + 8 * s, 1);
       mbar_init(b_fullB + 8 * s, 1);
     }
-    for (int a = 0; a < NA; ++a) mbar_init(b_aslot + 8 * a, 1);
+    for (int a = 0; a < NA; ++a) {
+      mbar_init(b_aslot + 8 * a, 1);
+      mbar_init(b_aready + 8 * a, NCV);
+    }
     for (int b = 0; b < 2; ++b) {
       mbar_init(b_bslot + 8 * b, 1);
       mbar_init(b_accf + 8 * b, 1);
@@ -418,6 +445,7 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       for (int k = 0; k < STAGES && sqB.valid(I); ++k) issueB();
     }
+    __syncwarp();
     float* sVL = reinterpret_cast<float*>(sm + C::OFF_VL);
     float* sML = reinterpret_cast<float*>(sm + C::OFF_ML);
     float* sST = reinterpret_cast<float*>(sm + C::OFF_ST);
@@ -469,6 +497,7 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
           stt[1] = fmaf(lo, ao, l * an);
         }
       }
+      __syncwarp();
       // ---- value basis -> rows padded to QP bytes (conflict-free ldmatrix.trans) -----
       {
         const uint4* src = reinterpret_cast<const uint4*>(st + C::B_BV);
@@ -484,6 +513,7 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
           issueB();
         }
       }
+      __syncwarp();
       // ---- expand once through B_V (mma.sync), merge with the running o --------------
       // o_j[h][d] = l_j * vscale * sum_r (v_lat[h][r] / l_j) B_V[r][d]: the normalised
       // v_lat is a weighted mean of INT8 codes (|.| <= 127), safe as an f16 operand.
@@ -527,124 +557,137 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
           rec[et * (FD + 4) + 1] = stt[1];
         }
       }
+      __syncwarp();
       named_sync(BAR_EPI, NEP);
     }
     if (et == 0 && *ab.flag) drain(b_fullB, issuedB);
     __syncwarp();
   } else if (w >= NCW) {
     // ============================================================= converter warps ===
+    // Warps 8-10 convert: key basis -> B tile, key codes -> FP16 A tiles; each warp
+    // arrives on aready[slot] once its share of a tile is written.  Lane 0 of warp 11
+    // issues the MMAs and the ring-A copies, so conversion never waits behind an issue.
     setmaxnreg_dec<96>();
-    const int pt = tid - PT0;
-    const uint32_t sA_u = smem_u32(sm + C::OFF_A), sB_u = smem_u32(sm + C::OFF_B);
-    Seq sqA = sq;   // ring-A copies run STAGES iterations ahead
-    int issuedA = 0;
-    auto issueA = [&]() {
-      const int s = issuedA % STAGES;
-      const int64_t slot = (int64_t)sqA.unit() * p.NBc + sqA.j();
-      uint8_t* st = sm + C::OFF_RA + s * C::STAGE_A;
-      const uint32_t bar = b_fullA + 8 * s;
-      mbar_expect_tx(bar, C::CK + C::BK);
-      bulk_g2s_hint(smem_u32(st + C::A_CK), p.ck + slot * C::CK, C::CK, bar, stream_policy);
-      bulk_g2s_hint(smem_u32(st + C::A_BK), reinterpret_cast<const uint8_t*>(p.bk) + slot * C::BK, C::BK, bar,
-                    stream_policy);
-      ++issuedA;
-      sqA.next(I);
-    };
-    if (pt == 0) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      for (int k = 0; k < STAGES && sqA.valid(I); ++k) issueA();
-    }
-    int it = 0;
-    int64_t n_issued = 0;   // M-tiles handed to the tensor core
-    for (; sq.valid(I); sq.next(I), ++it) {
-      const int s = it % STAGES;
-      const uint8_t* st = sm + C::OFF_RA + s * C::STAGE_A;
-      const bool ok = waitw(b_fullA + 8 * s, (uint32_t)((it / STAGES) & 1), ab);
-      // key basis [RK][16 chunks] -> B tile [16 n-chunks][RK rows] (conflict-free walk)
-      const int bs = it & 1;
-      bool okb = ok;
-      if (it >= 2) okb = waitw(b_bslot + 8 * bs, (uint32_t)((it / 2 - 1) & 1), ab) && okb;
-      if (okb) {
-        const uint4* srcb = reinterpret_cast<const uint4*>(st + C::A_BK);
-        uint4* dstb = reinterpret_cast<uint4*>(sm + C::OFF_B + bs * C::BK);
-#pragma unroll
-        for (int q = 0; q < RK * 16 / NPT; ++q) {
-          const int idx = q * NPT + pt;
-          const int l = idx & 31, W = idx >> 5, a = l & 7, b = l >> 3;
-          int k, nc;
-          if (RK == 32) {
-            nc = a + 8 * (W & 1);
-            k = 8 * b + ((a + (W >> 1)) & 7);
-          } else {
-            nc = a + 8 * (b >> 1);
-            k = 8 * (b & 1) + ((a + W) & 7);
-          }
-          dstb[nc * RK + k] = srcb[k * 16 + nc];
-        }
-      }
-      // key codes -> FP16 A tiles, one M-tile at a time
-#pragma unroll 1
-      for (int mt = 0; mt < MT; ++mt) {
-        const int64_t n = (int64_t)it * MT + mt;
-        const int as = (int)(n % NA);
-        bool oka = okb;
-        if (n >= NA) oka = waitw(b_aslot + 8 * as, (uint32_t)((n / NA - 1) & 1), ab) && oka;
-        if (oka) {
-          const uint8_t* src = st + C::A_CK + mt * 128 * RK;
-          uint8_t* dst = sm + C::OFF_A + as * C::ATILE;
-#pragma unroll
-          for (int q = 0; q < 128 * (RK / 16) / NPT; ++q) {
-            const int e = q * NPT + pt;
-            const int tau = RK == 32 ? (e >> 1) : e, hf = RK == 32 ? (e & 1) : 0;
-            const uint4 v = *reinterpret_cast<const uint4*>(src + tau * RK + hf * 16);
-            uint4 o0, o1;
-            i8x4_to_h2(v.x, o0.x, o0.y);
-            i8x4_to_h2(v.y, o0.z, o0.w);
-            i8x4_to_h2(v.z, o1.x, o1.y);
-            i8x4_to_h2(v.w, o1.z, o1.w);
-            uint8_t* d = dst + 2 * hf * 2048 + (tau >> 3) * 128 + (tau & 7) * 16;
-            *reinterpret_cast<uint4*>(d) = o0;
-            *reinterpret_cast<uint4*>(d + 2048) = o1;
-          }
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        named_sync(BAR_CONV, NPT);
-        if (pt == 0 && oka && !*ab.flag) {
-          const int b = (int)(n & 1);
-          bool oke = true;
-          if (n >= 2) oke = wait1(b_acce + 8 * b, (uint32_t)((n / 2 - 1) & 1), ab);
-          if (oke) {
-            tc_fence_after();
-            const uint32_t d = tbase + 256u + 128u * (uint32_t)b;
-            const uint32_t a_u = sA_u + as * C::ATILE, b_u = sB_u + bs * C::BK;
-#pragma unroll
-            for (int ks = 0; ks < RK / 16; ++ks) {
-              const uint64_t ad = umma_desc(a_u + ks * 2 * 2048, 2048, 128);
-              const uint64_t bd = umma_desc(b_u + ks * 256, 128, RK * 16);
-              umma_f16(d, ad, bd, ks > 0 ? 1u : 0u);
+    const int wc = w - NCW;
+    if (wc < NCV) {
+      const int ct = tid - PT0;   // 0 .. 32 NCV - 1
+      int it = 0;
+      for (; sq.valid(I); sq.next(I), ++it) {
+        const int s = it % STAGES;
+        const uint8_t* st = sm + C::OFF_RA + s * C::STAGE_A;
+        bool ok = waitw(b_fullA + 8 * s, (uint32_t)((it / STAGES) & 1), ab);
+        // key basis [RK][16 chunks] -> B tile [16 n-chunks][RK rows] (conflict-free walk)
+        const int bs = it & 1;
+        if (it >= 2) ok = waitw(b_bslot + 8 * bs, (uint32_t)((it / 2 - 1) & 1), ab) && ok;
+        if (ok) {
+          const uint4* srcb = reinterpret_cast<const uint4*>(st + C::A_BK);
+          uint4* dstb = reinterpret_cast<uint4*>(sm + C::OFF_B + bs * C::BK);
+          for (int idx = ct; idx < RK * 16; idx += NCV * 32) {
+            const int l = idx & 31, W = idx >> 5, a = l & 7, b = l >> 3;
+            int k, nc;
+            if (RK == 32) {
+              nc = a + 8 * (W & 1);
+              k = 8 * b + ((a + (W >> 1)) & 7);
+            } else {
+              nc = a + 8 * (b >> 1);
+              k = 8 * (b & 1) + ((a + W) & 7);
             }
-            umma_commit(b_accf + 8 * b);
-            umma_commit(b_aslot + 8 * as);
-            if (mt == MT - 1) umma_commit(b_bslot + 8 * bs);
-            n_issued = n + 1;
+            dstb[nc * RK + k] = srcb[k * 16 + nc];
           }
         }
-        __syncwarp();
+        // key codes -> FP16 A tiles, one M-tile at a time
+#pragma unroll 1
+        for (int mt = 0; mt < MT; ++mt) {
+          const int64_t n = (int64_t)it * MT + mt;
+          const int as = (int)(n % NA);
+          bool oka = ok;
+          if (n >= NA) oka = waitw(b_aslot + 8 * as, (uint32_t)((n / NA - 1) & 1), ab) && oka;
+          if (oka) {
+            const uint8_t* src = st + C::A_CK + mt * 128 * RK;
+            uint8_t* dst = sm + C::OFF_A + as * C::ATILE;
+            for (int e = ct; e < 128 * (RK / 16); e += NCV * 32) {
+              const int tau = RK == 32 ? (e >> 1) : e, hf = RK == 32 ? (e & 1) : 0;
+              const uint4 v = *reinterpret_cast<const uint4*>(src + tau * RK + hf * 16);
+              uint4 o0, o1;
+              i8x4_to_h2(v.x, o0.x, o0.y);
+              i8x4_to_h2(v.y, o0.z, o0.w);
+              i8x4_to_h2(v.z, o1.x, o1.y);
+              i8x4_to_h2(v.w, o1.z, o1.w);
+              uint8_t* d = dst + 2 * hf * 2048 + (tau >> 3) * 128 + (tau & 7) * 16;
+              *reinterpret_cast<uint4*>(d) = o0;
+              *reinterpret_cast<uint4*>(d + 2048) = o1;
+            }
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) mbar_arrive(b_aready + 8 * as);
+          __syncwarp();
+        }
       }
-      // stage s of ring A is converted: refill it
-      if (pt == 0 && sqA.valid(I) && !*ab.flag) issueA();
+    } else {
+      // ---- MMA issuer (lane 0 of warp 11) --------------------------------------------
+      if (lane == 0) {
+        const uint32_t sA_u = smem_u32(sm + C::OFF_A), sB_u = smem_u32(sm + C::OFF_B);
+        Seq sqA = sq;   // ring-A copies run STAGES iterations ahead
+        int issuedA = 0;
+        auto issueA = [&]() {
+          const int s = issuedA % STAGES;
+          const int64_t slot = (int64_t)sqA.unit() * p.NBc + sqA.j();
+          uint8_t* st = sm + C::OFF_RA + s * C::STAGE_A;
+          const uint32_t bar = b_fullA + 8 * s;
+          mbar_expect_tx(bar, C::CK + C::BK);
+          bulk_g2s_hint(smem_u32(st + C::A_CK), p.ck + slot * C::CK, C::CK, bar, stream_policy);
+          bulk_g2s_hint(smem_u32(st + C::A_BK), reinterpret_cast<const uint8_t*>(p.bk) + slot * C::BK, C::BK, bar,
+                        stream_policy);
+          ++issuedA;
+          sqA.next(I);
+        };
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        for (int k = 0; k < STAGES && sqA.valid(I); ++k) issueA();
+        int it = 0;
+        int64_t n_issued = 0;   // M-tiles handed to the tensor core
+        for (; sq.valid(I); sq.next(I), ++it) {
+          const int bs = it & 1;
+#pragma unroll 1
+          for (int mt = 0; mt < MT; ++mt) {
+            const int64_t n = (int64_t)it * MT + mt;
+            const int as = (int)(n % NA), b = (int)(n & 1);
+            bool ok = wait1(b_aready + 8 * as, (uint32_t)((n / NA) & 1), ab);
+            if (n >= 2) ok = wait1(b_acce + 8 * b, (uint32_t)((n / 2 - 1) & 1), ab) && ok;
+            if (ok && !*ab.flag) {
+              tc_fence_after();
+              const uint32_t d = tbase + 256u + 128u * (uint32_t)b;
+              const uint32_t a_u = sA_u + as * C::ATILE, b_u = sB_u + bs * C::BK;
+#pragma unroll
+              for (int ks = 0; ks < RK / 16; ++ks) {
+                const uint64_t ad = umma_desc(a_u + ks * 2 * 2048, 2048, 128);
+                const uint64_t bd = umma_desc(b_u + ks * 256, 128, RK * 16);
+                umma_f16(d, ad, bd, ks > 0 ? 1u : 0u);
+              }
+              umma_commit(b_accf + 8 * b);
+              umma_commit(b_aslot + 8 * as);
+              if (mt == MT - 1) umma_commit(b_bslot + 8 * bs);
+              n_issued = n + 1;
+            }
+          }
+          // every converter warp has finished with stage it % STAGES of ring A: refill it
+          if (sqA.valid(I) && !*ab.flag) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issueA();
+          }
+        }
+        if (*ab.flag) {
+          drain(b_fullA, issuedA);
+          if (n_issued > 0) {   // the last MMAs handed to the tensor core
+            const int64_t n = n_issued - 1;
+            const uint64_t t0 = gtimer();
+            while (!mbar_try_wait_sleep(b_accf + 8 * (n & 1), (uint32_t)((n / 2) & 1)) && gtimer() - t0 < kWaitNs) {
+            }
+          }
+        }
+      }
       __syncwarp();
     }
-    if (pt == 0 && *ab.flag) {
-      drain(b_fullA, issuedA);
-      if (n_issued > 0) {   // the last MMAs handed to the tensor core
-        const int64_t n = n_issued - 1;
-        const uint64_t t0 = gtimer();
-        while (!mbar_try_wait(b_accf + 8 * (n & 1), (uint32_t)((n / 2) & 1)) && gtimer() - t0 < kWaitNs) {
-        }
-      }
-    }
-    __syncwarp();
   } else {
     // ============================================================== consumer warps ===
     setmaxnreg_inc<160>();
@@ -702,6 +745,7 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(b_acce + 8 * (int)(n & 1));
+        __syncwarp();
       }
 #pragma unroll
       for (int i = 0; i < MT; ++i) {
@@ -735,6 +779,7 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(b_acce + 8 * (int)(n1 & 1));
+          __syncwarp();
         }
       }
       // ---- per-warp softmax over its tokens (log2 domain) ------------------------------
@@ -816,6 +861,7 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(b_pready + 8 * b2);
+      __syncwarp();
     }
   }
   tc_fence_before();
