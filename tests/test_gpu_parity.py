@@ -391,6 +391,29 @@ def test_fast_kernel_matches_oracle_and_generic(case, mode, generic_path):
     generic_path(False)
 
 
+# (case, plan): plans drive several items and multi-block ranges through one CTA, the
+# way large workloads run (units per item, blocks per range, CTAs)
+PLAN_CASES = [
+    ((51, 3, 4, 4, 128, 512, 6, 32, 32, 9, False), "4,3,2"),     # 3 items per CTA, 3-block ranges
+    ((52, 3, 4, 4, 128, 512, 6, 32, 32, 9, False), "5,2,3"),     # ragged last group of units
+    ((53, 2, 4, 2, 128, 512, 5, 16, 32, 0, False), "8,5,1"),     # one CTA merges all blocks
+    ((54, 2, 4, 8, 128, 256, 7, 32, 16, 3, False), "3,4,2"),     # two M-tiles, ragged last range
+]
+
+
+@pytest.mark.parametrize("case,plan", PLAN_CASES)
+def test_fast_kernel_multi_item_plans(case, plan, generic_path, monkeypatch):
+    r = _random_case(*case)
+    monkeypatch.setenv("SPX_FAST_PLAN", plan)
+    generic_path(False)
+    fast, ref = _run_random(r, torch.float16, "decode")
+    _close(fast, ref)
+    generic_path(True)
+    gen, _ = _run_random(r, torch.float16, "decode")
+    _close(fast, gen)
+    generic_path(False)
+
+
 def test_fast_kernel_long_context_properties(generic_path):
     """A 16-block (8K-token) cache at k=32: fast and generic CUDA paths agree, the
     output is a convex combination of values (softmax weights), and the result is

@@ -28,6 +28,8 @@
 // workspace error word, after which all waits return at once and no new copies or MMAs
 // are issued, so every role still reaches each named barrier and the CTA exits.
 #include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
 
 #include "spx_common.cuh"
 #include "spx_decode.cuh"
@@ -76,11 +78,12 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t a, uint32_t bytes) {
 __device__ __forceinline__ void mbar_arrive(uint32_t a) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(a) : "memory");
 }
+// Non-blocking test of a phase (the common, already-completed case of every wait).
 __device__ __forceinline__ bool mbar_try_wait(uint32_t a, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(a), "r"(parity)
@@ -644,6 +647,9 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
         };
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         for (int k = 0; k < STAGES && sqA.valid(I); ++k) issueA();
+        // descriptors of A slot 0 / B slot 0, k-step 0; other slots and k-steps differ
+        // only in the start-address field (address >> 4 in the low 14 bits)
+        const uint64_t ad0 = umma_desc(sA_u, 2048, 128), bd0 = umma_desc(sB_u, 128, RK * 16);
         int it = 0;
         int64_t n_issued = 0;   // M-tiles handed to the tensor core
         for (; sq.valid(I); sq.next(I), ++it) {
@@ -652,18 +658,18 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
           for (int mt = 0; mt < MT; ++mt) {
             const int64_t n = (int64_t)it * MT + mt;
             const int as = (int)(n % NA), b = (int)(n & 1);
-            bool ok = wait1(b_aready + 8 * as, (uint32_t)((n / NA) & 1), ab);
-            if (n >= 2) ok = wait1(b_acce + 8 * b, (uint32_t)((n / 2 - 1) & 1), ab) && ok;
+            // test both barriers at once; sleep on whichever is not there yet
+            const bool ra = mbar_try_wait(b_aready + 8 * as, (uint32_t)((n / NA) & 1));
+            const bool re = n < 2 || mbar_try_wait(b_acce + 8 * b, (uint32_t)((n / 2 - 1) & 1));
+            bool ok = ra || wait1(b_aready + 8 * as, (uint32_t)((n / NA) & 1), ab);
+            if (!re) ok = wait1(b_acce + 8 * b, (uint32_t)((n / 2 - 1) & 1), ab) && ok;
             if (ok && !*ab.flag) {
               tc_fence_after();
               const uint32_t d = tbase + 256u + 128u * (uint32_t)b;
-              const uint32_t a_u = sA_u + as * C::ATILE, b_u = sB_u + bs * C::BK;
+              const uint64_t ad = ad0 + (uint64_t)((as * C::ATILE) >> 4), bd = bd0 + (uint64_t)((bs * C::BK) >> 4);
 #pragma unroll
-              for (int ks = 0; ks < RK / 16; ++ks) {
-                const uint64_t ad = umma_desc(a_u + ks * 2 * 2048, 2048, 128);
-                const uint64_t bd = umma_desc(b_u + ks * 256, 128, RK * 16);
-                umma_f16(d, ad, bd, ks > 0 ? 1u : 0u);
-              }
+              for (int ks = 0; ks < RK / 16; ++ks)
+                umma_f16(d, ad + (uint64_t)((ks * 2 * 2048) >> 4), bd + (uint64_t)((ks * 256) >> 4), ks > 0 ? 1u : 0u);
               umma_commit(b_accf + 8 * b);
               umma_commit(b_aslot + 8 * as);
               if (mt == MT - 1) umma_commit(b_bslot + 8 * bs);
@@ -915,8 +921,27 @@ static int num_sms() {
 struct Plan {
   int G, JR, ngroups, nranges, nitems, grid;
 };
+static Plan make_plan(int units, int nblk, int G, int JR, int sms) {
+  const int Gu = G < units ? G : units;
+  const int ngroups = (units + Gu - 1) / Gu;
+  const int nranges = (nblk + JR - 1) / JR;
+  const int items = ngroups * nranges;
+  return Plan{Gu, JR, ngroups, nranges, items, items < sms ? items : sms};
+}
+// SPX_FAST_PLAN="G,JR,CTAS" fixes units per item (<= 32), blocks per range and the
+// persistent grid (a tuning knob; the tests use it to drive several items and block
+// ranges through one CTA on small inputs).
+static bool plan_override(int units, int nblk, Plan* out) {
+  const char* e = getenv("SPX_FAST_PLAN");
+  int G = 0, JR = 0, ctas = 0;
+  if (!e || sscanf(e, "%d,%d,%d", &G, &JR, &ctas) != 3) return false;
+  if (G < 1 || G > GMAX || JR < 1 || ctas < 1) return false;
+  *out = make_plan(units, nblk, G, JR < nblk ? JR : nblk, ctas);
+  return true;
+}
 static Plan plan(int units, int nblk, int sms) {
   Plan best{};
+  if (plan_override(units, nblk, &best)) return best;
   long best_cost = -1;
   for (int G : {32, 16, 8}) {
     const int Gu = G < units ? G : units;
@@ -930,7 +955,7 @@ static Plan plan(int units, int nblk, int sms) {
       const long cost = rounds * Gu * JR;
       if (best_cost < 0 || cost < best_cost) {
         best_cost = cost;
-        best = Plan{Gu, JR, ngroups, nranges, (int)items, (int)(items < sms ? items : sms)};
+        best = make_plan(units, nblk, Gu, JR, sms);
       }
     }
   }
