@@ -39,7 +39,7 @@ namespace fastk {
 
 constexpr int FD = 128;
 constexpr int STAGES = 3;
-constexpr int NA = 3;                      // A-tile slots (one M-tile each)
+constexpr int NA = 2;                      // A-tile slots, paired with the two TMEM accumulators
 constexpr int NCW = 8;                     // consumer warps (warpgroups 0, 1)
 constexpr int NPW = 4;                     // converter warps (warpgroup 2)
 constexpr int NEW = 4;                     // epilogue warps (warpgroup 3)
@@ -333,8 +333,8 @@ struct Cfg {
   static constexpr int OFF_ML = OFF_VL + 8 * RV * 4;   // per head (l_j, a_old, a_new, -) [8][4]
   static constexpr int OFF_ST = OFF_ML + 8 * 4 * 4;    // running (m, l) per unit of the item [GMAX][8][2]
   static constexpr int OFF_BAR = OFF_ST + GMAX * 8 * 2 * 4;
-  // barriers: fullA[S], fullB[S], aslot[NA], bslot[2], accf[2], acce[2], pready[2], pfree[2], aready[NA]
-  static constexpr int NBAR = 2 * STAGES + 2 * NA + 8;
+  // barriers: fullA[S], fullB[S], bslot[2], accf[2], acce[2], pready[2], pfree[2], aready[NA]
+  static constexpr int NBAR = 2 * STAGES + NA + 10;
   static constexpr int OFF_TM = OFF_BAR + NBAR * 8;    // TMEM base address, abort flag
   static constexpr int BYTES = OFF_TM + 16;
   static_assert(STAGE_A % 128 == 0 && STAGE_B % 128 == 0 && OFF_A % 128 == 0 && OFF_BAR % 8 == 0, "alignment");
@@ -380,8 +380,8 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
   const int g = lane >> 2, t = lane & 3;
   const int nrep = p.nrep;
   const uint32_t bar0 = smem_u32(sm + C::OFF_BAR);
-  const uint32_t b_fullA = bar0, b_fullB = bar0 + 8 * STAGES, b_aslot = bar0 + 16 * STAGES;
-  const uint32_t b_bslot = b_aslot + 8 * NA, b_accf = b_bslot + 16, b_acce = b_accf + 16, b_pready = b_acce + 16,
+  const uint32_t b_fullA = bar0, b_fullB = bar0 + 8 * STAGES;
+  const uint32_t b_bslot = bar0 + 16 * STAGES, b_accf = b_bslot + 16, b_acce = b_accf + 16, b_pready = b_acce + 16,
                  b_pfree = b_pready + 16;
   const uint32_t b_aready = b_pfree + 16;   // A tile (and, for the first, the B tile) converted
   uint32_t* tm_slot = reinterpret_cast<uint32_t*>(sm + C::OFF_TM);
@@ -396,10 +396,7 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
       mbar_init(b_fullA + 8 * s, 1);
       mbar_init(b_fullB + 8 * s, 1);
     }
-    for (int a = 0; a < NA; ++a) {
-      mbar_init(b_aslot + 8 * a, 1);
-      mbar_init(b_aready + 8 * a, NCV);
-    }
+    for (int a = 0; a < NA; ++a) mbar_init(b_aready + 8 * a, NCV);
     for (int b = 0; b < 2; ++b) {
       mbar_init(b_bslot + 8 * b, 1);
       mbar_init(b_accf + 8 * b, 1);
@@ -602,9 +599,11 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
 #pragma unroll 1
         for (int mt = 0; mt < MT; ++mt) {
           const int64_t n = (int64_t)it * MT + mt;
-          const int as = (int)(n % NA);
+          // A slot n & 1 is free once M-tile n - 2, the last one read from it, is done:
+          // that is the completion of accumulator n & 1's previous phase
+          const int as = (int)(n & 1);
           bool oka = ok;
-          if (n >= NA) oka = waitw(b_aslot + 8 * as, (uint32_t)((n / NA - 1) & 1), ab) && oka;
+          if (n >= 2) oka = waitw(b_accf + 8 * as, (uint32_t)(((n - 2) / 2) & 1), ab) && oka;
           if (oka) {
             const uint8_t* src = st + C::A_CK + mt * 128 * RK;
             uint8_t* dst = sm + C::OFF_A + as * C::ATILE;
@@ -657,11 +656,11 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
 #pragma unroll 1
           for (int mt = 0; mt < MT; ++mt) {
             const int64_t n = (int64_t)it * MT + mt;
-            const int as = (int)(n % NA), b = (int)(n & 1);
+            const int as = (int)(n & 1), b = as;
             // test both barriers at once; sleep on whichever is not there yet
-            const bool ra = mbar_try_wait(b_aready + 8 * as, (uint32_t)((n / NA) & 1));
+            const bool ra = mbar_try_wait(b_aready + 8 * as, (uint32_t)((n / 2) & 1));
             const bool re = n < 2 || mbar_try_wait(b_acce + 8 * b, (uint32_t)((n / 2 - 1) & 1));
-            bool ok = ra || wait1(b_aready + 8 * as, (uint32_t)((n / NA) & 1), ab);
+            bool ok = ra || wait1(b_aready + 8 * as, (uint32_t)((n / 2) & 1), ab);
             if (!re) ok = wait1(b_acce + 8 * b, (uint32_t)((n / 2 - 1) & 1), ab) && ok;
             if (ok && !*ab.flag) {
               tc_fence_after();
@@ -671,7 +670,6 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
               for (int ks = 0; ks < RK / 16; ++ks)
                 umma_f16(d, ad + (uint64_t)((ks * 2 * 2048) >> 4), bd + (uint64_t)((ks * 256) >> 4), ks > 0 ? 1u : 0u);
               umma_commit(b_accf + 8 * b);
-              umma_commit(b_aslot + 8 * as);
               if (mt == MT - 1) umma_commit(b_bslot + 8 * bs);
               n_issued = n + 1;
             }
