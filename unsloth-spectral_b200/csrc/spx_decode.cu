@@ -149,25 +149,32 @@ __global__ void __launch_bounds__(256) hot_merge_kernel(DecodeParams p) {
   float* ssc = sq + nrep * D;       // [nrep][hot]
   float* sml = ssc + nrep * hot;    // [nrep][2]
   float* swt = sml + 2 * nrep;      // [nrep][nc + 1] merge weights, then 1/L
+  float* sred = swt + nrep * (nc + 1);   // [slices][nrep][D] partial value sums
+  int* spos = reinterpret_cast<int*>(sred + (blockDim.x / D) * nrep * D);   // [hot] clamped table rows
   const int64_t lbg = (int64_t)lb * p.H + g;
   const T* q = reinterpret_cast<const T*>(p.q) + ((int64_t)lb * p.Hq + (int64_t)g * nrep) * D;
   for (int i = tid; i < nrep * D; i += blockDim.x) sq[i] = to_f(q[i]);
+  for (int t = tid; t < hot; t += blockDim.x) {
+    const int64_t a = p.hpos[t];
+    spos[t] = (int)(a < 0 ? 0 : (a >= p.rope_len ? p.rope_len - 1 : a));
+  }
   // a cold-tier kernel that gave up waiting marks the workspace header: report NaN
   const bool cold_failed = nb > 0 && reinterpret_cast<const int*>(p.ws)[-64] != 0;
   __syncthreads();
   const T* hk = reinterpret_cast<const T*>(p.hk) + lbg * p.HC * D;
   const T* hv = reinterpret_cast<const T*>(p.hv) + lbg * p.HC * D;
   const bool second_half = (p.mode == SPX_ROPE_ABSOLUTE) && !p.tied;
-  for (int t = tid; t < hot; t += blockDim.x) {
-    int64_t a = p.hpos[t];
-    a = a < 0 ? 0 : (a >= p.rope_len ? p.rope_len - 1 : a);
+  // scores: one warp per hot token, lanes over the rotation pairs (coalesced rows)
+#pragma unroll 2
+  for (int t = warp; t < hot; t += nwarps) {
+    const int64_t a = spos[t];
     const float* cr = p.cosT + a * D;
     const float* sr = p.sinT + a * D;
     const T* krow = hk + (int64_t)t * D;
     float s[kMaxRep];
 #pragma unroll
     for (int h = 0; h < kMaxRep; ++h) s[h] = 0.f;
-    for (int i = 0; i < half; ++i) {
+    for (int i = lane; i < half; i += 32) {
       const float k1 = to_f(krow[i]), k2 = to_f(krow[i + half]);
       const float c1 = cr[i], s1 = sr[i];
       const float c2 = second_half ? cr[i + half] : c1;
@@ -181,10 +188,10 @@ __global__ void __launch_bounds__(256) hot_merge_kernel(DecodeParams p) {
 #pragma unroll
     for (int h = 0; h < kMaxRep; ++h) {
       if (h < nrep) {
-        float v = s[h] * p.scale;
+        float v = warp_sum(s[h]) * p.scale;
         if (p.mask && p.mask[((int64_t)b * p.Hq + g * nrep + h) * p.mask_stride + (int64_t)nb * p.Tb + t] == 0)
           v = -INFINITY;
-        ssc[h * hot + t] = v;
+        if (lane == 0) ssc[h * hot + t] = v;
       }
     }
   }
@@ -223,10 +230,31 @@ __global__ void __launch_bounds__(256) hot_merge_kernel(DecodeParams p) {
   __syncthreads();
   T* out = reinterpret_cast<T*>(p.out) + ((int64_t)lb * p.Hq + (int64_t)g * nrep) * D;
   const float* recs = p.ws + (lbg * p.nparts) * nrep * (int64_t)(D + 4);
+  // hot values: thread (slice, d) reads each V element once for every head of the group
+  {
+    const int slices = blockDim.x / D;
+    const int sl = tid / D, d = tid - sl * D;
+    if (sl < slices) {
+      float acc[kMaxRep];
+#pragma unroll
+      for (int h = 0; h < kMaxRep; ++h) acc[h] = 0.f;
+#pragma unroll 4
+      for (int t = sl; t < hot; t += slices) {
+        const float v = to_f(hv[(int64_t)t * D + d]);
+#pragma unroll
+        for (int h = 0; h < kMaxRep; ++h)
+          if (h < nrep) acc[h] = fmaf(ssc[h * hot + t], v, acc[h]);
+      }
+#pragma unroll
+      for (int h = 0; h < kMaxRep; ++h)
+        if (h < nrep) sred[(sl * nrep + h) * D + d] = acc[h];
+    }
+  }
+  __syncthreads();
   for (int e = tid; e < nrep * D; e += blockDim.x) {
     const int h = e / D, d = e - h * D;
     float acc = 0.f;
-    for (int t = 0; t < hot; ++t) acc = fmaf(ssc[h * hot + t], to_f(hv[(int64_t)t * D + d]), acc);
+    for (int sl = 0; sl < (int)(blockDim.x / D); ++sl) acc += sred[(sl * nrep + h) * D + d];
     acc *= sml[2 * h];
     for (int jj = 0; jj < nc; ++jj) acc = fmaf(swt[h * (nc + 1) + jj], recs[((int64_t)jj * nrep + h) * (D + 4) + 4 + d], acc);
     out[(int64_t)h * D + d] = from_f<T>(cold_failed ? NAN : acc * sml[2 * h + 1]);
@@ -257,7 +285,8 @@ static int launch_cold(const DecodeParams& p, cudaStream_t st) {
 
 template <typename T>
 static int launch_hot_merge(const DecodeParams& p, cudaStream_t st) {
-  const size_t smem = ((size_t)p.nrep * p.D + (size_t)p.nrep * p.hot + 2 * p.nrep + (size_t)p.nrep * (p.nblk + 1)) *
+  const size_t smem = ((size_t)p.nrep * p.D + (size_t)p.nrep * p.hot + 2 * p.nrep + (size_t)p.nrep * (p.nblk + 1) +
+                       (size_t)(256 / p.D) * p.nrep * p.D + (size_t)p.hot) *
                       sizeof(float);
   SPX_REQUIRE(smem <= kMaxSmem, SPX_ERR_UNSUPPORTED,
               "hot tier of %d tokens with %d blocks needs %zu bytes of shared memory", p.hot, p.nblk, smem);
