@@ -142,6 +142,110 @@ __global__ void __launch_bounds__(256) orth_kernel(float* __restrict__ X, int ro
   for (int e = threadIdx.x; e < rows * r; e += blockDim.x) Xi[e] = sx[e];
 }
 
+// ---------------------------------------- in-place Cholesky-QR orthonormalisation
+// X: f32 [rows][r] per matrix, one CTA per matrix.  Each pass forms the Gram matrix
+// G = X^T X in float64 (products of two float32 values are exact in float64), factors
+// G = L L^T with one warp, and solves X := X L^{-T} row by row.  Two passes give an
+// orthonormal basis to float32 accuracy while cond(X) <= ~1e6; a third pass runs when
+// the first one saw a larger pivot spread.  A pivot at rounding level of a zero column
+// (relative 1e-30) leaves that column zero, as classical Gram-Schmidt does.
+// Shared memory: G [r][r] f64, L [r][r] f32 (inverse diagonal on the diagonal),
+// X [rows][r | 1] f32 (odd pitch: the row-parallel solve is bank-conflict free).
+size_t cholqr_smem(int rows, int r) {
+  return (size_t)r * r * 8 + (size_t)r * r * 4 + (size_t)rows * (r | 1) * 4;
+}
+
+__global__ void __launch_bounds__(256) cholqr_kernel(float* __restrict__ X, int rows, int r) {
+  extern __shared__ double smd[];
+  double* G = smd;                                       // [r][r]
+  float* Lf = reinterpret_cast<float*>(G + r * r);       // [r][r]
+  const int rp = r | 1;
+  float* sx = Lf + r * r;                                // [rows][rp]
+  __shared__ int third;
+  const int i = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float* Xi = X + (int64_t)i * rows * r;
+  for (int e = tid; e < rows * r; e += blockDim.x) {
+    const int t = e / r, c = e - t * r;
+    sx[t * rp + c] = Xi[e];
+  }
+  if (tid == 0) third = 0;
+  __syncthreads();
+  const int nb2 = (r + 1) >> 1;                // 2x2 tiles of G per side
+  for (int pass = 0; pass < 3; ++pass) {
+    if (pass == 2 && !third) break;
+    // ---- Gram, upper triangle by 2x2 tiles ---------------------------------------
+    for (int tb = tid; tb < nb2 * (nb2 + 1) / 2; tb += blockDim.x) {
+      int ta = 0, rem = tb;
+      while (rem >= nb2 - ta) {   // tile (ta, tb') with ta <= tb'
+        rem -= nb2 - ta;
+        ++ta;
+      }
+      const int a0 = 2 * ta, b0 = 2 * (ta + rem);
+      const int a1 = a0 + 1 < r ? a0 + 1 : a0, b1 = b0 + 1 < r ? b0 + 1 : b0;
+      double g00 = 0.0, g01 = 0.0, g10 = 0.0, g11 = 0.0;
+      for (int t = 0; t < rows; ++t) {
+        const float* xr = sx + t * rp;
+        const double xa0 = xr[a0], xa1 = xr[a1], xb0 = xr[b0], xb1 = xr[b1];
+        g00 = fma(xa0, xb0, g00);
+        g01 = fma(xa0, xb1, g01);
+        g10 = fma(xa1, xb0, g10);
+        g11 = fma(xa1, xb1, g11);
+      }
+      G[a0 * r + b0] = g00; G[b0 * r + a0] = g00;
+      if (b1 != b0) { G[a0 * r + b1] = g01; G[b1 * r + a0] = g01; }
+      if (a1 != a0) { G[a1 * r + b0] = g10; G[b0 * r + a1] = g10; }
+      if (a1 != a0 && b1 != b0) { G[a1 * r + b1] = g11; G[b1 * r + a1] = g11; }
+    }
+    __syncthreads();
+    // ---- Cholesky G = L L^T (right-looking, one warp) -----------------------------
+    if (warp == 0) {
+      double dmax = 0.0;
+      for (int j = lane; j < r; j += 32) dmax = fmax(dmax, G[j * r + j]);
+      for (int o = 16; o > 0; o >>= 1) dmax = fmax(dmax, __shfl_xor_sync(0xffffffffu, dmax, o));
+      double pmin = 1e300, pmax = 0.0;
+      for (int j = 0; j < r; ++j) {
+        const double piv = G[j * r + j];
+        const bool ok = piv > 1e-30 * dmax && dmax > 0.0;
+        const double d = ok ? sqrt(piv) : 0.0;
+        if (ok) {
+          pmin = fmin(pmin, piv);
+          pmax = fmax(pmax, piv);
+        }
+        for (int a = j + 1 + lane; a < r; a += 32) G[a * r + j] = ok ? G[a * r + j] / d : 0.0;
+        __syncwarp();
+        // trailing update of the lower triangle: G[a][c] -= L[a][j] L[c][j], j < c <= a
+        for (int a = j + 1 + lane; a < r; a += 32) {
+          const double la = G[a * r + j];
+          for (int c = j + 1; c <= a; ++c) G[a * r + c] = fma(-la, G[c * r + j], G[a * r + c]);
+        }
+        if (lane == 0) Lf[j * r + j] = ok ? (float)(1.0 / d) : 0.f;
+        __syncwarp();
+      }
+      for (int e = lane; e < r * r; e += 32) {
+        const int a = e / r, c = e - a * r;
+        if (c < a) Lf[e] = (float)G[e];
+      }
+      if (lane == 0 && pass == 0 && pmax > 1e12 * pmin) third = 1;
+    }
+    __syncthreads();
+    // ---- X := X L^{-T}, one row per thread ------------------------------------------
+    for (int t = tid; t < rows; t += blockDim.x) {
+      float* xr = sx + t * rp;
+      for (int j = 0; j < r; ++j) {
+        float v = xr[j];
+        const float* lj = Lf + j * r;
+        for (int c = 0; c < j; ++c) v = fmaf(-xr[c], lj[c], v);
+        xr[j] = v * lj[j];
+      }
+    }
+    __syncthreads();
+  }
+  for (int e = tid; e < rows * r; e += blockDim.x) {
+    const int t = e / r, c = e - t * r;
+    Xi[e] = sx[t * rp + c];
+  }
+}
+
 // ----------------------------------------------- small SVD through a Jacobi eigensolve
 // Z = Bp^T: f32 [n][r].  Outputs Wk f32 [r][k], S f32 [k], Vh f32 [k][n].
 __global__ void __launch_bounds__(256) small_svd_kernel(const float* __restrict__ Z, float* __restrict__ Wk,
@@ -152,11 +256,11 @@ __global__ void __launch_bounds__(256) small_svd_kernel(const float* __restrict_
   double* G = smd;                    // [rp][rp]
   double* W = G + rp * rp;            // [rp][rp]
   double* cs = W + rp * rp;           // [rp/2][2]
-  int* pairs = reinterpret_cast<int*>(cs + rp);   // [rp]
+  int* pairs = reinterpret_cast<int*>(cs + rp);   // [rp] (round-robin pairs of this round)
   int* perm = pairs + rp;                          // [rp]
   float* sz = reinterpret_cast<float*>(perm + rp); // [n][r]
   __shared__ double off_s[32];
-  __shared__ int done;
+  __shared__ int done, rotated;
   const int i = blockIdx.x;
   const float* Zi = Z + (int64_t)i * n * r;
   for (int e = threadIdx.x; e < n * r; e += blockDim.x) sz[e] = Zi[e];
@@ -171,20 +275,29 @@ __global__ void __launch_bounds__(256) small_svd_kernel(const float* __restrict_
     G[e] = g;
     W[e] = (a == b) ? 1.0 : 0.0;
   }
-  if (threadIdx.x < rp) pairs[threadIdx.x] = threadIdx.x;
   if (threadIdx.x == 0) done = 0;
   __syncthreads();
   const int np = rp / 2;
+  // a rotation is skipped once |G_pq| <= 1e-13 sqrt(|G_pp G_qq|) (far below what the
+  // float32 outputs resolve); a sweep without rotations ends the iteration
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   for (int sweep = 0; sweep < 30 && !done; ++sweep) {
+    if (threadIdx.x == 0) rotated = 0;
+    __syncthreads();
     for (int round = 0; round < rp - 1; ++round) {
-      // pair u couples pairs[u] and pairs[rp-1-u]
+      // circle method: index rp-1 is fixed and meets `round`; pair u >= 1 couples
+      // (round + u) and (round - u) modulo rp - 1.  Every pair meets once per sweep.
       if (threadIdx.x < np) {
-        int p = pairs[threadIdx.x], q = pairs[rp - 1 - threadIdx.x];
+        const int u = threadIdx.x, nn = rp - 1;
+        int p = u == 0 ? round : (round + u) % nn;
+        int q = u == 0 ? nn : (round - u + nn) % nn;
         if (p > q) { const int tmp = p; p = q; q = tmp; }
+        pairs[2 * u] = p;
+        pairs[2 * u + 1] = q;
         double c = 1.0, s = 0.0;
         const double apq = G[p * rp + q];
-        if (q < r && fabs(apq) > 1e-300) {
+        if (q < r && fabs(apq) > 1e-300 && fabs(apq) > 1e-13 * sqrt(fabs(G[p * rp + p] * G[q * rp + q]))) {
+          rotated = 1;
           const double tau = (G[q * rp + q] - G[p * rp + p]) / (2.0 * apq);
           const double t = (tau >= 0 ? 1.0 : -1.0) / (fabs(tau) + sqrt(1.0 + tau * tau));
           c = 1.0 / sqrt(1.0 + t * t);
@@ -197,8 +310,7 @@ __global__ void __launch_bounds__(256) small_svd_kernel(const float* __restrict_
       // rows: new_p = c row_p - s row_q ; new_q = s row_p + c row_q
       for (int e = threadIdx.x; e < np * rp; e += blockDim.x) {
         const int u = e / rp, col = e - u * rp;
-        int p = pairs[u], q = pairs[rp - 1 - u];
-        if (p > q) { const int tmp = p; p = q; q = tmp; }
+        const int p = pairs[2 * u], q = pairs[2 * u + 1];
         const double c = cs[2 * u], s = cs[2 * u + 1];
         const double gp = G[p * rp + col], gq = G[q * rp + col];
         G[p * rp + col] = c * gp - s * gq;
@@ -208,8 +320,7 @@ __global__ void __launch_bounds__(256) small_svd_kernel(const float* __restrict_
       // columns of G and W
       for (int e = threadIdx.x; e < np * rp; e += blockDim.x) {
         const int u = e / rp, row = e - u * rp;
-        int p = pairs[u], q = pairs[rp - 1 - u];
-        if (p > q) { const int tmp = p; p = q; q = tmp; }
+        const int p = pairs[2 * u], q = pairs[2 * u + 1];
         const double c = cs[2 * u], s = cs[2 * u + 1];
         const double gp = G[row * rp + p], gq = G[row * rp + q];
         G[row * rp + p] = c * gp - s * gq;
@@ -217,13 +328,6 @@ __global__ void __launch_bounds__(256) small_svd_kernel(const float* __restrict_
         const double wp = W[row * rp + p], wq = W[row * rp + q];
         W[row * rp + p] = c * wp - s * wq;
         W[row * rp + q] = s * wp + c * wq;
-      }
-      __syncthreads();
-      // rotate the tournament: keep pairs[0], shift the rest by one
-      if (threadIdx.x == 0) {
-        const int last = pairs[rp - 1];
-        for (int u = rp - 1; u > 1; --u) pairs[u] = pairs[u - 1];
-        pairs[1] = last;
       }
       __syncthreads();
     }
@@ -249,7 +353,7 @@ __global__ void __launch_bounds__(256) small_svd_kernel(const float* __restrict_
         o2 += off_s[w];
         d2 += off_s[16 + w];
       }
-      if (o2 <= 1e-28 * d2 || d2 == 0.0) done = 1;
+      if (o2 <= 1e-24 * d2 || d2 == 0.0 || !rotated) done = 1;
     }
     __syncthreads();
   }
@@ -441,8 +545,14 @@ static int run_chain(const spx_rsvd_args* a, const RsvdWs& w, cudaStream_t st) {
   cudaFuncSetAttribute(gemm_mx_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smx);
   cudaFuncSetAttribute(orth_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
   const dim3 gmx((m + 63) / 64, Nb), gmty((n + 31) / 32, Nb);
+  // Cholesky-QR when its shared memory fits, classical Gram-Schmidt (CGS2) otherwise
+  cudaFuncSetAttribute(cholqr_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
   auto orth = [&](float* X, int rows) {
-    orth_kernel<<<Nb, 256, ((size_t)rows * r + r) * sizeof(float), st>>>(X, rows, r);
+    const size_t cq = cholqr_smem(rows, r);
+    if (cq <= 220 * 1024)
+      cholqr_kernel<<<Nb, 256, cq, st>>>(X, rows, r);
+    else
+      orth_kernel<<<Nb, 256, ((size_t)rows * r + r) * sizeof(float), st>>>(X, rows, r);
   };
   gemm_mx_kernel<T><<<gmx, 256, smx, st>>>(M, ms, a->omega, w.Y, m, n, r);
   orth(w.Y, m);
