@@ -20,6 +20,9 @@ namespace spx {
 
 // ------------------------------------------------------------ Y = M X  (CUDA cores)
 // X: f32 [n][r] per matrix.  Y: f32 [m][r].  grid (ceil(m/64), Nb), 256 threads.
+// Register tiles: thread (row pair rp = tid / 8, column group cg = tid % 8) owns rows
+// 2rp, 2rp+1 and columns cg, cg + 8, ... (< r <= 64), so each shared-memory load feeds
+// several FMAs.
 template <typename T>
 __global__ void __launch_bounds__(256) gemm_mx_kernel(const T* __restrict__ M, int64_t ms,
                                                       const float* __restrict__ X, float* __restrict__ Y, int m,
@@ -32,41 +35,64 @@ __global__ void __launch_bounds__(256) gemm_mx_kernel(const T* __restrict__ M, i
   const float* Xi = X + (int64_t)i * n * r;
   for (int e = threadIdx.x; e < n * r; e += blockDim.x) sx[e] = Xi[e];
   const int rows = min(64, m - row0);
-  for (int e = threadIdx.x; e < rows * n; e += blockDim.x) {
+  for (int e = threadIdx.x; e < 64 * n; e += blockDim.x) {
     const int t = e / n, d = e - t * n;
-    smt[t * (n + 1) + d] = to_f(Mi[(int64_t)(row0 + t) * n + d]);
+    smt[t * (n + 1) + d] = t < rows ? to_f(Mi[(int64_t)(row0 + t) * n + d]) : 0.f;
   }
   __syncthreads();
+  const int rpi = threadIdx.x >> 3, cg = threadIdx.x & 7;
+  float acc0[8], acc1[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) acc0[u] = acc1[u] = 0.f;
+  const float* m0 = smt + (2 * rpi) * (n + 1);
+  const float* m1 = m0 + (n + 1);
+  for (int d = 0; d < n; ++d) {
+    const float a0 = m0[d], a1 = m1[d];
+    const float* xr = sx + d * r;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int c = cg + 8 * u;
+      if (c < r) {
+        const float xv = xr[c];
+        acc0[u] = fmaf(a0, xv, acc0[u]);
+        acc1[u] = fmaf(a1, xv, acc1[u]);
+      }
+    }
+  }
   float* Yi = Y + (int64_t)i * m * r;
-  for (int e = threadIdx.x; e < rows * r; e += blockDim.x) {
-    const int t = e / r, c = e - t * r;
-    float acc = 0.f;
-    for (int d = 0; d < n; ++d) acc = fmaf(smt[t * (n + 1) + d], sx[d * r + c], acc);
-    Yi[(int64_t)(row0 + t) * r + c] = acc;
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const int c = cg + 8 * u;
+    if (c < r) {
+      if (2 * rpi < rows) Yi[(int64_t)(row0 + 2 * rpi) * r + c] = acc0[u];
+      if (2 * rpi + 1 < rows) Yi[(int64_t)(row0 + 2 * rpi + 1) * r + c] = acc1[u];
+    }
   }
 }
 
 // ---------------------------------------------------------- Z = M^T Y (CUDA cores)
-// Y: f32 [m][r]; Z: f32 [n][r].  grid (ceil(n/32), Nb), 256 threads.
+// Y: f32 [m][r]; Z: f32 [n][r].  grid (ceil(n/64), Nb), 256 threads.  Thread (column
+// pair dp = tid / 8, group cg = tid % 8) owns columns 2dp, 2dp+1 of M and outputs
+// cg, cg + 8, ... of r, accumulated over 64-row tiles of M and Y staged in shared memory.
 template <typename T>
 __global__ void __launch_bounds__(256) gemm_mty_kernel(const T* __restrict__ M, int64_t ms,
                                                        const float* __restrict__ Y, float* __restrict__ Z, int m,
                                                        int n, int r) {
-  __shared__ float smt[64][33];
+  __shared__ float smt[64][65];
   __shared__ float sy[64][65];
-  const int i = blockIdx.y, col0 = blockIdx.x * 32;
-  const int cols = min(32, n - col0);
+  const int i = blockIdx.y, col0 = blockIdx.x * 64;
+  const int cols = min(64, n - col0);
   const T* Mi = M + (int64_t)i * ms;
   const float* Yi = Y + (int64_t)i * m * r;
-  float acc[8];
+  const int dpi = threadIdx.x >> 3, cg = threadIdx.x & 7;
+  float acc0[8], acc1[8];
 #pragma unroll
-  for (int u = 0; u < 8; ++u) acc[u] = 0.f;
-  // thread owns outputs e = tid + 256*u, (col = e / r, c = e % r) for e < 32*r
+  for (int u = 0; u < 8; ++u) acc0[u] = acc1[u] = 0.f;
   for (int t0 = 0; t0 < m; t0 += 64) {
     const int rows = min(64, m - t0);
     __syncthreads();
-    for (int e = threadIdx.x; e < 64 * 32; e += blockDim.x) {
-      const int t = e / 32, d = e - t * 32;
+    for (int e = threadIdx.x; e < 64 * 64; e += blockDim.x) {
+      const int t = e >> 6, d = e & 63;
       smt[t][d] = (t < rows && d < cols) ? to_f(Mi[(int64_t)(t0 + t) * n + col0 + d]) : 0.f;
     }
     for (int e = threadIdx.x; e < 64 * r; e += blockDim.x) {
@@ -74,24 +100,26 @@ __global__ void __launch_bounds__(256) gemm_mty_kernel(const T* __restrict__ M, 
       sy[t][c] = t < rows ? Yi[(int64_t)(t0 + t) * r + c] : 0.f;
     }
     __syncthreads();
+    for (int t = 0; t < 64; ++t) {
+      const float a0 = smt[t][2 * dpi], a1 = smt[t][2 * dpi + 1];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int e = threadIdx.x + 256 * u;
-      if (e < 32 * r) {
-        const int d = e / r, c = e - d * r;
-        float a = acc[u];
-        for (int t = 0; t < 64; ++t) a = fmaf(smt[t][d], sy[t][c], a);
-        acc[u] = a;
+      for (int u = 0; u < 8; ++u) {
+        const int c = cg + 8 * u;
+        if (c < r) {
+          const float yv = sy[t][c];
+          acc0[u] = fmaf(a0, yv, acc0[u]);
+          acc1[u] = fmaf(a1, yv, acc1[u]);
+        }
       }
     }
   }
   float* Zi = Z + (int64_t)i * n * r;
 #pragma unroll
   for (int u = 0; u < 8; ++u) {
-    const int e = threadIdx.x + 256 * u;
-    if (e < 32 * r) {
-      const int d = e / r, c = e - d * r;
-      if (d < cols) Zi[(int64_t)(col0 + d) * r + c] = acc[u];
+    const int c = cg + 8 * u;
+    if (c < r) {
+      if (2 * dpi < cols) Zi[(int64_t)(col0 + 2 * dpi) * r + c] = acc0[u];
+      if (2 * dpi + 1 < cols) Zi[(int64_t)(col0 + 2 * dpi + 1) * r + c] = acc1[u];
     }
   }
 }
@@ -246,149 +274,106 @@ __global__ void __launch_bounds__(256) cholqr_kernel(float* __restrict__ X, int 
   }
 }
 
-// ----------------------------------------------- small SVD through a Jacobi eigensolve
-// Z = Bp^T: f32 [n][r].  Outputs Wk f32 [r][k], S f32 [k], Vh f32 [k][n].
+// ------------------------------------------------ small SVD by one-sided Jacobi
+// Z = Bp^T: f32 [n][r] (n <= 128, r <= 64).  One-sided (Hestenes) Jacobi on the columns
+// of A = Bp^T: plane rotations A J make the columns orthogonal; then A J = Vh^T S (column
+// norms are the singular values) and J holds the left singular vectors of Bp, i.e. the
+// eigenvectors of Bp Bp^T.  Bp Bp^T is never formed, so small singular values keep their
+// relative accuracy in float32.  A round applies rp/2 disjoint rotations (circle
+// ordering: index rp-1 meets `round`, pair u >= 1 couples round +- u modulo rp-1), one
+// warp per rotation; a pair is rotated while |a_p . a_q| > 2e-6 |a_p| |a_q| (a few times
+// the float32 rounding of a 128-term dot product), and a sweep without rotations ends
+// the iteration.
+// Outputs Wk f32 [r][k], S f32 [k], Vh f32 [k][n] (descending singular values).
+size_t small_svd_smem(int n, int r) {
+  const int rp = (r + 1) & ~1;
+  return ((size_t)rp * 128 + (size_t)rp * rp + rp) * sizeof(float) + rp * sizeof(int);
+}
+
 __global__ void __launch_bounds__(256) small_svd_kernel(const float* __restrict__ Z, float* __restrict__ Wk,
                                                         float* __restrict__ S, float* __restrict__ Vh, int n, int r,
                                                         int k) {
-  extern __shared__ double smd[];
+  extern __shared__ float smf[];
   const int rp = (r + 1) & ~1;        // padded to even for the round-robin ordering
-  double* G = smd;                    // [rp][rp]
-  double* W = G + rp * rp;            // [rp][rp]
-  double* cs = W + rp * rp;           // [rp/2][2]
-  int* pairs = reinterpret_cast<int*>(cs + rp);   // [rp] (round-robin pairs of this round)
-  int* perm = pairs + rp;                          // [rp]
-  float* sz = reinterpret_cast<float*>(perm + rp); // [n][r]
-  __shared__ double off_s[32];
-  __shared__ int done, rotated;
-  const int i = blockIdx.x;
+  float* A = smf;                     // [rp][128] columns of Bp^T (zero padded)
+  float* J = A + rp * 128;            // [rp][rp] column-major: J[c * rp + a] = J(a, c)
+  float* nrm = J + rp * rp;           // [rp] column norms
+  int* perm = reinterpret_cast<int*>(nrm + rp);   // [rp]
+  __shared__ int rotated;
+  const int i = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
   const float* Zi = Z + (int64_t)i * n * r;
-  for (int e = threadIdx.x; e < n * r; e += blockDim.x) sz[e] = Zi[e];
-  __syncthreads();
-  // Gram matrix in float64, identity for the padding index
-  for (int e = threadIdx.x; e < rp * rp; e += blockDim.x) {
-    const int a = e / rp, b = e - a * rp;
-    double g = 0.0;
-    if (a < r && b < r) {
-      for (int d = 0; d < n; ++d) g += (double)sz[d * r + a] * (double)sz[d * r + b];
-    }
-    G[e] = g;
-    W[e] = (a == b) ? 1.0 : 0.0;
+  for (int e = tid; e < rp * 128; e += blockDim.x) {
+    const int c = e >> 7, d = e & 127;
+    A[e] = (c < r && d < n) ? Zi[(int64_t)d * r + c] : 0.f;
   }
-  if (threadIdx.x == 0) done = 0;
+  for (int e = tid; e < rp * rp; e += blockDim.x) J[e] = (e / rp == e % rp) ? 1.f : 0.f;
   __syncthreads();
-  const int np = rp / 2;
-  // a rotation is skipped once |G_pq| <= 1e-13 sqrt(|G_pp G_qq|) (far below what the
-  // float32 outputs resolve); a sweep without rotations ends the iteration
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  for (int sweep = 0; sweep < 30 && !done; ++sweep) {
-    if (threadIdx.x == 0) rotated = 0;
+  const int np = rp / 2, nn = rp - 1;
+  for (int sweep = 0; sweep < 30; ++sweep) {
+    if (tid == 0) rotated = 0;
     __syncthreads();
-    for (int round = 0; round < rp - 1; ++round) {
-      // circle method: index rp-1 is fixed and meets `round`; pair u >= 1 couples
-      // (round + u) and (round - u) modulo rp - 1.  Every pair meets once per sweep.
-      if (threadIdx.x < np) {
-        const int u = threadIdx.x, nn = rp - 1;
+    for (int round = 0; round < nn; ++round) {
+      for (int u = warp; u < np; u += nw) {
         int p = u == 0 ? round : (round + u) % nn;
         int q = u == 0 ? nn : (round - u + nn) % nn;
         if (p > q) { const int tmp = p; p = q; q = tmp; }
-        pairs[2 * u] = p;
-        pairs[2 * u + 1] = q;
-        double c = 1.0, s = 0.0;
-        const double apq = G[p * rp + q];
-        if (q < r && fabs(apq) > 1e-300 && fabs(apq) > 1e-13 * sqrt(fabs(G[p * rp + p] * G[q * rp + q]))) {
-          rotated = 1;
-          const double tau = (G[q * rp + q] - G[p * rp + p]) / (2.0 * apq);
-          const double t = (tau >= 0 ? 1.0 : -1.0) / (fabs(tau) + sqrt(1.0 + tau * tau));
-          c = 1.0 / sqrt(1.0 + t * t);
-          s = t * c;
+        if (q >= r) continue;   // the padding column
+        float4 ap = reinterpret_cast<const float4*>(A + p * 128)[lane];
+        float4 aq = reinterpret_cast<const float4*>(A + q * 128)[lane];
+        float al = ap.x * ap.x + ap.y * ap.y + ap.z * ap.z + ap.w * ap.w;
+        float be = aq.x * aq.x + aq.y * aq.y + aq.z * aq.z + aq.w * aq.w;
+        float ga = ap.x * aq.x + ap.y * aq.y + ap.z * aq.z + ap.w * aq.w;
+        al = warp_sum(al);
+        be = warp_sum(be);
+        ga = warp_sum(ga);
+        if (!(fabsf(ga) > 2e-6f * sqrtf(al * be)) || ga == 0.f) continue;
+        const float zeta = (be - al) / (2.f * ga);
+        const float t = (zeta >= 0.f ? 1.f : -1.f) / (fabsf(zeta) + sqrtf(1.f + zeta * zeta));
+        const float c = rsqrtf(1.f + t * t), sn = t * c;
+        float4 np4, nq4;
+        np4.x = c * ap.x - sn * aq.x; nq4.x = sn * ap.x + c * aq.x;
+        np4.y = c * ap.y - sn * aq.y; nq4.y = sn * ap.y + c * aq.y;
+        np4.z = c * ap.z - sn * aq.z; nq4.z = sn * ap.z + c * aq.z;
+        np4.w = c * ap.w - sn * aq.w; nq4.w = sn * ap.w + c * aq.w;
+        reinterpret_cast<float4*>(A + p * 128)[lane] = np4;
+        reinterpret_cast<float4*>(A + q * 128)[lane] = nq4;
+        for (int a = lane; a < r; a += 32) {
+          const float jp = J[p * rp + a], jq = J[q * rp + a];
+          J[p * rp + a] = c * jp - sn * jq;
+          J[q * rp + a] = sn * jp + c * jq;
         }
-        cs[2 * threadIdx.x] = c;
-        cs[2 * threadIdx.x + 1] = s;
-      }
-      __syncthreads();
-      // rows: new_p = c row_p - s row_q ; new_q = s row_p + c row_q
-      for (int e = threadIdx.x; e < np * rp; e += blockDim.x) {
-        const int u = e / rp, col = e - u * rp;
-        const int p = pairs[2 * u], q = pairs[2 * u + 1];
-        const double c = cs[2 * u], s = cs[2 * u + 1];
-        const double gp = G[p * rp + col], gq = G[q * rp + col];
-        G[p * rp + col] = c * gp - s * gq;
-        G[q * rp + col] = s * gp + c * gq;
-      }
-      __syncthreads();
-      // columns of G and W
-      for (int e = threadIdx.x; e < np * rp; e += blockDim.x) {
-        const int u = e / rp, row = e - u * rp;
-        const int p = pairs[2 * u], q = pairs[2 * u + 1];
-        const double c = cs[2 * u], s = cs[2 * u + 1];
-        const double gp = G[row * rp + p], gq = G[row * rp + q];
-        G[row * rp + p] = c * gp - s * gq;
-        G[row * rp + q] = s * gp + c * gq;
-        const double wp = W[row * rp + p], wq = W[row * rp + q];
-        W[row * rp + p] = c * wp - s * wq;
-        W[row * rp + q] = s * wp + c * wq;
+        if (lane == 0) rotated = 1;
       }
       __syncthreads();
     }
-    // convergence: off-diagonal mass relative to the diagonal
-    double off = 0.0, dia = 0.0;
-    for (int e = threadIdx.x; e < r * r; e += blockDim.x) {
-      const int a = e / r, b = e - a * r;
-      const double g = G[a * rp + b];
-      if (a == b) dia += g * g; else off += g * g;
-    }
-    for (int o = 16; o > 0; o >>= 1) {
-      off += __shfl_xor_sync(0xffffffffu, off, o);
-      dia += __shfl_xor_sync(0xffffffffu, dia, o);
-    }
-    if (lane == 0) {
-      off_s[warp] = off;
-      off_s[16 + warp] = dia;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      double o2 = 0.0, d2 = 0.0;
-      for (int w = 0; w < nw; ++w) {
-        o2 += off_s[w];
-        d2 += off_s[16 + w];
-      }
-      if (o2 <= 1e-24 * d2 || d2 == 0.0 || !rotated) done = 1;
-    }
+    if (!rotated) break;
     __syncthreads();
   }
-  // order eigenvalues descending
-  if (threadIdx.x == 0) {
-    for (int a = 0; a < r; ++a) perm[a] = a;
-    for (int a = 0; a < r; ++a) {
-      int best = a;
-      for (int b = a + 1; b < r; ++b)
-        if (G[perm[b] * rp + perm[b]] > G[perm[best] * rp + perm[best]]) best = b;
-      const int tmp = perm[a];
-      perm[a] = perm[best];
-      perm[best] = tmp;
-    }
+  // singular values = column norms; order descending (rank, ties by index)
+  for (int c = warp; c < r; c += nw) {
+    const float4 v = reinterpret_cast<const float4*>(A + c * 128)[lane];
+    const float ss = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
+    if (lane == 0) nrm[c] = sqrtf(ss);
   }
   __syncthreads();
-  const double lam0 = fmax(G[perm[0] * rp + perm[0]], 0.0);
-  for (int j = threadIdx.x; j < k; j += blockDim.x) {
-    const double lam = fmax(G[perm[j] * rp + perm[j]], 0.0);
-    S[(int64_t)i * k + j] = (float)sqrt(lam);
+  for (int a = tid; a < r; a += blockDim.x) {
+    const float na = nrm[a];
+    int rank = 0;
+    for (int b = 0; b < r; ++b) rank += (nrm[b] > na) || (nrm[b] == na && b < a);
+    perm[rank] = a;
   }
-  for (int e = threadIdx.x; e < r * k; e += blockDim.x) {
+  __syncthreads();
+  const float s0 = nrm[perm[0]];
+  for (int j = tid; j < k; j += blockDim.x) S[(int64_t)i * k + j] = nrm[perm[j]];
+  for (int e = tid; e < r * k; e += blockDim.x) {
     const int a = e / k, j = e - a * k;
-    Wk[(int64_t)i * r * k + e] = (float)W[a * rp + perm[j]];
+    Wk[(int64_t)i * r * k + e] = J[perm[j] * rp + a];
   }
-  for (int e = threadIdx.x; e < k * n; e += blockDim.x) {
+  for (int e = tid; e < k * n; e += blockDim.x) {
     const int j = e / n, d = e - j * n;
     const int pj = perm[j];
-    const double lam = fmax(G[pj * rp + pj], 0.0);
-    double v = 0.0;
-    if (lam > 1e-24 * lam0 && lam > 0.0) {
-      for (int a = 0; a < r; ++a) v += W[a * rp + pj] * (double)sz[d * r + a];
-      v /= sqrt(lam);
-    }
-    Vh[(int64_t)i * k * n + e] = (float)v;
+    const float sj = nrm[pj];
+    Vh[(int64_t)i * k * n + e] = (sj > 1e-12f * s0 && sj > 0.f) ? A[pj * 128 + d] / sj : 0.f;
   }
 }
 
@@ -544,7 +529,7 @@ static int run_chain(const spx_rsvd_args* a, const RsvdWs& w, cudaStream_t st) {
   const size_t smx = ((size_t)n * r + 64 * (size_t)(n + 1)) * sizeof(float);
   cudaFuncSetAttribute(gemm_mx_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smx);
   cudaFuncSetAttribute(orth_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-  const dim3 gmx((m + 63) / 64, Nb), gmty((n + 31) / 32, Nb);
+  const dim3 gmx((m + 63) / 64, Nb), gmty((n + 63) / 64, Nb);
   // Cholesky-QR when its shared memory fits, classical Gram-Schmidt (CGS2) otherwise
   cudaFuncSetAttribute(cholqr_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
   auto orth = [&](float* X, int rows) {
@@ -566,7 +551,7 @@ static int run_chain(const spx_rsvd_args* a, const RsvdWs& w, cudaStream_t st) {
   int rc = launch_status("rsvd gemm/orth chain");
   if (rc != SPX_OK) return rc;
   const int rp = (r + 1) & ~1;
-  const size_t ssvd = (2 * (size_t)rp * rp + rp) * sizeof(double) + 2 * rp * sizeof(int) + (size_t)n * r * sizeof(float);
+  const size_t ssvd = small_svd_smem(n, r);
   cudaFuncSetAttribute(small_svd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssvd);
   small_svd_kernel<<<Nb, 256, ssvd, st>>>(w.Z, w.Wk, w.S, w.Vh, n, r, k);
   rc = launch_status("small_svd_kernel");
