@@ -211,6 +211,7 @@ __global__ void __launch_bounds__(256) cholqr_kernel(float* __restrict__ X, int 
       const int a0 = 2 * ta, b0 = 2 * (ta + rem);
       const int a1 = a0 + 1 < r ? a0 + 1 : a0, b1 = b0 + 1 < r ? b0 + 1 : b0;
       double g00 = 0.0, g01 = 0.0, g10 = 0.0, g11 = 0.0;
+#pragma unroll 4
       for (int t = 0; t < rows; ++t) {
         const float* xr = sx + t * rp;
         const double xa0 = xr[a0], xa1 = xr[a1], xb0 = xr[b0], xb1 = xr[b1];
@@ -225,45 +226,64 @@ __global__ void __launch_bounds__(256) cholqr_kernel(float* __restrict__ X, int 
       if (a1 != a0 && b1 != b0) { G[a1 * r + b1] = g11; G[b1 * r + a1] = g11; }
     }
     __syncthreads();
-    // ---- Cholesky G = L L^T (right-looking, one warp) -----------------------------
-    if (warp == 0) {
-      double dmax = 0.0;
-      for (int j = lane; j < r; j += 32) dmax = fmax(dmax, G[j * r + j]);
-      for (int o = 16; o > 0; o >>= 1) dmax = fmax(dmax, __shfl_xor_sync(0xffffffffu, dmax, o));
-      double pmin = 1e300, pmax = 0.0;
+    // ---- Cholesky G = L L^T (right-looking; each step's trailing update is spread
+    //      over the whole block) --------------------------------------------------------
+    {
+      __shared__ double dmax_s, pmin_s, pmax_s;
+      if (tid == 0) {
+        double dm = 0.0;
+        for (int j = 0; j < r; ++j) dm = fmax(dm, G[j * r + j]);
+        dmax_s = dm;
+        pmin_s = 1e300;
+        pmax_s = 0.0;
+      }
+      __syncthreads();
+      const double dmax = dmax_s;
       for (int j = 0; j < r; ++j) {
         const double piv = G[j * r + j];
         const bool ok = piv > 1e-30 * dmax && dmax > 0.0;
         const double d = ok ? sqrt(piv) : 0.0;
-        if (ok) {
-          pmin = fmin(pmin, piv);
-          pmax = fmax(pmax, piv);
+        // column j of L (every thread reads the pivot before anyone overwrites it)
+        __syncthreads();
+        for (int a = j + 1 + tid; a < r; a += blockDim.x) G[a * r + j] = ok ? G[a * r + j] / d : 0.0;
+        if (tid == 0) {
+          Lf[j * r + j] = ok ? (float)(1.0 / d) : 0.f;
+          if (ok) {
+            pmin_s = fmin(pmin_s, piv);
+            pmax_s = fmax(pmax_s, piv);
+          }
         }
-        for (int a = j + 1 + lane; a < r; a += 32) G[a * r + j] = ok ? G[a * r + j] / d : 0.0;
-        __syncwarp();
+        __syncthreads();
         // trailing update of the lower triangle: G[a][c] -= L[a][j] L[c][j], j < c <= a
-        for (int a = j + 1 + lane; a < r; a += 32) {
-          const double la = G[a * r + j];
-          for (int c = j + 1; c <= a; ++c) G[a * r + c] = fma(-la, G[c * r + j], G[a * r + c]);
+        const int m = r - j - 1;
+        for (int e = tid; e < m * m; e += blockDim.x) {
+          const int a = j + 1 + e / m, c = j + 1 + e % m;
+          if (c <= a) G[a * r + c] = fma(-G[a * r + j], G[c * r + j], G[a * r + c]);
         }
-        if (lane == 0) Lf[j * r + j] = ok ? (float)(1.0 / d) : 0.f;
-        __syncwarp();
+        __syncthreads();
       }
-      for (int e = lane; e < r * r; e += 32) {
+      for (int e = tid; e < r * r; e += blockDim.x) {
         const int a = e / r, c = e - a * r;
         if (c < a) Lf[e] = (float)G[e];
       }
-      if (lane == 0 && pass == 0 && pmax > 1e12 * pmin) third = 1;
+      if (tid == 0 && pass == 0 && pmax_s > 1e12 * pmin_s) third = 1;
     }
     __syncthreads();
     // ---- X := X L^{-T}, one row per thread ------------------------------------------
     for (int t = tid; t < rows; t += blockDim.x) {
       float* xr = sx + t * rp;
       for (int j = 0; j < r; ++j) {
-        float v = xr[j];
         const float* lj = Lf + j * r;
-        for (int c = 0; c < j; ++c) v = fmaf(-xr[c], lj[c], v);
-        xr[j] = v * lj[j];
+        float v0 = xr[j], v1 = 0.f, v2 = 0.f, v3 = 0.f;   // four independent chains
+        int c = 0;
+        for (; c + 4 <= j; c += 4) {
+          v0 = fmaf(-xr[c], lj[c], v0);
+          v1 = fmaf(-xr[c + 1], lj[c + 1], v1);
+          v2 = fmaf(-xr[c + 2], lj[c + 2], v2);
+          v3 = fmaf(-xr[c + 3], lj[c + 3], v3);
+        }
+        for (; c < j; ++c) v0 = fmaf(-xr[c], lj[c], v0);
+        xr[j] = ((v0 + v1) + (v2 + v3)) * lj[j];
       }
     }
     __syncthreads();
