@@ -914,8 +914,11 @@ static int num_sms() {
   return cache[dev];
 }
 
-// Items of G units x JR blocks: pick the split whose slowest CTA does the least work
-// (rounds of items x item size), preferring longer block ranges (fewer partial records).
+// Items of G units x JR blocks: pick the split whose slowest CTA does the least work:
+// rounds of items x item size in unit-blocks, plus the partial records - one per (unit,
+// block range), written by this kernel and read back by the merge kernel, each about
+// 1/12 of a unit-block's bytes - spread over the SMs, plus one RoPE reload (about 1.5
+// unit-blocks of stall) each time a CTA moves to a new block.
 struct Plan {
   int G, JR, ngroups, nranges, nitems, grid;
 };
@@ -950,7 +953,7 @@ static Plan plan(int units, int nblk, int sms) {
       if (nranges != nr) continue;
       const long items = (long)ngroups * nranges;
       const long rounds = (items + sms - 1) / sms;
-      const long cost = rounds * Gu * JR;
+      const long cost = 12 * rounds * Gu * JR + ((long)units * nranges + sms - 1) / sms + 18 * rounds * JR;
       if (best_cost < 0 || cost < best_cost) {
         best_cost = cost;
         best = make_plan(units, nblk, Gu, JR, sms);
