@@ -4,13 +4,14 @@
 //   Y = M Omega; Q = orth(Y)
 //   repeat n_iter: Z = orth(M^T Q); Q = orth(M Z)      (subspace iteration)
 //   Bp^T = M^T Q                                        ([n, r])
-//   Bp Bp^T = W diag(lambda) W^T   (cyclic Jacobi, float64, parallel ordering)
-//   S = sqrt(lambda), Vh_j = W_j^T Bp / S_j, U = Q W     (truncated to k)
+//   Bp = W S Vh by one-sided Jacobi on the columns of Bp^T (float32, round-robin)
+//   U = Q W (truncated to k)
 //   C = U * S -> per-matrix INT8 codes, scale, (min, max); basis = Vh in basis dtype.
 // The reference runs the power iterations un-normalised; re-orthonormalising every
 // step spans the same subspace in exact arithmetic and avoids the float32 loss of the
-// un-normalised form.  orth() is classical Gram-Schmidt applied twice (CGS2), which is
-// as stable as Householder QR for these sizes.
+// un-normalised form.  orth() is Cholesky-QR applied twice (float64 Gram matrix), with
+// classical Gram-Schmidt (CGS2) for shapes whose panel does not fit in shared memory;
+// both are as stable as Householder QR for these well-conditioned panels.
 #include <math.h>
 
 #include "spx_common.cuh"
