@@ -104,6 +104,21 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t a, uint32_t parity)
       : "memory");
   return ok != 0;
 }
+// Two independent phase tests in one statement, so that their latencies overlap.
+__device__ __forceinline__ void mbar_test2(uint32_t a, uint32_t pa, uint32_t b, uint32_t pb, bool& ra, bool& rb) {
+  uint32_t x, y;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%2], %3;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 q, [%4], %5;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t"
+      "selp.u32 %1, 1, 0, q;\n\t}"
+      : "=r"(x), "=r"(y)
+      : "r"(a), "r"(pa), "r"(b), "r"(pb)
+      : "memory");
+  ra = x != 0;
+  rb = y != 0;
+}
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
                "l"(src), "r"(bytes), "r"(bar)
@@ -658,8 +673,9 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
             const int64_t n = (int64_t)it * MT + mt;
             const int as = (int)(n & 1), b = as;
             // test both barriers at once; sleep on whichever is not there yet
-            const bool ra = mbar_try_wait(b_aready + 8 * as, (uint32_t)((n / 2) & 1));
-            const bool re = n < 2 || mbar_try_wait(b_acce + 8 * b, (uint32_t)((n / 2 - 1) & 1));
+            bool ra, re;
+            mbar_test2(b_aready + 8 * as, (uint32_t)((n / 2) & 1), b_acce + 8 * b, (uint32_t)((n / 2 + 1) & 1), ra, re);
+            re = re || n < 2;   // (n / 2 + 1) & 1 == (n / 2 - 1) & 1: the previous release of buffer b
             bool ok = ra || wait1(b_aready + 8 * as, (uint32_t)((n / 2) & 1), ab);
             if (!re) ok = wait1(b_acce + 8 * b, (uint32_t)((n / 2 - 1) & 1), ab) && ok;
             if (ok && !*ab.flag) {
