@@ -9,12 +9,14 @@
 //
 // Warp roles (4 warpgroups, 512 threads, one CTA per SM; registers rebalanced with
 // setmaxnreg: 160 for the consumers, 96 for the others):
-//   warpgroup 2  warps 8-10 convert ring A (INT8 key codes [T][RK], FP16 key basis
+//   warpgroup 2  warps 8-9 convert ring A (INT8 key codes [T][RK], FP16 key basis
 //                [RK][128]) -> FP16 UMMA A tiles (K-major, no swizzle) and the MN-major B
-//                tile, signalling each tile on an mbarrier; lane 0 of warp 11 bulk-copies
-//                ring A 3 stages ahead and issues
+//                tile, signalling each tile on an mbarrier; lane 0 of warp 10 (even
+//                M-tiles) and of warp 11 (odd M-tiles) issue
 //                  tcgen05.mma kind::f16  M=128 tokens x N=128 dims x K=16, D = f16
-//                (K~ = codes_K @ B_K) into one of two TMEM accumulators per M-tile.
+//                (K~ = codes_K @ B_K) into TMEM accumulator 0 / 1, so the two
+//                accumulators cycle independently; lane 0 of warp 11 also bulk-copies
+//                ring A 3 stages ahead.
 //   warpgroups 0-1  consumers, two warps per TMEM lane quadrant, 16 tokens of each
 //                M-tile: K~ via tcgen05.ld 16x256b.pack::16b (already f16 pairs; the next
 //                M-tile loads while this one computes), RoPE rows via tcgen05.ld 16x256b,
@@ -49,7 +51,7 @@ constexpr int NPT = NPW * 32;
 constexpr int ET0 = (NCW + NPW) * 32;      // first epilogue thread
 constexpr int NEP = NEW * 32;
 constexpr int GMAX = 32;                   // units per item at most
-constexpr int NCV = NPW - 1;               // converter warps that convert; the last one issues MMAs
+constexpr int NCV = NPW - 2;               // converter warps that convert; the other two issue MMAs
 constexpr int BAR_EPI = 3;                 // named barrier of the epilogue warps
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LN2 = 0.6931471805599453f;
@@ -325,6 +327,7 @@ __device__ __forceinline__ void i8x4_to_h2(uint32_t w, uint32_t& lo, uint32_t& h
 // ------------------------------------------------------------------ configuration ---
 template <int RK, int RV, int MT>
 struct Cfg {
+  static_assert(MT % 2 == 0, "M-tile n uses accumulator n & 1 == mt & 1 only for an even tile count");
   static constexpr int TB = MT * 128;                  // tokens per block
   static constexpr int CK = TB * RK;                   // INT8 key codes
   static constexpr int CV = RV * TB;                   // INT8 value codes (value-tile layout)
@@ -413,7 +416,7 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
     }
     for (int a = 0; a < NA; ++a) mbar_init(b_aready + 8 * a, NCV);
     for (int b = 0; b < 2; ++b) {
-      mbar_init(b_bslot + 8 * b, 1);
+      mbar_init(b_bslot + 8 * b, 2);   // one commit per MMA-issue lane
       mbar_init(b_accf + 8 * b, 1);
       mbar_init(b_acce + 8 * b, NCW);
       mbar_init(b_pready + 8 * b, NCW);
@@ -579,9 +582,10 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
     __syncwarp();
   } else if (w >= NCW) {
     // ============================================================= converter warps ===
-    // Warps 8-10 convert: key basis -> B tile, key codes -> FP16 A tiles; each warp
-    // arrives on aready[slot] once its share of a tile is written.  Lane 0 of warp 11
-    // issues the MMAs and the ring-A copies, so conversion never waits behind an issue.
+    // Warps 8-9 convert: key basis -> B tile, key codes -> FP16 A tiles; each warp
+    // arrives on aready[slot] once its share of a tile is written.  Lane 0 of warps 10
+    // and 11 issue the MMAs (and warp 11 the ring-A copies), so conversion never waits
+    // behind an issue.
     setmaxnreg_dec<96>();
     const int wc = w - NCW;
     if (wc < NCV) {
@@ -642,7 +646,10 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
         }
       }
     } else {
-      // ---- MMA issuer (lane 0 of warp 11) --------------------------------------------
+      // ---- MMA issuers: lane 0 of warp 10 (even M-tiles, accumulator 0) and of warp 11
+      //      (odd M-tiles, accumulator 1, and the ring-A copies), so that each
+      //      accumulator cycles independently of the other -----------------------------
+      const int par = wc - NCV;
       if (lane == 0) {
         const uint32_t sA_u = smem_u32(sm + C::OFF_A), sB_u = smem_u32(sm + C::OFF_B);
         Seq sqA = sq;   // ring-A copies run STAGES iterations ahead
@@ -659,8 +666,10 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
           ++issuedA;
           sqA.next(I);
         };
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        for (int k = 0; k < STAGES && sqA.valid(I); ++k) issueA();
+        if (par == 1) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          for (int k = 0; k < STAGES && sqA.valid(I); ++k) issueA();
+        }
         // descriptors of A slot 0 / B slot 0, k-step 0; other slots and k-steps differ
         // only in the start-address field (address >> 4 in the low 14 bits)
         const uint64_t ad0 = umma_desc(sA_u, 2048, 128), bd0 = umma_desc(sB_u, 128, RK * 16);
@@ -669,7 +678,7 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
         for (; sq.valid(I); sq.next(I), ++it) {
           const int bs = it & 1;
 #pragma unroll 1
-          for (int mt = 0; mt < MT; ++mt) {
+          for (int mt = par; mt < MT; mt += 2) {
             const int64_t n = (int64_t)it * MT + mt;
             const int as = (int)(n & 1), b = as;
             // test both barriers at once; sleep on whichever is not there yet
@@ -686,18 +695,19 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
               for (int ks = 0; ks < RK / 16; ++ks)
                 umma_f16(d, ad + (uint64_t)((ks * 2 * 2048) >> 4), bd + (uint64_t)((ks * 256) >> 4), ks > 0 ? 1u : 0u);
               umma_commit(b_accf + 8 * b);
-              if (mt == MT - 1) umma_commit(b_bslot + 8 * bs);
+              if (mt >= MT - 2) umma_commit(b_bslot + 8 * bs);
               n_issued = n + 1;
             }
           }
-          // every converter warp has finished with stage it % STAGES of ring A: refill it
-          if (sqA.valid(I) && !*ab.flag) {
+          // every converter warp has finished with stage it % STAGES of ring A (the last
+          // M-tile, converted last, is ready): refill it
+          if (par == 1 && sqA.valid(I) && !*ab.flag) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             issueA();
           }
         }
         if (*ab.flag) {
-          drain(b_fullA, issuedA);
+          if (par == 1) drain(b_fullA, issuedA);
           if (n_issued > 0) {   // the last MMAs handed to the tensor core
             const int64_t n = n_issued - 1;
             const uint64_t t0 = gtimer();
