@@ -8,7 +8,7 @@
 // partial record per (unit, range) is written for the hot-tier/merge kernel.
 //
 // Warp roles (4 warpgroups, 512 threads, one CTA per SM; registers rebalanced with
-// setmaxnreg: 160 for the consumers, 96 for the others):
+// setmaxnreg: 176 for the consumers, 80 for the others):
 //   warpgroup 2  warps 8-9 convert ring A (INT8 key codes [T][RK], FP16 key basis
 //                [RK][128]) -> FP16 UMMA A tiles (K-major, no swizzle) and the MN-major B
 //                tile, signalling each tile on an mbarrier; lane 0 of warp 10 (even
@@ -340,11 +340,16 @@ struct Cfg {
   static constexpr int B_CV = 0, B_BV = CV, B_Q = CV + BV, STAGE_B = B_Q + QB;
   static constexpr int OFF_RA = 0;
   static constexpr int OFF_RB = OFF_RA + STAGES * STAGE_A;
-  static constexpr int ATILE = 128 * RK * 2;           // one M-tile of FP16 key codes
-  static constexpr int OFF_A = OFF_RB + STAGES * STAGE_B;   // [NA] x [RK/8 chunks][16 groups][8 rows][16 B]
+  // one M-tile of FP16 key codes: per K-step of 16 codes a [2 k-chunks][16 groups][8 rows]
+  // [16 B] block; K-step blocks 4096 + 64 bytes apart, so that the converters' two stores
+  // of a token's halves fall into different banks
+  static constexpr int KSTR = 128 * 16 * 2 + 64;
+  static constexpr int ATILE = ((RK / 16) * KSTR + 127) / 128 * 128;
+  static constexpr int OFF_A = OFF_RB + STAGES * STAGE_B;   // [NA] x ATILE
   static constexpr int OFF_B = OFF_A + NA * ATILE;     // [2] x [16 n-chunks][RK rows][16 B]
-  // consumer -> epilogue partials, double-buffered: m [8][8], l [8][8], v_lat [8][RV][8]
-  static constexpr int PART = NCW * 8 * 4 * 2 + NCW * RV * 8 * 4;
+  // consumer -> epilogue partials, double-buffered: m [8][8], l [8][8], v_lat [8 warps][8 heads][RVP]
+  static constexpr int RVP = RV + 4;                   // padded rank pitch (conflict-free both ways)
+  static constexpr int PART = NCW * 8 * 4 * 2 + NCW * 8 * RVP * 4;
   static constexpr int OFF_P = OFF_B + 2 * BK;
   static constexpr int OFF_BVP = OFF_P + 2 * PART;     // value basis, rows padded to QP bytes
   static constexpr int OFF_VL = OFF_BVP + RV * QP;     // combined v_lat [8][RV]
@@ -439,7 +444,7 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
     // ============================================================== epilogue warps ===
     // combine the consumer warps' partials, expand v_lat through B_V, merge into the
     // unit's running (m, l, o); thread 384 also streams ring B (values, queries).
-    setmaxnreg_dec<96>();
+    setmaxnreg_dec<80>();
     const int et = tid - ET0, ew = et >> 5;
     Seq sqB = sq;   // ring-B copies run STAGES iterations ahead
     int issuedB = 0;
@@ -499,7 +504,7 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
 #pragma unroll
         for (int ww = 0; ww < NCW; ++ww) {
           const float wt = exp2f(sM[ww * 8 + h] - M);
-          v = fmaf(sV[(ww * RV + r) * 8 + h], wt, v);
+          v = fmaf(sV[(ww * 8 + h) * C::RVP + r], wt, v);
           l = fmaf(sL[ww * 8 + h], wt, l);
         }
         sVL[h * RV + r] = v;
@@ -586,7 +591,7 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
     // arrives on aready[slot] once its share of a tile is written.  Lane 0 of warps 10
     // and 11 issue the MMAs (and warp 11 the ring-A copies), so conversion never waits
     // behind an issue.
-    setmaxnreg_dec<96>();
+    setmaxnreg_dec<80>();
     const int wc = w - NCW;
     if (wc < NCV) {
       const int ct = tid - PT0;   // 0 .. 32 NCV - 1
@@ -634,7 +639,7 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
               i8x4_to_h2(v.y, o0.z, o0.w);
               i8x4_to_h2(v.z, o1.x, o1.y);
               i8x4_to_h2(v.w, o1.z, o1.w);
-              uint8_t* d = dst + 2 * hf * 2048 + (tau >> 3) * 128 + (tau & 7) * 16;
+              uint8_t* d = dst + hf * C::KSTR + (tau >> 3) * 128 + (tau & 7) * 16;
               *reinterpret_cast<uint4*>(d) = o0;
               *reinterpret_cast<uint4*>(d + 2048) = o1;
             }
@@ -693,7 +698,7 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
               const uint64_t ad = ad0 + (uint64_t)((as * C::ATILE) >> 4), bd = bd0 + (uint64_t)((bs * C::BK) >> 4);
 #pragma unroll
               for (int ks = 0; ks < RK / 16; ++ks)
-                umma_f16(d, ad + (uint64_t)((ks * 2 * 2048) >> 4), bd + (uint64_t)((ks * 256) >> 4), ks > 0 ? 1u : 0u);
+                umma_f16(d, ad + (uint64_t)((ks * C::KSTR) >> 4), bd + (uint64_t)((ks * 256) >> 4), ks > 0 ? 1u : 0u);
               umma_commit(b_accf + 8 * b);
               if (mt >= MT - 2) umma_commit(b_bslot + 8 * bs);
               n_issued = n + 1;
@@ -720,7 +725,7 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
     }
   } else {
     // ============================================================== consumer warps ===
-    setmaxnreg_inc<160>();
+    setmaxnreg_inc<176>();
     const int lane_off = 32 * (w & 3) + 16 * (w >> 2);
     const uint4* rope_tab = reinterpret_cast<const uint4*>(p.rope);
     const bool live0 = 2 * t < nrep, live1 = 2 * t + 1 < nrep, hl = g < nrep;
@@ -883,11 +888,11 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
       }
 #pragma unroll
       for (int rt = 0; rt < RV / 16; ++rt) {
-        float* base = sV + (w * RV + rt * 16) * 8;
-        base[g * 8 + 2 * t] = vacc[rt][0];
-        base[g * 8 + 2 * t + 1] = vacc[rt][1];
-        base[(g + 8) * 8 + 2 * t] = vacc[rt][2];
-        base[(g + 8) * 8 + 2 * t + 1] = vacc[rt][3];
+        float* base = sV + (w * 8 + 2 * t) * C::RVP + rt * 16 + g;   // [warp][head][rank]
+        base[0] = vacc[rt][0];
+        base[C::RVP] = vacc[rt][1];
+        base[8] = vacc[rt][2];
+        base[C::RVP + 8] = vacc[rt][3];
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(b_pready + 8 * b2);
