@@ -560,15 +560,25 @@ static int run_chain(const spx_rsvd_args* a, const RsvdWs& w, cudaStream_t st) {
     else
       orth_kernel<<<Nb, 256, ((size_t)rows * r + r) * sizeof(float), st>>>(X, rows, r);
   };
-  gemm_mx_kernel<T><<<gmx, 256, smx, st>>>(M, ms, a->omega, w.Y, m, n, r);
+  // 16-bit inputs of 128 columns run the products on the tensor cores (spx_rsvd_tc.cu)
+  const bool tc = rsvd_tc_supported(a->in_dtype, a->M, ms, m, n, r);
+  auto mx = [&](const float* X, float* Y) {
+    if (tc) rsvd_tc_gemm(0, a->in_dtype, M, ms, X, Y, Nb, m, r, st);
+    else gemm_mx_kernel<T><<<gmx, 256, smx, st>>>(M, ms, X, Y, m, n, r);
+  };
+  auto mty = [&](const float* Y, float* Z) {
+    if (tc) rsvd_tc_gemm(1, a->in_dtype, M, ms, Y, Z, Nb, m, r, st);
+    else gemm_mty_kernel<T><<<gmty, 256, 0, st>>>(M, ms, Y, Z, m, n, r);
+  };
+  mx(a->omega, w.Y);
   orth(w.Y, m);
   for (int it = 0; it < a->n_iter; ++it) {
-    gemm_mty_kernel<T><<<gmty, 256, 0, st>>>(M, ms, w.Y, w.Z, m, n, r);
+    mty(w.Y, w.Z);
     orth(w.Z, n);
-    gemm_mx_kernel<T><<<gmx, 256, smx, st>>>(M, ms, w.Z, w.Y, m, n, r);
+    mx(w.Z, w.Y);
     orth(w.Y, m);
   }
-  gemm_mty_kernel<T><<<gmty, 256, 0, st>>>(M, ms, w.Y, w.Z, m, n, r);
+  mty(w.Y, w.Z);
   int rc = launch_status("rsvd gemm/orth chain");
   if (rc != SPX_OK) return rc;
   const int rp = (r + 1) & ~1;

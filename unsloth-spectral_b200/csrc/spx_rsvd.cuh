@@ -1,5 +1,6 @@
 // Parameters of the rSVD lift / quantisation epilogue.
 #pragma once
+#include <cuda_runtime.h>
 #include <stdint.h>
 
 namespace spx {
@@ -24,5 +25,11 @@ struct LiftParams {
   int basis_dtype;
   int64_t basis_mat_stride;
 };
+
+// Tensor-core products of the subspace iteration (spx_rsvd_tc.cu): mode 0 Y = M X,
+// mode 1 Z = M^T Y, for 16-bit M of 128 columns and m % 128 == 0.
+bool rsvd_tc_supported(int dtype, const void* M, int64_t ms, int m, int n, int r);
+int rsvd_tc_gemm(int mode, int dtype, const void* M, int64_t ms, const float* X, float* Y, int Nb, int m, int r,
+                 cudaStream_t st);
 
 }  // namespace spx
