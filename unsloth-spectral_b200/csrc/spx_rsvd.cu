@@ -181,28 +181,71 @@ __global__ void __launch_bounds__(256) orth_kernel(float* __restrict__ X, int ro
 // Shared memory: G [r][r] f64, L [r][r] f32 (inverse diagonal on the diagonal),
 // X [rows][r | 1] f32 (odd pitch: the row-parallel solve is bank-conflict free).
 size_t cholqr_smem(int rows, int r) {
-  return (size_t)r * r * 8 + (size_t)r * r * 4 + (size_t)rows * (r | 1) * 4;
+  return (size_t)r * (r | 1) * 8 + (size_t)r * r * 4 + (size_t)rows * (r | 1) * 4;
 }
 
+// 1 / sqrt(x) for a positive finite float64 x, in a short dependent chain: x is scaled
+// by an even power of two into [1, 4), the float32 rsqrtf seed is refined by two
+// Newton-Raphson steps y <- y (3 - m y^2) / 2 (relative error ~1e-7 -> ~1e-14 -> ~1e-16)
+// and the power of two is put back.  Subnormal x takes the library path.
+__device__ __forceinline__ double rsqrt_pos(double x) {
+  if (x < 2.2250738585072014e-308) return 1.0 / sqrt(x);
+  const int e = ((__double2hiint(x) >> 20) & 0x7ff) - 1023;
+  const int k = e >> 1;   // floor(e / 2)
+  const double m = x * __hiloint2double((1023 - 2 * k) << 20, 0);
+  double y = (double)rsqrtf((float)m);
+  y = y * fma(-0.5 * m * y, y, 1.5);
+  y = y * fma(-0.5 * m * y, y, 1.5);
+  return y * __hiloint2double((1023 - k) << 20, 0);
+}
+
+template <int RMAX>
 __global__ void __launch_bounds__(256) cholqr_kernel(float* __restrict__ X, int rows, int r) {
   extern __shared__ double smd[];
-  double* G = smd;                                       // [r][r]
-  float* Lf = reinterpret_cast<float*>(G + r * r);       // [r][r]
-  const int rp = r | 1;
+  const int rp = r | 1;                                  // odd pitches: conflict-free columns
+  double* G = smd;                                       // [r][rp]
+  float* Lf = reinterpret_cast<float*>(G + r * rp);      // [r][r]
   float* sx = Lf + r * r;                                // [rows][rp]
   __shared__ int third;
   const int i = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float* Xi = X + (int64_t)i * rows * r;
-  for (int e = tid; e < rows * r; e += blockDim.x) {
-    const int t = e / r, c = e - t * r;
-    sx[t * rp + c] = Xi[e];
+  // panel -> shared memory; float4 loads, eight in flight per thread
+  const bool vec = (rows * r) % 4 == 0;
+  if (vec) {
+    const int n4 = rows * r / 4;
+    const float4* X4 = reinterpret_cast<const float4*>(Xi);
+    for (int e0 = 0; e0 < n4; e0 += 8 * 256) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int e = e0 + u * 256 + tid;
+        v[u] = e < n4 ? X4[e] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int e = 4 * (e0 + u * 256 + tid);
+        if (e < rows * r) {
+          const float vv[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int t = (e + q) / r, c = (e + q) - t * r;
+            sx[t * rp + c] = vv[q];
+          }
+        }
+      }
+    }
+  } else {
+    for (int e = tid; e < rows * r; e += blockDim.x) {
+      const int t = e / r, c = e - t * r;
+      sx[t * rp + c] = Xi[e];
+    }
   }
   if (tid == 0) third = 0;
   __syncthreads();
   const int nb2 = (r + 1) >> 1;                // 2x2 tiles of G per side
   for (int pass = 0; pass < 3; ++pass) {
     if (pass == 2 && !third) break;
-    // ---- Gram, upper triangle by 2x2 tiles ---------------------------------------
+    // ---- Gram by 2x2 tiles of the upper triangle, stored as the lower triangle ---------
     for (int tb = tid; tb < nb2 * (nb2 + 1) / 2; tb += blockDim.x) {
       int ta = 0, rem = tb;
       while (rem >= nb2 - ta) {   // tile (ta, tb') with ta <= tb'
@@ -221,77 +264,156 @@ __global__ void __launch_bounds__(256) cholqr_kernel(float* __restrict__ X, int 
         g10 = fma(xa1, xb0, g10);
         g11 = fma(xa1, xb1, g11);
       }
-      G[a0 * r + b0] = g00; G[b0 * r + a0] = g00;
-      if (b1 != b0) { G[a0 * r + b1] = g01; G[b1 * r + a0] = g01; }
-      if (a1 != a0) { G[a1 * r + b0] = g10; G[b0 * r + a1] = g10; }
-      if (a1 != a0 && b1 != b0) { G[a1 * r + b1] = g11; G[b1 * r + a1] = g11; }
+      G[b0 * rp + a0] = g00;
+      if (b1 != b0) G[b1 * rp + a0] = g01;
+      if (a1 != a0 && a1 <= b0) G[b0 * rp + a1] = g10;
+      if (a1 != a0 && b1 != b0) G[b1 * rp + a1] = g11;
     }
     __syncthreads();
-    // ---- Cholesky G = L L^T (right-looking; each step's trailing update is spread
-    //      over the whole block) --------------------------------------------------------
+    // ---- Cholesky G = L L^T, right-looking, one block barrier per column -------------
+    // Each thread owns fixed entries (a, c), a >= c, of the lower triangle.  Step j
+    // updates every owned entry with c > j from the still unscaled column j,
+    //     G[a][c] -= G[a][j] G[c][j] / G[j][j],
+    // and scales the owned entries of column j - 1 by 1 / sqrt(pivot j - 1); column j is
+    // read and never written during step j, so the step needs no inner barrier.  The
+    // owner of diagonal entry j + 1 finishes it in step j and publishes 1 / pivot and
+    // 1 / sqrt(pivot) for the next step (one short rsqrt chain per step, not one per
+    // thread).  A pivot at or below 1e-30 of the largest diagonal entry gives a zero
+    // column.
     {
-      __shared__ double dmax_s, pmin_s, pmax_s;
+      __shared__ double dmax_s;
+      __shared__ double pivs[64], coef_s[64], scale_s[64];
       if (tid == 0) {
         double dm = 0.0;
-        for (int j = 0; j < r; ++j) dm = fmax(dm, G[j * r + j]);
+        for (int j = 0; j < r; ++j) dm = fmax(dm, G[j * rp + j]);
         dmax_s = dm;
-        pmin_s = 1e300;
-        pmax_s = 0.0;
+        const double p0 = G[0];
+        const bool ok = p0 > 1e-30 * dm && dm > 0.0;
+        const double rs = ok ? rsqrt_pos(p0) : 0.0;
+        pivs[0] = ok ? p0 : 0.0;
+        coef_s[0] = rs * rs;
+        scale_s[0] = rs;
       }
       __syncthreads();
       const double dmax = dmax_s;
+      constexpr int OWN = 9;   // r <= 64: 2080 entries over 256 threads
+      int oa[OWN], oc[OWN];
+      const int ntri = r * (r + 1) / 2;
+#pragma unroll
+      for (int q = 0; q < OWN; ++q) {
+        int e = tid + 256 * q, a = 0;
+        if (e < ntri) {
+          a = (int)((sqrt(8.0 * e + 1.0) - 1.0) * 0.5);   // row of triangle entry e
+          while (a * (a + 1) / 2 > e) --a;
+          while ((a + 1) * (a + 2) / 2 <= e) ++a;
+          oa[q] = a;
+          oc[q] = e - a * (a + 1) / 2;
+        } else {
+          oa[q] = -1;
+          oc[q] = -1;
+        }
+      }
       for (int j = 0; j < r; ++j) {
-        const double piv = G[j * r + j];
-        const bool ok = piv > 1e-30 * dmax && dmax > 0.0;
-        const double d = ok ? sqrt(piv) : 0.0;
-        // column j of L (every thread reads the pivot before anyone overwrites it)
-        __syncthreads();
-        for (int a = j + 1 + tid; a < r; a += blockDim.x) G[a * r + j] = ok ? G[a * r + j] / d : 0.0;
-        if (tid == 0) {
-          Lf[j * r + j] = ok ? (float)(1.0 / d) : 0.f;
-          if (ok) {
-            pmin_s = fmin(pmin_s, piv);
-            pmax_s = fmax(pmax_s, piv);
+        const double coef = coef_s[j], prev_scale = j > 0 ? scale_s[j - 1] : 0.0;
+#pragma unroll
+        for (int q = 0; q < OWN; ++q) {
+          const int a = oa[q], c = oc[q];
+          if (c > j) {
+            const double v = fma(-G[a * rp + j] * coef, G[c * rp + j], G[a * rp + c]);
+            G[a * rp + c] = v;
+            if (a == j + 1 && c == j + 1) {   // the next pivot is final
+              const bool ok = v > 1e-30 * dmax && dmax > 0.0;
+              const double rs = ok ? rsqrt_pos(v) : 0.0;
+              pivs[j + 1] = ok ? v : 0.0;
+              coef_s[j + 1] = rs * rs;
+              scale_s[j + 1] = rs;
+            }
+          } else if (c == j - 1 && a > c) {
+            G[a * rp + c] *= prev_scale;
           }
         }
         __syncthreads();
-        // trailing update of the lower triangle: G[a][c] -= L[a][j] L[c][j], j < c <= a
-        const int m = r - j - 1;
-        for (int e = tid; e < m * m; e += blockDim.x) {
-          const int a = j + 1 + e / m, c = j + 1 + e % m;
-          if (c <= a) G[a * r + c] = fma(-G[a * r + j], G[c * r + j], G[a * r + c]);
-        }
-        __syncthreads();
       }
-      for (int e = tid; e < r * r; e += blockDim.x) {
-        const int a = e / r, c = e - a * r;
-        if (c < a) Lf[e] = (float)G[e];
+      // L to float (strict lower part: every column c < r - 1 was scaled at step c + 1),
+      // 1 / L[j][j] on the diagonal
+#pragma unroll
+      for (int q = 0; q < OWN; ++q) {
+        const int a = oa[q], c = oc[q];
+        if (c >= 0 && a > c) Lf[a * r + c] = (float)G[a * rp + c];
       }
-      if (tid == 0 && pass == 0 && pmax_s > 1e12 * pmin_s) third = 1;
+      for (int j = tid; j < r; j += blockDim.x) Lf[j * r + j] = (float)scale_s[j];
+      if (tid == 0 && pass == 0) {
+        double pmin = 1e300, pmax = 0.0;
+        for (int j = 0; j < r; ++j)
+          if (pivs[j] > 0.0) {
+            pmin = fmin(pmin, pivs[j]);
+            pmax = fmax(pmax, pivs[j]);
+          }
+        if (pmax > 1e12 * pmin) third = 1;
+      }
     }
     __syncthreads();
-    // ---- X := X L^{-T}, one row per thread ------------------------------------------
-    for (int t = tid; t < rows; t += blockDim.x) {
-      float* xr = sx + t * rp;
-      for (int j = 0; j < r; ++j) {
-        const float* lj = Lf + j * r;
-        float v0 = xr[j], v1 = 0.f, v2 = 0.f, v3 = 0.f;   // four independent chains
-        int c = 0;
-        for (; c + 4 <= j; c += 4) {
-          v0 = fmaf(-xr[c], lj[c], v0);
-          v1 = fmaf(-xr[c + 1], lj[c + 1], v1);
-          v2 = fmaf(-xr[c + 2], lj[c + 2], v2);
-          v3 = fmaf(-xr[c + 3], lj[c + 3], v3);
-        }
-        for (; c < j; ++c) v0 = fmaf(-xr[c], lj[c], v0);
-        xr[j] = ((v0 + v1) + (v2 + v3)) * lj[j];
+    // ---- X := X L^{-T}, two rows per thread held in registers (r <= RMAX): each L
+    //      element is one broadcast load feeding four independent FMA chains ------------
+    for (int t0 = tid; t0 < rows; t0 += 2 * blockDim.x) {
+      const int t1 = t0 + blockDim.x;   // lane i reads row i: conflict-free at the odd pitch
+      const bool two = t1 < rows;
+      float* x0r = sx + t0 * rp;
+      float* x1r = two ? sx + t1 * rp : x0r;
+      float x0[RMAX], x1[RMAX];
+#pragma unroll
+      for (int c = 0; c < RMAX; ++c) {
+        x0[c] = c < r ? x0r[c] : 0.f;
+        x1[c] = c < r ? x1r[c] : 0.f;
       }
+#pragma unroll
+      for (int j = 0; j < RMAX; ++j) {
+        if (j < r) {
+          const float* lj = Lf + j * r;
+          float a0 = x0[j], a1 = 0.f, b0 = x1[j], b1 = 0.f;
+#pragma unroll
+          for (int c = 0; c + 1 < j; c += 2) {
+            const float l0 = lj[c], l1 = lj[c + 1];
+            a0 = fmaf(-x0[c], l0, a0);
+            a1 = fmaf(-x0[c + 1], l1, a1);
+            b0 = fmaf(-x1[c], l0, b0);
+            b1 = fmaf(-x1[c + 1], l1, b1);
+          }
+          if (j & 1) {
+            const float l0 = lj[j - 1];
+            a0 = fmaf(-x0[j - 1], l0, a0);
+            b0 = fmaf(-x1[j - 1], l0, b0);
+          }
+          const float dinv = lj[j];
+          x0[j] = (a0 + a1) * dinv;
+          x1[j] = (b0 + b1) * dinv;
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < RMAX; ++c)
+        if (c < r) {
+          x0r[c] = x0[c];
+          if (two) x1r[c] = x1[c];
+        }
     }
     __syncthreads();
   }
-  for (int e = tid; e < rows * r; e += blockDim.x) {
-    const int t = e / r, c = e - t * r;
-    Xi[e] = sx[t * rp + c];
+  if (vec) {
+    float4* X4 = reinterpret_cast<float4*>(Xi);
+    for (int e = tid; e < rows * r / 4; e += blockDim.x) {
+      float vv[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int t = (4 * e + q) / r, c = (4 * e + q) - t * r;
+        vv[q] = sx[t * rp + c];
+      }
+      X4[e] = make_float4(vv[0], vv[1], vv[2], vv[3]);
+    }
+  } else {
+    for (int e = tid; e < rows * r; e += blockDim.x) {
+      const int t = e / r, c = e - t * r;
+      Xi[e] = sx[t * rp + c];
+    }
   }
 }
 
@@ -552,11 +674,16 @@ static int run_chain(const spx_rsvd_args* a, const RsvdWs& w, cudaStream_t st) {
   cudaFuncSetAttribute(orth_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
   const dim3 gmx((m + 63) / 64, Nb), gmty((n + 63) / 64, Nb);
   // Cholesky-QR when its shared memory fits, classical Gram-Schmidt (CGS2) otherwise
-  cudaFuncSetAttribute(cholqr_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+  cudaFuncSetAttribute(cholqr_kernel<24>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+  cudaFuncSetAttribute(cholqr_kernel<40>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+  cudaFuncSetAttribute(cholqr_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
   auto orth = [&](float* X, int rows) {
     const size_t cq = cholqr_smem(rows, r);
-    if (cq <= 220 * 1024)
-      cholqr_kernel<<<Nb, 256, cq, st>>>(X, rows, r);
+    if (cq <= 220 * 1024) {
+      if (r <= 24) cholqr_kernel<24><<<Nb, 256, cq, st>>>(X, rows, r);
+      else if (r <= 40) cholqr_kernel<40><<<Nb, 256, cq, st>>>(X, rows, r);
+      else cholqr_kernel<64><<<Nb, 256, cq, st>>>(X, rows, r);
+    }
     else
       orth_kernel<<<Nb, 256, ((size_t)rows * r + r) * sizeof(float), st>>>(X, rows, r);
   };

@@ -162,8 +162,14 @@ __global__ void __launch_bounds__(NTH) tc_gemm_kernel(const T* __restrict__ M, i
   // power-of-two scale of the right-hand side (mode 0): max |x| * sc < 1
   float sc = 1.f, inv = 1.f;
   if (MODE == 0) {
+    // 128 r floats, r % 4 == 0: float4 loads, all in flight at once
     float mx = 0.f;
-    for (int e = tid; e < 128 * r; e += NTH) mx = fmaxf(mx, fabsf(Xi[e]));
+    const float4* X4 = reinterpret_cast<const float4*>(Xi);
+#pragma unroll 8
+    for (int e = tid; e < 32 * r; e += NTH) {
+      const float4 v = __ldg(X4 + e);
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if (lane == 0) sred[w] = mx;
@@ -192,43 +198,64 @@ __global__ void __launch_bounds__(NTH) tc_gemm_kernel(const T* __restrict__ M, i
       cp_async16(dst0 + c * 2048 + (t >> 3) * 128 + (t & 7) * 16, src0 + (int64_t)t * 128 + c * 8);
     }
   };
-  // 128 rows x r columns of f32 (row stride r) -> hi / lo K-major B tiles of rp columns:
-  // element (k, j) at (k / 8) * LB + (j / 8) * 128 + (j % 8) * 16 + (k % 8) * 2.
-  auto stage_b = [&](const float* src, uint8_t* dst, float scale) {
-    for (int e = tid; e < 16 * rp; e += NTH) {
-      const int kc = e / rp, j = e - kc * rp;
-      uint32_t hi[4], lo[4];
+  // 128 rows x r columns of f32 (row stride r, r % 4 == 0) -> hi / lo K-major B tiles of
+  // rp columns: element (k, j) at (k / 8) * LB + (j / 8) * 128 + (j % 8) * 16 + (k % 8) * 2.
+  // Item (k-chunk kc, column quad jq) of a thread: 8 rows x float4, loaded in one go
+  // (load_b) and converted / stored once the destination stage is free (store_b).
+  const int nq = rp / 4, nitem = 16 * nq;   // <= 256 items: at most 2 per thread
+  auto load_b = [&](const float* src, float4 (&v)[2][8]) {
 #pragma unroll
-      for (int u = 0; u < 8; u += 2) {
-        float x0 = 0.f, x1 = 0.f;
-        if (j < r) {
-          x0 = src[(int64_t)(8 * kc + u) * r + j] * scale;
-          x1 = src[(int64_t)(8 * kc + u + 1) * r + j] * scale;
+    for (int q = 0; q < 2; ++q) {
+      const int e = tid + NTH * q, kc = e / nq, jq = e - kc * nq;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        v[q][u] = (e < nitem && 4 * jq < r) ? __ldg(reinterpret_cast<const float4*>(src + (int64_t)(8 * kc + u) * r) + jq)
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  auto store_b = [&](const float4 (&v)[2][8], uint8_t* dst, float scale) {
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int e = tid + NTH * q, kc = e / nq, jq = e - kc * nq;
+      if (e >= nitem) continue;
+#pragma unroll
+      for (int i0 = 0; i0 < 4; ++i0) {
+        const int i = (i0 + jq) & 3;   // rotated order: fewer bank conflicts between threads
+        const int j = 4 * jq + i;
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int u = 0; u < 8; u += 2) {
+          const float x0 = (i == 0 ? v[q][u].x : i == 1 ? v[q][u].y : i == 2 ? v[q][u].z : v[q][u].w) * scale;
+          const float x1 =
+              (i == 0 ? v[q][u + 1].x : i == 1 ? v[q][u + 1].y : i == 2 ? v[q][u + 1].z : v[q][u + 1].w) * scale;
+          const uint16_t h0 = H::bits(x0), h1 = H::bits(x1);
+          const uint16_t l0 = H::bits(x0 - H::back(h0)), l1 = H::bits(x1 - H::back(h1));
+          hi[u >> 1] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+          lo[u >> 1] = (uint32_t)l0 | ((uint32_t)l1 << 16);
         }
-        const uint16_t h0 = H::bits(x0), h1 = H::bits(x1);
-        const uint16_t l0 = H::bits(x0 - H::back(h0)), l1 = H::bits(x1 - H::back(h1));
-        hi[u >> 1] = (uint32_t)h0 | ((uint32_t)h1 << 16);
-        lo[u >> 1] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+        const int off = kc * LB + (j >> 3) * 128 + (j & 7) * 16;
+        *reinterpret_cast<uint4*>(dst + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(dst + BSZ + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
       }
-      const int off = kc * LB + (j >> 3) * 128 + (j & 7) * 16;
-      *reinterpret_cast<uint4*>(dst + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-      *reinterpret_cast<uint4*>(dst + BSZ + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     }
   };
 
   const uint32_t id = idesc(H::kFmt, MODE, rp);
+  float4 vb[2][8];
   stage_a(0, 0);
   cp_async_commit();
-  stage_b(Xi, sB, sc);   // mode 0: X; mode 1: rows 0..127 of Y
+  load_b(Xi, vb);   // mode 0: X; mode 1: rows 0..127 of Y
+  store_b(vb, sB, sc);
   bool ok = true;
   for (int tt = 0; tt < nt; ++tt) {
     const int s = tt & 1;
     if (tt + 1 < nt) {
+      if (MODE == 1) load_b(Xi + (int64_t)(tt + 1) * 128 * r, vb);   // in flight across the wait
       // stage (tt + 1) & 1 was read by the MMAs of tile tt - 1
       if (tt >= 1) ok = mbar_wait(bar + 8 * ((tt + 1) & 1), (uint32_t)(((tt - 1) >> 1) & 1)) && ok;
       stage_a(tt + 1, (tt + 1) & 1);
       cp_async_commit();
-      if (MODE == 1) stage_b(Xi + (int64_t)(tt + 1) * 128 * r, sB + ((tt + 1) & 1) * 2 * BSZ, 1.f);
+      if (MODE == 1) store_b(vb, sB + ((tt + 1) & 1) * 2 * BSZ, 1.f);
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
@@ -301,7 +328,7 @@ static int launch(int mode, const T* M, int64_t ms, const float* X, float* Y, in
 
 bool rsvd_tc_supported(int dtype, const void* M, int64_t ms, int m, int n, int r) {
   if (dtype != SPX_F16 && dtype != SPX_BF16) return false;
-  if (n != 128 || m % 128 != 0 || m > 1024 || r > 64) return false;
+  if (n != 128 || m % 128 != 0 || m > 1024 || r > 64 || r % 4 != 0) return false;
   if ((m / 128) * ((r + 15) / 16 * 16) > 512) return false;   // TMEM columns of mode 0
   return (reinterpret_cast<uintptr_t>(M) & 15u) == 0 && (ms * 2) % 16 == 0;
 }
