@@ -184,23 +184,37 @@ size_t cholqr_smem(int rows, int r) {
   return (size_t)r * (r | 1) * 8 + (size_t)r * r * 4 + (size_t)rows * (r | 1) * 4;
 }
 
-// 1 / sqrt(x) for a positive finite float64 x, in a short dependent chain: x is scaled
-// by an even power of two into [1, 4), the float32 rsqrtf seed is refined by two
-// Newton-Raphson steps y <- y (3 - m y^2) / 2 (relative error ~1e-7 -> ~1e-14 -> ~1e-16)
-// and the power of two is put back.  Subnormal x takes the library path.
-__device__ __forceinline__ double rsqrt_pos(double x) {
-  if (x < 2.2250738585072014e-308) return 1.0 / sqrt(x);
+// 1 / sqrt(x) for a positive finite float64 x, to float32 accuracy (it only scales the
+// float32 copy of L): x is scaled by an even power of two into [1, 4), the rsqrtf value
+// of that is refined by one Newton-Raphson step y <- y (3 - m y^2) / 2 and the power of
+// two put back.  Subnormal x takes the library path.
+__device__ __forceinline__ float rsqrt_pos_f(double x) {
+  if (x < 2.2250738585072014e-308) return (float)(1.0 / sqrt(x));
   const int e = ((__double2hiint(x) >> 20) & 0x7ff) - 1023;
   const int k = e >> 1;   // floor(e / 2)
-  const double m = x * __hiloint2double((1023 - 2 * k) << 20, 0);
-  double y = (double)rsqrtf((float)m);
-  y = y * fma(-0.5 * m * y, y, 1.5);
-  y = y * fma(-0.5 * m * y, y, 1.5);
-  return y * __hiloint2double((1023 - k) << 20, 0);
+  const float m = (float)(x * __hiloint2double((1023 - 2 * k) << 20, 0));
+  float y = rsqrtf(m);
+  y = y * fmaf(-0.5f * m * y, y, 1.5f);
+  return (float)((double)y * __hiloint2double((1023 - k) << 20, 0));
+}
+
+// 1 / x for a positive finite float64 x to float64 accuracy: x = m 2^e with m in [1, 2),
+// the float32 reciprocal of m refined by two Newton-Raphson steps y <- y + y (1 - m y)
+// (relative error ~6e-8 -> ~4e-15 -> ~1e-16), times 2^-e.  Subnormal or huge x takes
+// the library path.
+__device__ __forceinline__ double recip_pos(double x) {
+  const int e = ((__double2hiint(x) >> 20) & 0x7ff) - 1023;
+  if (e <= -1023 || e >= 1023) return 1.0 / x;
+  const double s = __hiloint2double((1023 - e) << 20, 0);   // 2^-e
+  const double m = x * s;
+  double y = (double)__frcp_rn((float)m);
+  y = fma(y, fma(-m, y, 1.0), y);
+  y = fma(y, fma(-m, y, 1.0), y);
+  return y * s;
 }
 
 template <int RMAX>
-__global__ void __launch_bounds__(256) cholqr_kernel(float* __restrict__ X, int rows, int r) {
+__global__ void __launch_bounds__(256, RMAX <= 40 ? 2 : 1) cholqr_kernel(float* __restrict__ X, int rows, int r) {
   extern __shared__ double smd[];
   const int rp = r | 1;                                  // odd pitches: conflict-free columns
   double* G = smd;                                       // [r][rp]
@@ -254,16 +268,35 @@ __global__ void __launch_bounds__(256) cholqr_kernel(float* __restrict__ X, int 
       }
       const int a0 = 2 * ta, b0 = 2 * (ta + rem);
       const int a1 = a0 + 1 < r ? a0 + 1 : a0, b1 = b0 + 1 < r ? b0 + 1 : b0;
-      double g00 = 0.0, g01 = 0.0, g10 = 0.0, g11 = 0.0;
-#pragma unroll 4
-      for (int t = 0; t < rows; ++t) {
+      // four interleaved accumulation chains per entry (rows t mod 4): float64 FMA
+      // latency, not throughput, bounds a single chain
+      double g[4][4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) g[u][0] = g[u][1] = g[u][2] = g[u][3] = 0.0;
+      int t = 0;
+      for (; t + 4 <= rows; t += 4) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float* xr = sx + (t + u) * rp;
+          const double xa0 = xr[a0], xa1 = xr[a1], xb0 = xr[b0], xb1 = xr[b1];
+          g[u][0] = fma(xa0, xb0, g[u][0]);
+          g[u][1] = fma(xa0, xb1, g[u][1]);
+          g[u][2] = fma(xa1, xb0, g[u][2]);
+          g[u][3] = fma(xa1, xb1, g[u][3]);
+        }
+      }
+      for (; t < rows; ++t) {
         const float* xr = sx + t * rp;
         const double xa0 = xr[a0], xa1 = xr[a1], xb0 = xr[b0], xb1 = xr[b1];
-        g00 = fma(xa0, xb0, g00);
-        g01 = fma(xa0, xb1, g01);
-        g10 = fma(xa1, xb0, g10);
-        g11 = fma(xa1, xb1, g11);
+        g[0][0] = fma(xa0, xb0, g[0][0]);
+        g[0][1] = fma(xa0, xb1, g[0][1]);
+        g[0][2] = fma(xa1, xb0, g[0][2]);
+        g[0][3] = fma(xa1, xb1, g[0][3]);
       }
+      const double g00 = (g[0][0] + g[1][0]) + (g[2][0] + g[3][0]);
+      const double g01 = (g[0][1] + g[1][1]) + (g[2][1] + g[3][1]);
+      const double g10 = (g[0][2] + g[1][2]) + (g[2][2] + g[3][2]);
+      const double g11 = (g[0][3] + g[1][3]) + (g[2][3] + g[3][3]);
       G[b0 * rp + a0] = g00;
       if (b1 != b0) G[b1 * rp + a0] = g01;
       if (a1 != a0 && a1 <= b0) G[b0 * rp + a1] = g10;
@@ -276,10 +309,11 @@ __global__ void __launch_bounds__(256) cholqr_kernel(float* __restrict__ X, int 
     //     G[a][c] -= G[a][j] G[c][j] / G[j][j],
     // and scales the owned entries of column j - 1 by 1 / sqrt(pivot j - 1); column j is
     // read and never written during step j, so the step needs no inner barrier.  The
-    // owner of diagonal entry j + 1 finishes it in step j and publishes 1 / pivot and
-    // 1 / sqrt(pivot) for the next step (one short rsqrt chain per step, not one per
-    // thread).  A pivot at or below 1e-30 of the largest diagonal entry gives a zero
-    // column.
+    // owner of diagonal entry j + 1 finishes it in step j and publishes 1 / pivot (the
+    // float64 coefficient of the next step's updates) for everyone; 1 / sqrt(pivot j),
+    // which only scales the float32 copy of L, is computed meanwhile by thread 255 at
+    // float accuracy.  A pivot at or below 1e-30 of the largest diagonal entry gives a
+    // zero column.
     {
       __shared__ double dmax_s;
       __shared__ double pivs[64], coef_s[64], scale_s[64];
@@ -289,14 +323,12 @@ __global__ void __launch_bounds__(256) cholqr_kernel(float* __restrict__ X, int 
         dmax_s = dm;
         const double p0 = G[0];
         const bool ok = p0 > 1e-30 * dm && dm > 0.0;
-        const double rs = ok ? rsqrt_pos(p0) : 0.0;
         pivs[0] = ok ? p0 : 0.0;
-        coef_s[0] = rs * rs;
-        scale_s[0] = rs;
+        coef_s[0] = ok ? recip_pos(p0) : 0.0;
       }
       __syncthreads();
       const double dmax = dmax_s;
-      constexpr int OWN = 9;   // r <= 64: 2080 entries over 256 threads
+      constexpr int OWN = (RMAX * (RMAX + 1) / 2 + 255) / 256;   // triangle entries per thread
       int oa[OWN], oc[OWN];
       const int ntri = r * (r + 1) / 2;
 #pragma unroll
@@ -315,23 +347,32 @@ __global__ void __launch_bounds__(256) cholqr_kernel(float* __restrict__ X, int 
       }
       for (int j = 0; j < r; ++j) {
         const double coef = coef_s[j], prev_scale = j > 0 ? scale_s[j - 1] : 0.0;
+        double va[OWN], vb[OWN], vc[OWN];   // all operands first: the entries overlap
 #pragma unroll
         for (int q = 0; q < OWN; ++q) {
           const int a = oa[q], c = oc[q];
           if (c > j) {
-            const double v = fma(-G[a * rp + j] * coef, G[c * rp + j], G[a * rp + c]);
+            va[q] = G[a * rp + j];
+            vb[q] = G[c * rp + j];
+            vc[q] = G[a * rp + c];
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < OWN; ++q) {
+          const int a = oa[q], c = oc[q];
+          if (c > j) {
+            const double v = fma(-va[q] * coef, vb[q], vc[q]);
             G[a * rp + c] = v;
             if (a == j + 1 && c == j + 1) {   // the next pivot is final
               const bool ok = v > 1e-30 * dmax && dmax > 0.0;
-              const double rs = ok ? rsqrt_pos(v) : 0.0;
               pivs[j + 1] = ok ? v : 0.0;
-              coef_s[j + 1] = rs * rs;
-              scale_s[j + 1] = rs;
+              coef_s[j + 1] = ok ? recip_pos(v) : 0.0;
             }
           } else if (c == j - 1 && a > c) {
             G[a * rp + c] *= prev_scale;
           }
         }
+        if (tid == 255) scale_s[j] = pivs[j] > 0.0 ? (double)rsqrt_pos_f(pivs[j]) : 0.0;
         __syncthreads();
       }
       // L to float (strict lower part: every column c < r - 1 was scaled at step c + 1),
