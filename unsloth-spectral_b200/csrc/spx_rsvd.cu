@@ -174,10 +174,13 @@ __global__ void __launch_bounds__(256) orth_kernel(float* __restrict__ X, int ro
 // ---------------------------------------- in-place Cholesky-QR orthonormalisation
 // X: f32 [rows][r] per matrix, one CTA per matrix.  Each pass forms the Gram matrix
 // G = X^T X in float64 (products of two float32 values are exact in float64), factors
-// G = L L^T with one warp, and solves X := X L^{-T} row by row.  Two passes give an
+// G = L L^T in float64, and solves X := X L^{-T} row by row.  Two passes give an
 // orthonormal basis to float32 accuracy while cond(X) <= ~1e6; a third pass runs when
-// the first one saw a larger pivot spread.  A pivot at rounding level of a zero column
-// (relative 1e-30) leaves that column zero, as classical Gram-Schmidt does.
+// the first one saw a larger pivot spread.  With npass = 1 (the intermediate bases of
+// the subspace iteration, which only need to span the subspace with a well-conditioned
+// basis) the second pass runs only when the first pass's pivots spread by more than
+// 1e6 (cond(X) > 1e3).  A pivot at rounding level of a zero column (relative 1e-30)
+// leaves that column zero, as classical Gram-Schmidt does.
 // Shared memory: G [r][r] f64, L [r][r] f32 (inverse diagonal on the diagonal),
 // X [rows][r | 1] f32 (odd pitch: the row-parallel solve is bank-conflict free).
 size_t cholqr_smem(int rows, int r) {
@@ -214,13 +217,14 @@ __device__ __forceinline__ double recip_pos(double x) {
 }
 
 template <int RMAX>
-__global__ void __launch_bounds__(256, RMAX <= 40 ? 2 : 1) cholqr_kernel(float* __restrict__ X, int rows, int r) {
+__global__ void __launch_bounds__(256, RMAX <= 40 ? 2 : 1) cholqr_kernel(float* __restrict__ X, int rows, int r,
+                                                                    int npass) {
   extern __shared__ double smd[];
   const int rp = r | 1;                                  // odd pitches: conflict-free columns
   double* G = smd;                                       // [r][rp]
   float* Lf = reinterpret_cast<float*>(G + r * rp);      // [r][r]
   float* sx = Lf + r * r;                                // [rows][rp]
-  __shared__ int third;
+  __shared__ int second, third;
   const int i = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float* Xi = X + (int64_t)i * rows * r;
   // panel -> shared memory; float4 loads, eight in flight per thread
@@ -254,11 +258,14 @@ __global__ void __launch_bounds__(256, RMAX <= 40 ? 2 : 1) cholqr_kernel(float* 
       sx[t * rp + c] = Xi[e];
     }
   }
-  if (tid == 0) third = 0;
+  if (tid == 0) {
+    second = npass >= 2;
+    third = 0;
+  }
   __syncthreads();
   const int nb2 = (r + 1) >> 1;                // 2x2 tiles of G per side
   for (int pass = 0; pass < 3; ++pass) {
-    if (pass == 2 && !third) break;
+    if ((pass == 1 && !second) || (pass == 2 && !third)) break;
     // ---- Gram by 2x2 tiles of the upper triangle, stored as the lower triangle ---------
     for (int tb = tid; tb < nb2 * (nb2 + 1) / 2; tb += blockDim.x) {
       int ta = 0, rem = tb;
@@ -391,6 +398,7 @@ __global__ void __launch_bounds__(256, RMAX <= 40 ? 2 : 1) cholqr_kernel(float* 
             pmax = fmax(pmax, pivs[j]);
           }
         if (pmax > 1e12 * pmin) third = 1;
+        if (pmax > 1e6 * pmin) second = 1;
       }
     }
     __syncthreads();
@@ -718,12 +726,13 @@ static int run_chain(const spx_rsvd_args* a, const RsvdWs& w, cudaStream_t st) {
   cudaFuncSetAttribute(cholqr_kernel<24>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
   cudaFuncSetAttribute(cholqr_kernel<40>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
   cudaFuncSetAttribute(cholqr_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-  auto orth = [&](float* X, int rows) {
+  // npass 2 for the final basis Q (it feeds Bp and the lift), 1 for intermediate ones
+  auto orth = [&](float* X, int rows, int npass) {
     const size_t cq = cholqr_smem(rows, r);
     if (cq <= 220 * 1024) {
-      if (r <= 24) cholqr_kernel<24><<<Nb, 256, cq, st>>>(X, rows, r);
-      else if (r <= 40) cholqr_kernel<40><<<Nb, 256, cq, st>>>(X, rows, r);
-      else cholqr_kernel<64><<<Nb, 256, cq, st>>>(X, rows, r);
+      if (r <= 24) cholqr_kernel<24><<<Nb, 256, cq, st>>>(X, rows, r, npass);
+      else if (r <= 40) cholqr_kernel<40><<<Nb, 256, cq, st>>>(X, rows, r, npass);
+      else cholqr_kernel<64><<<Nb, 256, cq, st>>>(X, rows, r, npass);
     }
     else
       orth_kernel<<<Nb, 256, ((size_t)rows * r + r) * sizeof(float), st>>>(X, rows, r);
@@ -739,12 +748,12 @@ static int run_chain(const spx_rsvd_args* a, const RsvdWs& w, cudaStream_t st) {
     else gemm_mty_kernel<T><<<gmty, 256, 0, st>>>(M, ms, Y, Z, m, n, r);
   };
   mx(a->omega, w.Y);
-  orth(w.Y, m);
+  orth(w.Y, m, a->n_iter == 0 ? 2 : 1);
   for (int it = 0; it < a->n_iter; ++it) {
     mty(w.Y, w.Z);
-    orth(w.Z, n);
+    orth(w.Z, n, 1);
     mx(w.Z, w.Y);
-    orth(w.Y, m);
+    orth(w.Y, m, it == a->n_iter - 1 ? 2 : 1);
   }
   mty(w.Y, w.Z);
   int rc = launch_status("rsvd gemm/orth chain");
