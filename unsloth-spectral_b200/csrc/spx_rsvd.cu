@@ -473,13 +473,16 @@ __global__ void __launch_bounds__(256, RMAX <= 40 ? 2 : 1) cholqr_kernel(float* 
 // eigenvectors of Bp Bp^T.  Bp Bp^T is never formed, so small singular values keep their
 // relative accuracy in float32.  A round applies rp/2 disjoint rotations (circle
 // ordering: index rp-1 meets `round`, pair u >= 1 couples round +- u modulo rp-1), one
-// warp per rotation; a pair is rotated while |a_p . a_q| > 2e-6 |a_p| |a_q| (a few times
-// the float32 rounding of a 128-term dot product), and a sweep without rotations ends
-// the iteration.
+// 8-lane group per rotation (four rotations per warp at once); a pair is rotated while
+// |a_p . a_q| > 2e-6 |a_p| |a_q| (a few times the float32 rounding of a 128-term dot
+// product), and a sweep without rotations ends the iteration.  The squared column norms
+// are recomputed at the start of every sweep and updated in between by the exact
+// relations |a_p'|^2 = |a_p|^2 - t a_p.a_q, |a_q'|^2 = |a_q|^2 + t a_p.a_q, so a rotation
+// needs one reduction (a_p . a_q) instead of three.
 // Outputs Wk f32 [r][k], S f32 [k], Vh f32 [k][n] (descending singular values).
 size_t small_svd_smem(int n, int r) {
   const int rp = (r + 1) & ~1;
-  return ((size_t)rp * 128 + (size_t)rp * rp + rp) * sizeof(float) + rp * sizeof(int);
+  return ((size_t)rp * 128 + (size_t)rp * rp + 2 * rp) * sizeof(float) + rp * sizeof(int);
 }
 
 __global__ void __launch_bounds__(256) small_svd_kernel(const float* __restrict__ Z, float* __restrict__ Wk,
@@ -490,7 +493,8 @@ __global__ void __launch_bounds__(256) small_svd_kernel(const float* __restrict_
   float* A = smf;                     // [rp][128] columns of Bp^T (zero padded)
   float* J = A + rp * 128;            // [rp][rp] column-major: J[c * rp + a] = J(a, c)
   float* nrm = J + rp * rp;           // [rp] column norms
-  int* perm = reinterpret_cast<int*>(nrm + rp);   // [rp]
+  float* n2 = nrm + rp;               // [rp] squared column norms during the sweeps
+  int* perm = reinterpret_cast<int*>(n2 + rp);   // [rp]
   __shared__ int rotated;
   const int i = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
   const float* Zi = Z + (int64_t)i * n * r;
@@ -501,40 +505,60 @@ __global__ void __launch_bounds__(256) small_svd_kernel(const float* __restrict_
   for (int e = tid; e < rp * rp; e += blockDim.x) J[e] = (e / rp == e % rp) ? 1.f : 0.f;
   __syncthreads();
   const int np = rp / 2, nn = rp - 1;
+  const int grp = lane >> 3, gl = lane & 7;   // rotation slot of this lane's 8-lane group
+  const unsigned gmask = 0xFFu << (8 * grp);
   for (int sweep = 0; sweep < 30; ++sweep) {
+    for (int c = warp; c < rp; c += nw) {
+      const float4 v = reinterpret_cast<const float4*>(A + c * 128)[lane];
+      const float ss = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
+      if (lane == 0) n2[c] = ss;
+    }
     if (tid == 0) rotated = 0;
     __syncthreads();
     for (int round = 0; round < nn; ++round) {
-      for (int u = warp; u < np; u += nw) {
+      for (int u = 4 * warp + grp; u < np; u += 4 * nw) {
         int p = u == 0 ? round : (round + u) % nn;
         int q = u == 0 ? nn : (round - u + nn) % nn;
         if (p > q) { const int tmp = p; p = q; q = tmp; }
-        if (q >= r) continue;   // the padding column
-        float4 ap = reinterpret_cast<const float4*>(A + p * 128)[lane];
-        float4 aq = reinterpret_cast<const float4*>(A + q * 128)[lane];
-        float al = ap.x * ap.x + ap.y * ap.y + ap.z * ap.z + ap.w * ap.w;
-        float be = aq.x * aq.x + aq.y * aq.y + aq.z * aq.z + aq.w * aq.w;
-        float ga = ap.x * aq.x + ap.y * aq.y + ap.z * aq.z + ap.w * aq.w;
-        al = warp_sum(al);
-        be = warp_sum(be);
-        ga = warp_sum(ga);
+        if (q >= r) continue;   // the padding column (uniform across the group)
+        float4* cp = reinterpret_cast<float4*>(A + p * 128);
+        float4* cq = reinterpret_cast<float4*>(A + q * 128);
+        float4 ap[4], aq[4];
+        float ga = 0.f;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          ap[v] = cp[gl + 8 * v];
+          aq[v] = cq[gl + 8 * v];
+          ga += ap[v].x * aq[v].x + ap[v].y * aq[v].y + ap[v].z * aq[v].z + ap[v].w * aq[v].w;
+        }
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) ga += __shfl_xor_sync(gmask, ga, o);
+        const float al = n2[p], be = n2[q];
         if (!(fabsf(ga) > 2e-6f * sqrtf(al * be)) || ga == 0.f) continue;
         const float zeta = (be - al) / (2.f * ga);
         const float t = (zeta >= 0.f ? 1.f : -1.f) / (fabsf(zeta) + sqrtf(1.f + zeta * zeta));
         const float c = rsqrtf(1.f + t * t), sn = t * c;
-        float4 np4, nq4;
-        np4.x = c * ap.x - sn * aq.x; nq4.x = sn * ap.x + c * aq.x;
-        np4.y = c * ap.y - sn * aq.y; nq4.y = sn * ap.y + c * aq.y;
-        np4.z = c * ap.z - sn * aq.z; nq4.z = sn * ap.z + c * aq.z;
-        np4.w = c * ap.w - sn * aq.w; nq4.w = sn * ap.w + c * aq.w;
-        reinterpret_cast<float4*>(A + p * 128)[lane] = np4;
-        reinterpret_cast<float4*>(A + q * 128)[lane] = nq4;
-        for (int a = lane; a < r; a += 32) {
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          float4 np4, nq4;
+          np4.x = c * ap[v].x - sn * aq[v].x; nq4.x = sn * ap[v].x + c * aq[v].x;
+          np4.y = c * ap[v].y - sn * aq[v].y; nq4.y = sn * ap[v].y + c * aq[v].y;
+          np4.z = c * ap[v].z - sn * aq[v].z; nq4.z = sn * ap[v].z + c * aq[v].z;
+          np4.w = c * ap[v].w - sn * aq[v].w; nq4.w = sn * ap[v].w + c * aq[v].w;
+          cp[gl + 8 * v] = np4;
+          cq[gl + 8 * v] = nq4;
+        }
+        for (int a = gl; a < r; a += 8) {
           const float jp = J[p * rp + a], jq = J[q * rp + a];
           J[p * rp + a] = c * jp - sn * jq;
           J[q * rp + a] = sn * jp + c * jq;
         }
-        if (lane == 0) rotated = 1;
+        __syncwarp(gmask);
+        if (gl == 0) {
+          n2[p] = al - t * ga;
+          n2[q] = be + t * ga;
+          rotated = 1;
+        }
       }
       __syncthreads();
     }
@@ -570,29 +594,71 @@ __global__ void __launch_bounds__(256) small_svd_kernel(const float* __restrict_
 }
 
 // ------------------------------------------------- lift, C = U S, INT8 quantisation
+// Shared memory of lift_quant_kernel: W^T [k][r4], C [m][k + 1] (odd pitch: the
+// row-per-thread writes are bank-conflict free).
+size_t lift_smem(int m, int r, int k) {
+  const int r4 = (r + 3) & ~3;
+  return ((size_t)k * r4 + (size_t)m * (k + 1)) * sizeof(float);
+}
+
+// One CTA per matrix.  U = Q W row by row: a thread holds a row of Q in registers and
+// reads W^T from shared memory four entries at a time; C = U S stays in shared memory
+// for the INT8 pass.
+template <int RMAX>
 __global__ void __launch_bounds__(256) lift_quant_kernel(LiftParams p) {
   extern __shared__ float sm[];
   const int m = p.m, r = p.r, k = p.k, n = p.n;
-  float* sw = sm;                 // [r][k]
-  float* sc = sw + r * k;         // [m][k]  C = U * S
+  const int r4 = (r + 3) & ~3, kc = k + 1;
+  float* swt = sm;                // [k][r4] W^T, zero padded
+  float* sc = swt + k * r4;       // [m][kc]  C = U * S
   __shared__ float ss[64];
   __shared__ float red[3][32];
   const int i = blockIdx.x;
-  for (int e = threadIdx.x; e < r * k; e += blockDim.x) sw[e] = p.Wk[(int64_t)i * r * k + e];
+  for (int e = threadIdx.x; e < k * r4; e += blockDim.x) {
+    const int j = e / r4, a = e - j * r4;
+    swt[e] = a < r ? p.Wk[(int64_t)i * r * k + (int64_t)a * k + j] : 0.f;
+  }
   if (threadIdx.x < k) ss[threadIdx.x] = p.Sw[(int64_t)i * k + threadIdx.x];
   __syncthreads();
   const float* Qi = p.Q + (int64_t)i * m * r;
   float mn = INFINITY, mx = -INFINITY, am = 0.f;
-  for (int e = threadIdx.x; e < m * k; e += blockDim.x) {
-    const int t = e / k, j = e - t * k;
-    float u = 0.f;
-    for (int a = 0; a < r; ++a) u = fmaf(Qi[(int64_t)t * r + a], sw[a * k + j], u);
-    if (p.U) p.U[(int64_t)i * m * k + e] = u;
-    const float c = u * ss[j];
-    sc[e] = c;
-    mn = fminf(mn, c);
-    mx = fmaxf(mx, c);
-    am = fmaxf(am, fabsf(c));
+  for (int t = threadIdx.x; t < m; t += blockDim.x) {
+    float q[RMAX];
+    if ((r & 3) == 0) {   // rows of 16-byte multiples: float4 loads
+      const float4* q4 = reinterpret_cast<const float4*>(Qi + (int64_t)t * r);
+#pragma unroll
+      for (int a = 0; a < RMAX; a += 4) {
+        const float4 v = a < r ? __ldg(q4 + (a >> 2)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        q[a] = v.x;
+        q[a + 1] = v.y;
+        q[a + 2] = v.z;
+        q[a + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int a = 0; a < RMAX; ++a) q[a] = a < r ? __ldg(Qi + (int64_t)t * r + a) : 0.f;
+    }
+    for (int j = 0; j < k; ++j) {
+      const float4* w4 = reinterpret_cast<const float4*>(swt + j * r4);
+      float u0 = 0.f, u1 = 0.f;
+#pragma unroll
+      for (int a = 0; a < RMAX; a += 4) {
+        if (a < r) {
+          const float4 w = w4[a >> 2];
+          u0 = fmaf(q[a], w.x, u0);
+          u1 = fmaf(q[a + 1], w.y, u1);
+          u0 = fmaf(q[a + 2], w.z, u0);
+          u1 = fmaf(q[a + 3], w.w, u1);
+        }
+      }
+      const float u = u0 + u1;
+      if (p.U) p.U[(int64_t)i * m * k + (int64_t)t * k + j] = u;
+      const float c = u * ss[j];
+      sc[t * kc + j] = c;
+      mn = fminf(mn, c);
+      mx = fmaxf(mx, c);
+      am = fmaxf(am, fabsf(c));
+    }
   }
   for (int o = 16; o > 0; o >>= 1) {
     mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
@@ -632,7 +698,7 @@ __global__ void __launch_bounds__(256) lift_quant_kernel(LiftParams p) {
       int t, j;
       if (p.codes_j_stride == 1 || p.codes_tiled) { t = e / kp; j = e - t * kp; }
       else { j = e / m; t = e - j * m; }
-      const int8_t v = j < k ? (int8_t)(int)rintf(__fdiv_rn(sc[t * k + j], scale)) : (int8_t)0;
+      const int8_t v = j < k ? (int8_t)(int)rintf(__fdiv_rn(sc[t * kc + j], scale)) : (int8_t)0;
       if (p.codes_tiled)
         ci[vtile_offset(j, t, kp)] = v;
       else
@@ -691,8 +757,7 @@ static int validate(const spx_rsvd_args* a) {
   SPX_REQUIRE(a->n_iter >= 0 && a->n_iter <= 8, SPX_ERR_SHAPE, "n_iter %d outside [0, 8]", a->n_iter);
   SPX_REQUIRE(dtype_ok(a->in_dtype), SPX_ERR_UNSUPPORTED, "bad input dtype");
   SPX_REQUIRE((size_t)a->m * a->r * 4 + 4 * 64 <= 200 * 1024, SPX_ERR_UNSUPPORTED, "m*r too large for one CTA");
-  SPX_REQUIRE((size_t)a->m * a->k * 4 + (size_t)a->r * a->k * 4 <= 200 * 1024, SPX_ERR_UNSUPPORTED,
-              "m*k too large for one CTA");
+  SPX_REQUIRE(lift_smem(a->m, a->r, a->k) <= 200 * 1024, SPX_ERR_UNSUPPORTED, "m*k too large for one CTA");
   if (a->num_mats == 0) return SPX_OK;
   SPX_REQUIRE(a->M && a->omega, SPX_ERR_NULL, "M and omega are required");
   SPX_REQUIRE(a->M_mat_stride == 0 || a->M_mat_stride >= (int64_t)a->m * a->n, SPX_ERR_SHAPE,
@@ -777,9 +842,13 @@ static int run_chain(const spx_rsvd_args* a, const RsvdWs& w, cudaStream_t st) {
   lp.qscale = a->qscale; lp.scale_mat_stride = a->scale_mat_stride;
   lp.qminmax = a->qminmax; lp.minmax_mat_stride = a->minmax_mat_stride;
   lp.basis = a->basis; lp.basis_dtype = a->basis_dtype; lp.basis_mat_stride = a->basis_mat_stride;
-  const size_t slq = ((size_t)r * k + (size_t)m * k) * sizeof(float);
-  cudaFuncSetAttribute(lift_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)slq);
-  lift_quant_kernel<<<Nb, 256, slq, st>>>(lp);
+  const size_t slq = lift_smem(m, r, k);
+  cudaFuncSetAttribute(lift_quant_kernel<24>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)slq);
+  cudaFuncSetAttribute(lift_quant_kernel<40>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)slq);
+  cudaFuncSetAttribute(lift_quant_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)slq);
+  if (r <= 24) lift_quant_kernel<24><<<Nb, 256, slq, st>>>(lp);
+  else if (r <= 40) lift_quant_kernel<40><<<Nb, 256, slq, st>>>(lp);
+  else lift_quant_kernel<64><<<Nb, 256, slq, st>>>(lp);
   return launch_status("lift_quant_kernel");
 }
 
