@@ -159,32 +159,6 @@ __global__ void __launch_bounds__(NTH) tc_gemm_kernel(const T* __restrict__ M, i
     *sbad = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  // power-of-two scale of the right-hand side (mode 0): max |x| * sc < 1
-  float sc = 1.f, inv = 1.f;
-  if (MODE == 0) {
-    // 128 r floats, r % 4 == 0: float4 loads, all in flight at once
-    float mx = 0.f;
-    const float4* X4 = reinterpret_cast<const float4*>(Xi);
-#pragma unroll 8
-    for (int e = tid; e < 32 * r; e += NTH) {
-      const float4 v = __ldg(X4 + e);
-      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (lane == 0) sred[w] = mx;
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tbase = *tslot;
-  if (MODE == 0) {
-    const float mx = fmaxf(fmaxf(sred[0], sred[1]), fmaxf(sred[2], sred[3]));
-    int e2 = 0;
-    if (mx > 0.f && isfinite(mx)) frexpf(mx, &e2);   // mx = f 2^e2, 0.5 <= f < 1
-    sc = ldexpf(1.f, -e2);
-    inv = ldexpf(1.f, e2);
-  }
 
   // 128 x 128 tile tt of M -> A stage s (chunk layout above); 16 cp.async per thread.
   // A warp covers 8 rows x 4 chunks: 64 contiguous bytes per row, conflict-free stores.
@@ -245,6 +219,31 @@ __global__ void __launch_bounds__(NTH) tc_gemm_kernel(const T* __restrict__ M, i
   stage_a(0, 0);
   cp_async_commit();
   load_b(Xi, vb);   // mode 0: X; mode 1: rows 0..127 of Y
+  // power-of-two scale of the right-hand side (mode 0): max |x| * sc < 1, from the
+  // registers just loaded (the items cover X once)
+  float sc = 1.f, inv = 1.f;
+  if (MODE == 0) {
+    float mx = 0.f;
+#pragma unroll
+    for (int q = 0; q < 2; ++q)
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(vb[q][u].x), fabsf(vb[q][u].y)), fmaxf(fabsf(vb[q][u].z), fabsf(vb[q][u].w))));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) sred[w] = mx;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+  if (MODE == 0) {
+    const float mx = fmaxf(fmaxf(sred[0], sred[1]), fmaxf(sred[2], sred[3]));
+    int e2 = 0;
+    if (mx > 0.f && isfinite(mx)) frexpf(mx, &e2);   // mx = f 2^e2, 0.5 <= f < 1
+    sc = ldexpf(1.f, -e2);
+    inv = ldexpf(1.f, e2);
+  }
   store_b(vb, sB, sc);
   bool ok = true;
   for (int tt = 0; tt < nt; ++tt) {
@@ -286,18 +285,34 @@ __global__ void __launch_bounds__(NTH) tc_gemm_kernel(const T* __restrict__ M, i
   __syncthreads();
   const bool bad = *sbad != 0;
 
-  // epilogue: thread = accumulator row (TMEM lane 32 w + lane)
+  // epilogue: thread = accumulator row (TMEM lane 32 w + lane).  A tile's 128 output
+  // rows are one contiguous [128][r] block of global memory: rows go to shared memory
+  // (the A stages are free now) at pitch r + 4 (conflict-free float4 writes), then the
+  // block is copied out with coalesced float4 stores.
   const int row = 32 * w + lane;
   const uint32_t tl = tbase + ((uint32_t)(32 * w) << 16);
+  const int sp = r + 4, nq4 = r / 4;
+  float* stg = reinterpret_cast<float*>(sA);
   for (int tt = 0; tt < (MODE == 0 ? nt : 1); ++tt) {
-    float* dst = Yi + (int64_t)(MODE == 0 ? tt * 128 + row : row) * r;
+    float* srow = stg + row * sp;
     for (int cb = 0; cb < rp; cb += 16) {
       float v[16];
       tmem_ld16(tl + (uint32_t)(MODE == 0 ? tt * rp + cb : cb), v);
 #pragma unroll
-      for (int u = 0; u < 16; ++u)
-        if (cb + u < r) dst[cb + u] = bad ? __int_as_float(0x7fc00000) : v[u] * inv;
+      for (int u = 0; u < 16; u += 4)
+        if (cb + u < r) {
+          float4 o = make_float4(v[u] * inv, v[u + 1] * inv, v[u + 2] * inv, v[u + 3] * inv);
+          if (bad) o = make_float4(__int_as_float(0x7fc00000), 0.f, 0.f, 0.f);
+          *reinterpret_cast<float4*>(srow + cb + u) = o;
+        }
     }
+    __syncthreads();
+    float4* dst4 = reinterpret_cast<float4*>(Yi + (int64_t)(MODE == 0 ? tt * 128 : 0) * r);
+    for (int g = tid; g < 128 * nq4; g += NTH) {
+      const int rr = g / nq4, c4 = g - rr * nq4;
+      dst4[g] = *reinterpret_cast<const float4*>(stg + rr * sp + 4 * c4);
+    }
+    __syncthreads();
   }
   tc_fence_before();
   __syncthreads();
