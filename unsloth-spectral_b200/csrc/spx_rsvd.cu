@@ -201,10 +201,10 @@ __device__ __forceinline__ float rsqrt_pos_f(double x) {
   return (float)((double)y * __hiloint2double((1023 - k) << 20, 0));
 }
 
-// 1 / x for a positive finite float64 x to float64 accuracy: x = m 2^e with m in [1, 2),
-// the float32 reciprocal of m refined by two Newton-Raphson steps y <- y + y (1 - m y)
-// (relative error ~6e-8 -> ~4e-15 -> ~1e-16), times 2^-e.  Subnormal or huge x takes
-// the library path.
+// 1 / x for a positive finite float64 x: x = m 2^e with m in [1, 2), the float32
+// reciprocal of m refined by one Newton-Raphson step y <- y + y (1 - m y) (relative
+// error ~6e-8 -> ~4e-15, far below the float32 result the factor feeds), times 2^-e.
+// Subnormal or huge x takes the library path.
 __device__ __forceinline__ double recip_pos(double x) {
   const int e = ((__double2hiint(x) >> 20) & 0x7ff) - 1023;
   if (e <= -1023 || e >= 1023) return 1.0 / x;
@@ -212,13 +212,14 @@ __device__ __forceinline__ double recip_pos(double x) {
   const double m = x * s;
   double y = (double)__frcp_rn((float)m);
   y = fma(y, fma(-m, y, 1.0), y);
-  y = fma(y, fma(-m, y, 1.0), y);
   return y * s;
 }
 
-template <int RMAX>
-__global__ void __launch_bounds__(256, RMAX <= 40 ? 2 : 1) cholqr_kernel(float* __restrict__ X, int rows, int r,
-                                                                    int npass) {
+// NT threads per CTA: 256 for tall panels, 128 for panels of <= 128 rows (their shared
+// memory is small, so twice as many CTAs - and Cholesky chains - fit on an SM).
+template <int RMAX, int NT>
+__global__ void __launch_bounds__(NT, (RMAX <= 40 ? 2 : 1) * (256 / NT)) cholqr_kernel(float* __restrict__ X,
+                                                                                     int rows, int r, int npass) {
   extern __shared__ double smd[];
   const int rp = r | 1;                                  // odd pitches: conflict-free columns
   double* G = smd;                                       // [r][rp]
@@ -232,16 +233,16 @@ __global__ void __launch_bounds__(256, RMAX <= 40 ? 2 : 1) cholqr_kernel(float* 
   if (vec) {
     const int n4 = rows * r / 4;
     const float4* X4 = reinterpret_cast<const float4*>(Xi);
-    for (int e0 = 0; e0 < n4; e0 += 8 * 256) {
+    for (int e0 = 0; e0 < n4; e0 += 8 * NT) {
       float4 v[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const int e = e0 + u * 256 + tid;
+        const int e = e0 + u * NT + tid;
         v[u] = e < n4 ? X4[e] : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const int e = 4 * (e0 + u * 256 + tid);
+        const int e = 4 * (e0 + u * NT + tid);
         if (e < rows * r) {
           const float vv[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
 #pragma unroll
@@ -335,12 +336,12 @@ __global__ void __launch_bounds__(256, RMAX <= 40 ? 2 : 1) cholqr_kernel(float* 
       }
       __syncthreads();
       const double dmax = dmax_s;
-      constexpr int OWN = (RMAX * (RMAX + 1) / 2 + 255) / 256;   // triangle entries per thread
+      constexpr int OWN = (RMAX * (RMAX + 1) / 2 + NT - 1) / NT;   // triangle entries per thread
       int oa[OWN], oc[OWN];
       const int ntri = r * (r + 1) / 2;
 #pragma unroll
       for (int q = 0; q < OWN; ++q) {
-        int e = tid + 256 * q, a = 0;
+        int e = tid + NT * q, a = 0;
         if (e < ntri) {
           a = (int)((sqrt(8.0 * e + 1.0) - 1.0) * 0.5);   // row of triangle entry e
           while (a * (a + 1) / 2 > e) --a;
@@ -379,7 +380,7 @@ __global__ void __launch_bounds__(256, RMAX <= 40 ? 2 : 1) cholqr_kernel(float* 
             G[a * rp + c] *= prev_scale;
           }
         }
-        if (tid == 255) scale_s[j] = pivs[j] > 0.0 ? (double)rsqrt_pos_f(pivs[j]) : 0.0;
+        if (tid == NT - 1) scale_s[j] = pivs[j] > 0.0 ? (double)rsqrt_pos_f(pivs[j]) : 0.0;
         __syncthreads();
       }
       // L to float (strict lower part: every column c < r - 1 was scaled at step c + 1),
@@ -788,16 +789,25 @@ static int run_chain(const spx_rsvd_args* a, const RsvdWs& w, cudaStream_t st) {
   cudaFuncSetAttribute(orth_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
   const dim3 gmx((m + 63) / 64, Nb), gmty((n + 63) / 64, Nb);
   // Cholesky-QR when its shared memory fits, classical Gram-Schmidt (CGS2) otherwise
-  cudaFuncSetAttribute(cholqr_kernel<24>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-  cudaFuncSetAttribute(cholqr_kernel<40>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-  cudaFuncSetAttribute(cholqr_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+  cudaFuncSetAttribute(cholqr_kernel<24, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+  cudaFuncSetAttribute(cholqr_kernel<40, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+  cudaFuncSetAttribute(cholqr_kernel<64, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+  cudaFuncSetAttribute(cholqr_kernel<24, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+  cudaFuncSetAttribute(cholqr_kernel<40, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+  cudaFuncSetAttribute(cholqr_kernel<64, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
   // npass 2 for the final basis Q (it feeds Bp and the lift), 1 for intermediate ones
   auto orth = [&](float* X, int rows, int npass) {
     const size_t cq = cholqr_smem(rows, r);
     if (cq <= 220 * 1024) {
-      if (r <= 24) cholqr_kernel<24><<<Nb, 256, cq, st>>>(X, rows, r, npass);
-      else if (r <= 40) cholqr_kernel<40><<<Nb, 256, cq, st>>>(X, rows, r, npass);
-      else cholqr_kernel<64><<<Nb, 256, cq, st>>>(X, rows, r, npass);
+      if (rows <= 128) {
+        if (r <= 24) cholqr_kernel<24, 128><<<Nb, 128, cq, st>>>(X, rows, r, npass);
+        else if (r <= 40) cholqr_kernel<40, 128><<<Nb, 128, cq, st>>>(X, rows, r, npass);
+        else cholqr_kernel<64, 128><<<Nb, 128, cq, st>>>(X, rows, r, npass);
+      } else {
+        if (r <= 24) cholqr_kernel<24, 256><<<Nb, 256, cq, st>>>(X, rows, r, npass);
+        else if (r <= 40) cholqr_kernel<40, 256><<<Nb, 256, cq, st>>>(X, rows, r, npass);
+        else cholqr_kernel<64, 256><<<Nb, 256, cq, st>>>(X, rows, r, npass);
+      }
     }
     else
       orth_kernel<<<Nb, 256, ((size_t)rows * r + r) * sizeof(float), st>>>(X, rows, r);
