@@ -467,6 +467,335 @@ __global__ void __launch_bounds__(NT, (RMAX <= 40 ? 2 : 1) * (256 / NT)) cholqr_
   }
 }
 
+// ------------------------------- Cholesky-QR of tall panels as three kernels per pass
+// A panel of many rows fills shared memory, which caps the fused kernel at two CTAs -
+// two serial Cholesky chains - per SM.  For panels of more than 128 rows each pass runs
+// as: a streaming float64 Gram kernel (the panel passes through shared memory in
+// 128-row chunks), a Cholesky-only kernel (one small CTA per matrix, many per SM), and
+// a row-parallel triangular solve.  np[i] holds the number of passes matrix i needs:
+// the Gram kernel of pass 0 sets it to the requested count, the Cholesky of pass 0
+// raises it from the pivot spread (> 1e6: two passes, > 1e12: three), and every kernel
+// of a later pass returns at once for a matrix that needs no more.
+constexpr int kGramChunk = 128;
+// Gram tiling: 4 x 4 tiles of the upper triangle, each split over S interleaved row
+// subsets (rows t = s mod S of every chunk) so that ~256 threads are busy; 4 x 4 tiles
+// halve the float32 -> float64 conversions per FMA of 2 x 2 tiles.  The S partial sums
+// of an entry are added in a fixed order, so the result is deterministic.
+template <int RMAX>
+struct GramTiling {
+  static constexpr int NB4 = (RMAX + 3) / 4;
+  static constexpr int NTILE = NB4 * (NB4 + 1) / 2;
+  static constexpr int S = NTILE * 8 <= 256 ? 8 : NTILE * 4 <= 256 ? 4 : NTILE * 2 <= 256 ? 2 : 1;
+  static constexpr int TPT = (NTILE * S + 255) / 256;   // items per thread
+};
+size_t gram_smem(int r) {
+  const int rmax = r <= 24 ? 24 : r <= 40 ? 40 : 64;
+  const int nb4 = (rmax + 3) / 4, ntile = nb4 * (nb4 + 1) / 2;
+  const int S = ntile * 8 <= 256 ? 8 : ntile * 4 <= 256 ? 4 : ntile * 2 <= 256 ? 2 : 1;
+  return (size_t)kGramChunk * (r | 1) * sizeof(float) + (size_t)S * ntile * 16 * sizeof(double);
+}
+
+template <int RMAX>
+__global__ void __launch_bounds__(256) gram_kernel(const float* __restrict__ X, double* __restrict__ Gw,
+                                                   int* __restrict__ np, int pass, int npass0, int rows, int r) {
+  using GT = GramTiling<RMAX>;
+  const int i = blockIdx.x, tid = threadIdx.x;
+  if (pass == 0) {
+    if (tid == 0) np[i] = npass0;
+  } else if (pass >= np[i]) {
+    return;
+  }
+  extern __shared__ __align__(16) float gsm[];
+  const int rp = r | 1;
+  float* sxc = gsm;                                                        // [kGramChunk][rp]
+  double* red = reinterpret_cast<double*>(gsm + ((kGramChunk * rp + 3) & ~3));   // [S][NTILE][16]
+  // items: (tile, row subset); tile (ta, tb), ta <= tb, of 4 x 4 blocks
+  int it_ta[GT::TPT], it_tb[GT::TPT], it_s[GT::TPT];
+#pragma unroll
+  for (int q = 0; q < GT::TPT; ++q) {
+    const int item = tid + 256 * q;
+    if (item < GT::NTILE * GT::S) {
+      int tb = item / GT::S, ta = 0;
+      it_s[q] = item - tb * GT::S;
+      while (tb >= GT::NB4 - ta) {
+        tb -= GT::NB4 - ta;
+        ++ta;
+      }
+      it_ta[q] = ta;
+      it_tb[q] = ta + tb;
+    } else {
+      it_ta[q] = -1;
+      it_tb[q] = -1;
+      it_s[q] = 0;
+    }
+  }
+  double g[GT::TPT][16];
+#pragma unroll
+  for (int q = 0; q < GT::TPT; ++q)
+#pragma unroll
+    for (int e = 0; e < 16; ++e) g[q][e] = 0.0;
+  const float* Xi = X + (int64_t)i * rows * r;
+  for (int c0 = 0; c0 < rows; c0 += kGramChunk) {
+    const int nrow = min(kGramChunk, rows - c0);
+    __syncthreads();
+    if ((r & 3) == 0) {   // float4 loads, all of a thread's in flight at once
+      const int n4 = nrow * r / 4;
+      const float4* X4 = reinterpret_cast<const float4*>(Xi + (int64_t)c0 * r);
+      constexpr int U = (kGramChunk * RMAX / 4 + 255) / 256;
+      float4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int e = tid + 256 * u;
+        v[u] = e < n4 ? __ldg(X4 + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int e = 4 * (tid + 256 * u);
+        if (e < nrow * r) {
+          const int t = e / r, c = e - t * r;   // r % 4 == 0: the four stay in row t
+          float* d = sxc + t * rp + c;
+          d[0] = v[u].x;
+          d[1] = v[u].y;
+          d[2] = v[u].z;
+          d[3] = v[u].w;
+        }
+      }
+    } else {
+      for (int e = tid; e < nrow * r; e += 256) {
+        const int t = e / r, c = e - t * r;
+        sxc[t * rp + c] = Xi[(int64_t)c0 * r + e];
+      }
+    }
+    // zero the columns past r of the last 4-block (read by edge tiles, never stored)
+    for (int e = tid; e < nrow * (4 * GT::NB4 - r); e += 256) {
+      const int w4 = 4 * GT::NB4 - r, t = e / w4, c = r + (e - t * w4);
+      if (c < rp) sxc[t * rp + c] = 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < GT::TPT; ++q) {
+      if (it_ta[q] < 0) continue;
+      const int a0 = 4 * it_ta[q], b0 = 4 * it_tb[q];
+      for (int t = it_s[q]; t < nrow; t += GT::S) {
+        const float* xr = sxc + t * rp;
+        double xa[4], xb[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          xa[u] = a0 + u < rp ? xr[a0 + u] : 0.0;
+          xb[u] = b0 + u < rp ? xr[b0 + u] : 0.0;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int v = 0; v < 4; ++v) g[q][4 * u + v] = fma(xa[u], xb[v], g[q][4 * u + v]);
+      }
+    }
+  }
+  // partial sums -> shared memory; fixed-order sum over the S row subsets
+#pragma unroll
+  for (int q = 0; q < GT::TPT; ++q) {
+    if (it_ta[q] < 0) continue;
+    const int tile = (tid + 256 * q) / GT::S;
+    double* dst = red + ((int64_t)it_s[q] * GT::NTILE + tile) * 16;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) dst[e] = g[q][e];
+  }
+  __syncthreads();
+  double* Gi = Gw + (int64_t)i * r * r;
+  for (int e = tid; e < GT::NTILE * 16; e += 256) {
+    const int tile = e >> 4, u = (e >> 2) & 3, v = e & 3;
+    double sum = 0.0;
+    for (int s2 = 0; s2 < GT::S; ++s2) sum += red[((int64_t)s2 * GT::NTILE + tile) * 16 + (e & 15)];
+    // tile index -> (ta, tb)
+    int tb = tile, ta = 0;
+    while (tb >= GT::NB4 - ta) {
+      tb -= GT::NB4 - ta;
+      ++ta;
+    }
+    tb += ta;
+    const int col = 4 * ta + u, row = 4 * tb + v;   // entry (a, b) = (col, row), a <= b for lower storage
+    if (row < r && col < r && col <= row) Gi[row * r + col] = sum;
+  }
+}
+
+// Factor G = L L^T of one matrix per CTA (the block-parallel right-looking scheme of
+// cholqr_kernel, 128 threads); writes Lw [r][r] f32: strict lower part L, 1 / L[j][j] on
+// the diagonal.  In pass 0 the pivot spread raises np[i].
+template <int RMAX>
+__global__ void __launch_bounds__(128) chol_kernel(const double* __restrict__ Gw, float* __restrict__ Lw,
+                                                   int* __restrict__ np, int pass, int r) {
+  constexpr int NT = 128;
+  const int i = blockIdx.x, tid = threadIdx.x;
+  if (pass > 0 && pass >= np[i]) return;
+  const int rp = r | 1;
+  __shared__ double G[RMAX * (RMAX | 1)];
+  __shared__ double dmax_s;
+  __shared__ double pivs[RMAX], coef_s[RMAX], scale_s[RMAX];
+  const double* Gi = Gw + (int64_t)i * r * r;
+  for (int e = tid; e < r * r; e += NT) {
+    const int a = e / r, c = e - a * r;
+    if (c <= a) G[a * rp + c] = Gi[e];
+  }
+  __syncthreads();
+  if (tid == 0) {
+    double dm = 0.0;
+    for (int j = 0; j < r; ++j) dm = fmax(dm, G[j * rp + j]);
+    dmax_s = dm;
+    const double p0 = G[0];
+    const bool ok = p0 > 1e-30 * dm && dm > 0.0;
+    pivs[0] = ok ? p0 : 0.0;
+    coef_s[0] = ok ? recip_pos(p0) : 0.0;
+  }
+  __syncthreads();
+  const double dmax = dmax_s;
+  constexpr int OWN = (RMAX * (RMAX + 1) / 2 + NT - 1) / NT;
+  int oa[OWN], oc[OWN];
+  const int ntri = r * (r + 1) / 2;
+#pragma unroll
+  for (int q = 0; q < OWN; ++q) {
+    int e = tid + NT * q, a = 0;
+    if (e < ntri) {
+      a = (int)((sqrt(8.0 * e + 1.0) - 1.0) * 0.5);
+      while (a * (a + 1) / 2 > e) --a;
+      while ((a + 1) * (a + 2) / 2 <= e) ++a;
+      oa[q] = a;
+      oc[q] = e - a * (a + 1) / 2;
+    } else {
+      oa[q] = -1;
+      oc[q] = -1;
+    }
+  }
+  for (int j = 0; j < r; ++j) {
+    const double coef = coef_s[j], prev_scale = j > 0 ? scale_s[j - 1] : 0.0;
+#pragma unroll
+    for (int q = 0; q < OWN; ++q) {
+      const int a = oa[q], c = oc[q];
+      if (c > j) {
+        const double v = fma(-G[a * rp + j] * coef, G[c * rp + j], G[a * rp + c]);
+        G[a * rp + c] = v;
+        if (a == j + 1 && c == j + 1) {
+          const bool ok = v > 1e-30 * dmax && dmax > 0.0;
+          pivs[j + 1] = ok ? v : 0.0;
+          coef_s[j + 1] = ok ? recip_pos(v) : 0.0;
+        }
+      } else if (c == j - 1 && a > c) {
+        G[a * rp + c] *= prev_scale;
+      }
+    }
+    if (tid == NT - 1) scale_s[j] = pivs[j] > 0.0 ? (double)rsqrt_pos_f(pivs[j]) : 0.0;
+    __syncthreads();
+  }
+  float* Li = Lw + (int64_t)i * r * r;
+#pragma unroll
+  for (int q = 0; q < OWN; ++q) {
+    const int a = oa[q], c = oc[q];
+    if (c >= 0 && a > c) Li[a * r + c] = (float)G[a * rp + c];
+  }
+  for (int j = tid; j < r; j += NT) Li[j * r + j] = (float)scale_s[j];
+  if (tid == 0 && pass == 0) {
+    double pmin = 1e300, pmax = 0.0;
+    for (int j = 0; j < r; ++j)
+      if (pivs[j] > 0.0) {
+        pmin = fmin(pmin, pivs[j]);
+        pmax = fmax(pmax, pivs[j]);
+      }
+    int n = np[i];
+    if (pmax > 1e6 * pmin && n < 2) n = 2;
+    if (pmax > 1e12 * pmin) n = 3;
+    np[i] = n;
+  }
+}
+
+// X := X L^{-T}, grid (matrices, 128-row chunks), 128 threads.  The chunk is staged in
+// shared memory with coalesced float4 copies (odd row pitch: a thread reads its own row
+// conflict-free), each thread substitutes its row in registers reading L four entries
+// at a time (pitch rounded up to 4), and the chunk is copied back the same way.
+size_t trsolve_smem(int r) { return ((size_t)r * ((r + 3) & ~3) + 128 * (size_t)(r | 1)) * sizeof(float); }
+
+template <int RMAX>
+__global__ void __launch_bounds__(128) trsolve_kernel(float* __restrict__ X, const float* __restrict__ Lw,
+                                                      const int* __restrict__ np, int pass, int rows, int r) {
+  const int i = blockIdx.x, tid = threadIdx.x;
+  if (pass > 0 && pass >= np[i]) return;
+  constexpr int R4 = (RMAX + 3) & ~3;
+  extern __shared__ __align__(16) float tsm[];
+  const int r4 = (r + 3) & ~3, rp = r | 1;
+  float* Ls = tsm;             // [r][r4]
+  float* sx = tsm + r * r4;    // [128][rp]
+  const float* Li = Lw + (int64_t)i * r * r;
+  for (int e = tid; e < r * r4; e += 128) {
+    const int j = e / r4, c = e - j * r4;
+    Ls[e] = c < r ? Li[j * r + c] : 0.f;
+  }
+  const int t0 = blockIdx.y * 128, nrow = min(128, rows - t0);
+  float* Xc = X + ((int64_t)i * rows + t0) * r;
+  const bool vec = (r & 3) == 0;
+  if (vec) {
+    const float4* X4 = reinterpret_cast<const float4*>(Xc);
+    for (int e = tid; e < nrow * r / 4; e += 128) {
+      const float4 v = X4[e];
+      const int t = (4 * e) / r, c = 4 * e - t * r;
+      float* d = sx + t * rp + c;
+      d[0] = v.x;
+      d[1] = v.y;
+      d[2] = v.z;
+      d[3] = v.w;
+    }
+  } else {
+    for (int e = tid; e < nrow * r; e += 128) {
+      const int t = e / r, c = e - t * r;
+      sx[t * rp + c] = Xc[e];
+    }
+  }
+  __syncthreads();
+  if (tid < nrow) {
+    float* xr = sx + tid * rp;
+    float x[R4];
+#pragma unroll
+    for (int c = 0; c < R4; ++c) x[c] = c < r ? xr[c] : 0.f;
+#pragma unroll
+    for (int j = 0; j < RMAX; ++j) {
+      if (j < r) {
+        const float4* lj = reinterpret_cast<const float4*>(Ls + j * r4);
+        float a0 = x[j], a1 = 0.f;
+#pragma unroll
+        for (int c = 0; c < (j & ~3); c += 4) {   // entries c < j in whole quads
+          const float4 l = lj[c >> 2];
+          a0 = fmaf(-x[c], l.x, a0);
+          a1 = fmaf(-x[c + 1], l.y, a1);
+          a0 = fmaf(-x[c + 2], l.z, a0);
+          a1 = fmaf(-x[c + 3], l.w, a1);
+        }
+        if (j & 3) {   // the partial quad holding columns (j & ~3) .. j - 1 and the diagonal
+          const float4 l = lj[j >> 2];
+          const int c = j & ~3;
+          a0 = fmaf(-x[c], l.x, a0);
+          if ((j & 3) > 1) a1 = fmaf(-x[c + 1], l.y, a1);
+          if ((j & 3) > 2) a0 = fmaf(-x[c + 2], l.z, a0);
+        }
+        x[j] = (a0 + a1) * Ls[j * r4 + j];
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < R4; ++c)
+      if (c < r) xr[c] = x[c];
+  }
+  __syncthreads();
+  if (vec) {
+    float4* X4 = reinterpret_cast<float4*>(Xc);
+    for (int e = tid; e < nrow * r / 4; e += 128) {
+      const int t = (4 * e) / r, c = 4 * e - t * r;
+      const float* d = sx + t * rp + c;
+      X4[e] = make_float4(d[0], d[1], d[2], d[3]);
+    }
+  } else {
+    for (int e = tid; e < nrow * r; e += 128) {
+      const int t = e / r, c = e - t * r;
+      Xc[e] = sx[t * rp + c];
+    }
+  }
+}
+
 // ------------------------------------------------ small SVD by one-sided Jacobi
 // Z = Bp^T: f32 [n][r] (n <= 128, r <= 64).  One-sided (Hestenes) Jacobi on the columns
 // of A = Bp^T: plane rotations A J make the columns orthogonal; then A J = Vh^T S (column
@@ -727,6 +1056,9 @@ static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 struct RsvdWs {
   float *Y, *Z, *Wk, *S, *Vh;
+  double* G;   // [Nb][r][r] Gram matrices of the split Cholesky-QR
+  float* L;    // [Nb][r][r] its factors
+  int* np;     // [Nb] passes each matrix needs
   size_t bytes;
 };
 
@@ -744,6 +1076,9 @@ static RsvdWs carve(const spx_rsvd_args* a, char* base) {
   w.Wk = take(Nb * a->r * a->k * sizeof(float));
   w.S = take(Nb * a->k * sizeof(float));
   w.Vh = take(Nb * a->k * a->n * sizeof(float));
+  w.G = reinterpret_cast<double*>(take(Nb * a->r * a->r * sizeof(double)));
+  w.L = take(Nb * a->r * a->r * sizeof(float));
+  w.np = reinterpret_cast<int*>(take(Nb * sizeof(int)));
   w.bytes = off;
   return w;
 }
@@ -789,6 +1124,10 @@ static int run_chain(const spx_rsvd_args* a, const RsvdWs& w, cudaStream_t st) {
   cudaFuncSetAttribute(orth_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
   const dim3 gmx((m + 63) / 64, Nb), gmty((n + 63) / 64, Nb);
   // Cholesky-QR when its shared memory fits, classical Gram-Schmidt (CGS2) otherwise
+  cudaFuncSetAttribute(trsolve_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+  cudaFuncSetAttribute(gram_kernel<24>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+  cudaFuncSetAttribute(gram_kernel<40>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+  cudaFuncSetAttribute(gram_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
   cudaFuncSetAttribute(cholqr_kernel<24, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
   cudaFuncSetAttribute(cholqr_kernel<40, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
   cudaFuncSetAttribute(cholqr_kernel<64, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
@@ -797,6 +1136,26 @@ static int run_chain(const spx_rsvd_args* a, const RsvdWs& w, cudaStream_t st) {
   cudaFuncSetAttribute(cholqr_kernel<64, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
   // npass 2 for the final basis Q (it feeds Bp and the lift), 1 for intermediate ones
   auto orth = [&](float* X, int rows, int npass) {
+    if (rows > 128) {   // tall panel: Gram, factor and solve as three kernels per pass
+      const dim3 gs(Nb, (rows + 127) / 128);
+      const size_t sg = gram_smem(r), ts = trsolve_smem(r);
+      for (int pass = 0; pass < 3; ++pass) {
+        if (r <= 24) {
+          gram_kernel<24><<<Nb, 256, sg, st>>>(X, w.G, w.np, pass, npass, rows, r);
+          chol_kernel<24><<<Nb, 128, 0, st>>>(w.G, w.L, w.np, pass, r);
+          trsolve_kernel<24><<<gs, 128, ts, st>>>(X, w.L, w.np, pass, rows, r);
+        } else if (r <= 40) {
+          gram_kernel<40><<<Nb, 256, sg, st>>>(X, w.G, w.np, pass, npass, rows, r);
+          chol_kernel<40><<<Nb, 128, 0, st>>>(w.G, w.L, w.np, pass, r);
+          trsolve_kernel<40><<<gs, 128, ts, st>>>(X, w.L, w.np, pass, rows, r);
+        } else {
+          gram_kernel<64><<<Nb, 256, sg, st>>>(X, w.G, w.np, pass, npass, rows, r);
+          chol_kernel<64><<<Nb, 128, 0, st>>>(w.G, w.L, w.np, pass, r);
+          trsolve_kernel<64><<<gs, 128, ts, st>>>(X, w.L, w.np, pass, rows, r);
+        }
+      }
+      return;
+    }
     const size_t cq = cholqr_smem(rows, r);
     if (cq <= 220 * 1024) {
       if (rows <= 128) {
