@@ -723,25 +723,47 @@ __global__ void __launch_bounds__(128) trsolve_kernel(float* __restrict__ X, con
   float* Ls = tsm;             // [r][r4]
   float* sx = tsm + r * r4;    // [128][rp]
   const float* Li = Lw + (int64_t)i * r * r;
-  for (int e = tid; e < r * r4; e += 128) {
-    const int j = e / r4, c = e - j * r4;
-    Ls[e] = c < r ? Li[j * r + c] : 0.f;
-  }
   const int t0 = blockIdx.y * 128, nrow = min(128, rows - t0);
   float* Xc = X + ((int64_t)i * rows + t0) * r;
   const bool vec = (r & 3) == 0;
-  if (vec) {
+  if (vec) {   // r4 == r: L and the chunk are contiguous; float4 loads, all in flight at once
+    constexpr int UL = (RMAX * RMAX / 4 + 127) / 128, UX = (128 * RMAX / 4 + 127) / 128;
+    const float4* L4 = reinterpret_cast<const float4*>(Li);
     const float4* X4 = reinterpret_cast<const float4*>(Xc);
-    for (int e = tid; e < nrow * r / 4; e += 128) {
-      const float4 v = X4[e];
-      const int t = (4 * e) / r, c = 4 * e - t * r;
-      float* d = sx + t * rp + c;
-      d[0] = v.x;
-      d[1] = v.y;
-      d[2] = v.z;
-      d[3] = v.w;
+    const int nl4 = r * r / 4, nx4 = nrow * r / 4;
+    float4 vl[UL], vx[UX];
+#pragma unroll
+    for (int u = 0; u < UL; ++u) {
+      const int e = tid + 128 * u;
+      vl[u] = e < nl4 ? __ldg(L4 + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < UX; ++u) {
+      const int e = tid + 128 * u;
+      vx[u] = e < nx4 ? X4[e] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < UL; ++u) {
+      const int e = tid + 128 * u;
+      if (e < nl4) reinterpret_cast<float4*>(Ls)[e] = vl[u];
+    }
+#pragma unroll
+    for (int u = 0; u < UX; ++u) {
+      const int e = tid + 128 * u;
+      if (e < nx4) {
+        const int t = (4 * e) / r, c = 4 * e - t * r;
+        float* d = sx + t * rp + c;
+        d[0] = vx[u].x;
+        d[1] = vx[u].y;
+        d[2] = vx[u].z;
+        d[3] = vx[u].w;
+      }
     }
   } else {
+    for (int e = tid; e < r * r4; e += 128) {
+      const int j = e / r4, c = e - j * r4;
+      Ls[e] = c < r ? Li[j * r + c] : 0.f;
+    }
     for (int e = tid; e < nrow * r; e += 128) {
       const int t = e / r, c = e - t * r;
       sx[t * rp + c] = Xc[e];
