@@ -9,9 +9,9 @@
 //   C = U * S -> per-matrix INT8 codes, scale, (min, max); basis = Vh in basis dtype.
 // The reference runs the power iterations un-normalised; re-orthonormalising every
 // step spans the same subspace in exact arithmetic and avoids the float32 loss of the
-// un-normalised form.  orth() is Cholesky-QR applied twice (float64 Gram matrix), with
-// classical Gram-Schmidt (CGS2) for shapes whose panel does not fit in shared memory;
-// both are as stable as Householder QR for these well-conditioned panels.
+// un-normalised form.  orth() is Cholesky-QR with a float64 Gram matrix: two passes for
+// the final basis (as stable as Householder QR for these panels), one for intermediate
+// bases unless their conditioning asks for more.
 #include <math.h>
 
 #include "spx_common.cuh"
@@ -125,68 +125,6 @@ __global__ void __launch_bounds__(256) gemm_mty_kernel(const T* __restrict__ M, 
   }
 }
 
-// ------------------------------------------------ in-place CGS2 orthonormalisation
-// X: f32 [rows][r] per matrix, one CTA per matrix, the matrix held in shared memory.
-__global__ void __launch_bounds__(256) orth_kernel(float* __restrict__ X, int rows, int r) {
-  extern __shared__ float sm[];
-  float* sx = sm;                 // [rows][r]
-  float* coef = sx + rows * r;    // [r]
-  __shared__ float red[32];
-  const int i = blockIdx.x;
-  float* Xi = X + (int64_t)i * rows * r;
-  for (int e = threadIdx.x; e < rows * r; e += blockDim.x) sx[e] = Xi[e];
-  __syncthreads();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  for (int j = 0; j < r; ++j) {
-    for (int pass = 0; pass < 2; ++pass) {
-      for (int c = warp; c < j; c += nw) {
-        float a = 0.f;
-        for (int t = lane; t < rows; t += 32) a = fmaf(sx[t * r + c], sx[t * r + j], a);
-        a = warp_sum(a);
-        if (lane == 0) coef[c] = a;
-      }
-      __syncthreads();
-      for (int t = threadIdx.x; t < rows; t += blockDim.x) {
-        float v = sx[t * r + j];
-        for (int c = 0; c < j; ++c) v = fmaf(-coef[c], sx[t * r + c], v);
-        sx[t * r + j] = v;
-      }
-      __syncthreads();
-    }
-    float a = 0.f;
-    for (int t = threadIdx.x; t < rows; t += blockDim.x) a = fmaf(sx[t * r + j], sx[t * r + j], a);
-    a = warp_sum(a);
-    if (lane == 0) red[warp] = a;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      float s = 0.f;
-      for (int w = 0; w < nw; ++w) s += red[w];
-      red[0] = s > 1e-36f ? rsqrtf(s) : 0.f;  // a numerically zero column stays zero
-    }
-    __syncthreads();
-    const float inv = red[0];
-    for (int t = threadIdx.x; t < rows; t += blockDim.x) sx[t * r + j] *= inv;
-    __syncthreads();
-  }
-  for (int e = threadIdx.x; e < rows * r; e += blockDim.x) Xi[e] = sx[e];
-}
-
-// ---------------------------------------- in-place Cholesky-QR orthonormalisation
-// X: f32 [rows][r] per matrix, one CTA per matrix.  Each pass forms the Gram matrix
-// G = X^T X in float64 (products of two float32 values are exact in float64), factors
-// G = L L^T in float64, and solves X := X L^{-T} row by row.  Two passes give an
-// orthonormal basis to float32 accuracy while cond(X) <= ~1e6; a third pass runs when
-// the first one saw a larger pivot spread.  With npass = 1 (the intermediate bases of
-// the subspace iteration, which only need to span the subspace with a well-conditioned
-// basis) the second pass runs only when the first pass's pivots spread by more than
-// 1e6 (cond(X) > 1e3).  A pivot at rounding level of a zero column (relative 1e-30)
-// leaves that column zero, as classical Gram-Schmidt does.
-// Shared memory: G [r][r] f64, L [r][r] f32 (inverse diagonal on the diagonal),
-// X [rows][r | 1] f32 (odd pitch: the row-parallel solve is bank-conflict free).
-size_t cholqr_smem(int rows, int r) {
-  return (size_t)r * (r | 1) * 8 + (size_t)r * r * 4 + (size_t)rows * (r | 1) * 4;
-}
-
 // 1 / sqrt(x) for a positive finite float64 x, to float32 accuracy (it only scales the
 // float32 copy of L): x is scaled by an even power of two into [1, 4), the rsqrtf value
 // of that is refined by one Newton-Raphson step y <- y (3 - m y^2) / 2 and the power of
@@ -215,267 +153,22 @@ __device__ __forceinline__ double recip_pos(double x) {
   return y * s;
 }
 
-// NT threads per CTA: 256 for tall panels, 128 for panels of <= 128 rows (their shared
-// memory is small, so twice as many CTAs - and Cholesky chains - fit on an SM).
-template <int RMAX, int NT>
-__global__ void __launch_bounds__(NT, (RMAX <= 40 ? 2 : 1) * (256 / NT)) cholqr_kernel(float* __restrict__ X,
-                                                                                     int rows, int r, int npass) {
-  extern __shared__ double smd[];
-  const int rp = r | 1;                                  // odd pitches: conflict-free columns
-  double* G = smd;                                       // [r][rp]
-  float* Lf = reinterpret_cast<float*>(G + r * rp);      // [r][r]
-  float* sx = Lf + r * r;                                // [rows][rp]
-  __shared__ int second, third;
-  const int i = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  float* Xi = X + (int64_t)i * rows * r;
-  // panel -> shared memory; float4 loads, eight in flight per thread
-  const bool vec = (rows * r) % 4 == 0;
-  if (vec) {
-    const int n4 = rows * r / 4;
-    const float4* X4 = reinterpret_cast<const float4*>(Xi);
-    for (int e0 = 0; e0 < n4; e0 += 8 * NT) {
-      float4 v[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int e = e0 + u * NT + tid;
-        v[u] = e < n4 ? X4[e] : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int e = 4 * (e0 + u * NT + tid);
-        if (e < rows * r) {
-          const float vv[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int t = (e + q) / r, c = (e + q) - t * r;
-            sx[t * rp + c] = vv[q];
-          }
-        }
-      }
-    }
-  } else {
-    for (int e = tid; e < rows * r; e += blockDim.x) {
-      const int t = e / r, c = e - t * r;
-      sx[t * rp + c] = Xi[e];
-    }
-  }
-  if (tid == 0) {
-    second = npass >= 2;
-    third = 0;
-  }
-  __syncthreads();
-  const int nb2 = (r + 1) >> 1;                // 2x2 tiles of G per side
-  for (int pass = 0; pass < 3; ++pass) {
-    if ((pass == 1 && !second) || (pass == 2 && !third)) break;
-    // ---- Gram by 2x2 tiles of the upper triangle, stored as the lower triangle ---------
-    for (int tb = tid; tb < nb2 * (nb2 + 1) / 2; tb += blockDim.x) {
-      int ta = 0, rem = tb;
-      while (rem >= nb2 - ta) {   // tile (ta, tb') with ta <= tb'
-        rem -= nb2 - ta;
-        ++ta;
-      }
-      const int a0 = 2 * ta, b0 = 2 * (ta + rem);
-      const int a1 = a0 + 1 < r ? a0 + 1 : a0, b1 = b0 + 1 < r ? b0 + 1 : b0;
-      // four interleaved accumulation chains per entry (rows t mod 4): float64 FMA
-      // latency, not throughput, bounds a single chain
-      double g[4][4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) g[u][0] = g[u][1] = g[u][2] = g[u][3] = 0.0;
-      int t = 0;
-      for (; t + 4 <= rows; t += 4) {
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float* xr = sx + (t + u) * rp;
-          const double xa0 = xr[a0], xa1 = xr[a1], xb0 = xr[b0], xb1 = xr[b1];
-          g[u][0] = fma(xa0, xb0, g[u][0]);
-          g[u][1] = fma(xa0, xb1, g[u][1]);
-          g[u][2] = fma(xa1, xb0, g[u][2]);
-          g[u][3] = fma(xa1, xb1, g[u][3]);
-        }
-      }
-      for (; t < rows; ++t) {
-        const float* xr = sx + t * rp;
-        const double xa0 = xr[a0], xa1 = xr[a1], xb0 = xr[b0], xb1 = xr[b1];
-        g[0][0] = fma(xa0, xb0, g[0][0]);
-        g[0][1] = fma(xa0, xb1, g[0][1]);
-        g[0][2] = fma(xa1, xb0, g[0][2]);
-        g[0][3] = fma(xa1, xb1, g[0][3]);
-      }
-      const double g00 = (g[0][0] + g[1][0]) + (g[2][0] + g[3][0]);
-      const double g01 = (g[0][1] + g[1][1]) + (g[2][1] + g[3][1]);
-      const double g10 = (g[0][2] + g[1][2]) + (g[2][2] + g[3][2]);
-      const double g11 = (g[0][3] + g[1][3]) + (g[2][3] + g[3][3]);
-      G[b0 * rp + a0] = g00;
-      if (b1 != b0) G[b1 * rp + a0] = g01;
-      if (a1 != a0 && a1 <= b0) G[b0 * rp + a1] = g10;
-      if (a1 != a0 && b1 != b0) G[b1 * rp + a1] = g11;
-    }
-    __syncthreads();
-    // ---- Cholesky G = L L^T, right-looking, one block barrier per column -------------
-    // Each thread owns fixed entries (a, c), a >= c, of the lower triangle.  Step j
-    // updates every owned entry with c > j from the still unscaled column j,
-    //     G[a][c] -= G[a][j] G[c][j] / G[j][j],
-    // and scales the owned entries of column j - 1 by 1 / sqrt(pivot j - 1); column j is
-    // read and never written during step j, so the step needs no inner barrier.  The
-    // owner of diagonal entry j + 1 finishes it in step j and publishes 1 / pivot (the
-    // float64 coefficient of the next step's updates) for everyone; 1 / sqrt(pivot j),
-    // which only scales the float32 copy of L, is computed meanwhile by thread 255 at
-    // float accuracy.  A pivot at or below 1e-30 of the largest diagonal entry gives a
-    // zero column.
-    {
-      __shared__ double dmax_s;
-      __shared__ double pivs[64], coef_s[64], scale_s[64];
-      if (tid == 0) {
-        double dm = 0.0;
-        for (int j = 0; j < r; ++j) dm = fmax(dm, G[j * rp + j]);
-        dmax_s = dm;
-        const double p0 = G[0];
-        const bool ok = p0 > 1e-30 * dm && dm > 0.0;
-        pivs[0] = ok ? p0 : 0.0;
-        coef_s[0] = ok ? recip_pos(p0) : 0.0;
-      }
-      __syncthreads();
-      const double dmax = dmax_s;
-      constexpr int OWN = (RMAX * (RMAX + 1) / 2 + NT - 1) / NT;   // triangle entries per thread
-      int oa[OWN], oc[OWN];
-      const int ntri = r * (r + 1) / 2;
-#pragma unroll
-      for (int q = 0; q < OWN; ++q) {
-        int e = tid + NT * q, a = 0;
-        if (e < ntri) {
-          a = (int)((sqrt(8.0 * e + 1.0) - 1.0) * 0.5);   // row of triangle entry e
-          while (a * (a + 1) / 2 > e) --a;
-          while ((a + 1) * (a + 2) / 2 <= e) ++a;
-          oa[q] = a;
-          oc[q] = e - a * (a + 1) / 2;
-        } else {
-          oa[q] = -1;
-          oc[q] = -1;
-        }
-      }
-      for (int j = 0; j < r; ++j) {
-        const double coef = coef_s[j], prev_scale = j > 0 ? scale_s[j - 1] : 0.0;
-        double va[OWN], vb[OWN], vc[OWN];   // all operands first: the entries overlap
-#pragma unroll
-        for (int q = 0; q < OWN; ++q) {
-          const int a = oa[q], c = oc[q];
-          if (c > j) {
-            va[q] = G[a * rp + j];
-            vb[q] = G[c * rp + j];
-            vc[q] = G[a * rp + c];
-          }
-        }
-#pragma unroll
-        for (int q = 0; q < OWN; ++q) {
-          const int a = oa[q], c = oc[q];
-          if (c > j) {
-            const double v = fma(-va[q] * coef, vb[q], vc[q]);
-            G[a * rp + c] = v;
-            if (a == j + 1 && c == j + 1) {   // the next pivot is final
-              const bool ok = v > 1e-30 * dmax && dmax > 0.0;
-              pivs[j + 1] = ok ? v : 0.0;
-              coef_s[j + 1] = ok ? recip_pos(v) : 0.0;
-            }
-          } else if (c == j - 1 && a > c) {
-            G[a * rp + c] *= prev_scale;
-          }
-        }
-        if (tid == NT - 1) scale_s[j] = pivs[j] > 0.0 ? (double)rsqrt_pos_f(pivs[j]) : 0.0;
-        __syncthreads();
-      }
-      // L to float (strict lower part: every column c < r - 1 was scaled at step c + 1),
-      // 1 / L[j][j] on the diagonal
-#pragma unroll
-      for (int q = 0; q < OWN; ++q) {
-        const int a = oa[q], c = oc[q];
-        if (c >= 0 && a > c) Lf[a * r + c] = (float)G[a * rp + c];
-      }
-      for (int j = tid; j < r; j += blockDim.x) Lf[j * r + j] = (float)scale_s[j];
-      if (tid == 0 && pass == 0) {
-        double pmin = 1e300, pmax = 0.0;
-        for (int j = 0; j < r; ++j)
-          if (pivs[j] > 0.0) {
-            pmin = fmin(pmin, pivs[j]);
-            pmax = fmax(pmax, pivs[j]);
-          }
-        if (pmax > 1e12 * pmin) third = 1;
-        if (pmax > 1e6 * pmin) second = 1;
-      }
-    }
-    __syncthreads();
-    // ---- X := X L^{-T}, two rows per thread held in registers (r <= RMAX): each L
-    //      element is one broadcast load feeding four independent FMA chains ------------
-    for (int t0 = tid; t0 < rows; t0 += 2 * blockDim.x) {
-      const int t1 = t0 + blockDim.x;   // lane i reads row i: conflict-free at the odd pitch
-      const bool two = t1 < rows;
-      float* x0r = sx + t0 * rp;
-      float* x1r = two ? sx + t1 * rp : x0r;
-      float x0[RMAX], x1[RMAX];
-#pragma unroll
-      for (int c = 0; c < RMAX; ++c) {
-        x0[c] = c < r ? x0r[c] : 0.f;
-        x1[c] = c < r ? x1r[c] : 0.f;
-      }
-#pragma unroll
-      for (int j = 0; j < RMAX; ++j) {
-        if (j < r) {
-          const float* lj = Lf + j * r;
-          float a0 = x0[j], a1 = 0.f, b0 = x1[j], b1 = 0.f;
-#pragma unroll
-          for (int c = 0; c + 1 < j; c += 2) {
-            const float l0 = lj[c], l1 = lj[c + 1];
-            a0 = fmaf(-x0[c], l0, a0);
-            a1 = fmaf(-x0[c + 1], l1, a1);
-            b0 = fmaf(-x1[c], l0, b0);
-            b1 = fmaf(-x1[c + 1], l1, b1);
-          }
-          if (j & 1) {
-            const float l0 = lj[j - 1];
-            a0 = fmaf(-x0[j - 1], l0, a0);
-            b0 = fmaf(-x1[j - 1], l0, b0);
-          }
-          const float dinv = lj[j];
-          x0[j] = (a0 + a1) * dinv;
-          x1[j] = (b0 + b1) * dinv;
-        }
-      }
-#pragma unroll
-      for (int c = 0; c < RMAX; ++c)
-        if (c < r) {
-          x0r[c] = x0[c];
-          if (two) x1r[c] = x1[c];
-        }
-    }
-    __syncthreads();
-  }
-  if (vec) {
-    float4* X4 = reinterpret_cast<float4*>(Xi);
-    for (int e = tid; e < rows * r / 4; e += blockDim.x) {
-      float vv[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int t = (4 * e + q) / r, c = (4 * e + q) - t * r;
-        vv[q] = sx[t * rp + c];
-      }
-      X4[e] = make_float4(vv[0], vv[1], vv[2], vv[3]);
-    }
-  } else {
-    for (int e = tid; e < rows * r; e += blockDim.x) {
-      const int t = e / r, c = e - t * r;
-      Xi[e] = sx[t * rp + c];
-    }
-  }
-}
-
-// ------------------------------- Cholesky-QR of tall panels as three kernels per pass
-// A panel of many rows fills shared memory, which caps the fused kernel at two CTAs -
-// two serial Cholesky chains - per SM.  For panels of more than 128 rows each pass runs
-// as: a streaming float64 Gram kernel (the panel passes through shared memory in
-// 128-row chunks), a Cholesky-only kernel (one small CTA per matrix, many per SM), and
-// a row-parallel triangular solve.  np[i] holds the number of passes matrix i needs:
-// the Gram kernel of pass 0 sets it to the requested count, the Cholesky of pass 0
-// raises it from the pivot spread (> 1e6: two passes, > 1e12: three), and every kernel
-// of a later pass returns at once for a matrix that needs no more.
+// ------------------------------------- Cholesky-QR orthonormalisation, three kernels
+// X: f32 [rows][r] per matrix, orthonormalised in place.  Each pass forms the Gram
+// matrix G = X^T X in float64 (products of two float32 values are exact in float64),
+// factors G = L L^T in float64 and solves X := X L^{-T}.  Two passes give an orthonormal
+// basis to float32 accuracy while cond(X) <= ~1e6; a third runs when the first pass's
+// pivots spread by more than 1e12.  The intermediate bases of the subspace iteration
+// (which only need a well-conditioned basis of the right span) ask for one pass; a
+// second then runs only when the pivots spread by more than 1e6 (cond(X) > 1e3).  A
+// pivot at rounding level of a zero column (relative 1e-30) leaves that column zero.
+// A pass is three kernels, so that each step gets the parallelism it needs: a float64
+// Gram kernel (the panel streams through shared memory in 128-row chunks), a
+// Cholesky-only kernel (one small CTA per matrix, many per SM: the 40-odd dependent
+// column steps of many matrices overlap) and a row-parallel triangular solve.  np[i]
+// holds the number of passes matrix i needs: the Gram kernel of pass 0 sets it to the
+// requested count, the Cholesky of pass 0 raises it from the pivot spread, and every
+// kernel of a later pass returns at once for a matrix that needs no more.
 constexpr int kGramChunk = 128;
 // Gram tiling: 4 x 4 tiles of the upper triangle, each split over S interleaved row
 // subsets (rows t = s mod S of every chunk) so that ~256 threads are busy; 4 x 4 tiles
@@ -618,13 +311,20 @@ __global__ void __launch_bounds__(256) gram_kernel(const float* __restrict__ X, 
   }
 }
 
-// Factor G = L L^T of one matrix per CTA (the block-parallel right-looking scheme of
-// cholqr_kernel, 128 threads); writes Lw [r][r] f32: strict lower part L, 1 / L[j][j] on
-// the diagonal.  In pass 0 the pivot spread raises np[i].
+// Factor G = L L^T of one matrix per CTA, right-looking with one block barrier per
+// column: each thread owns fixed lower-triangle entries (a, c) and in step j updates
+// those with c > j from the still unscaled column j, G[a][c] -= G[a][j] G[c][j] / G[j][j],
+// and scales its entries of column j - 1 by 1 / sqrt(pivot j - 1); column j is only
+// read during step j.  The owner of diagonal entry j + 1 publishes 1 / pivot (float64,
+// a Newton-refined reciprocal) for the next step; thread NT - 1 computes 1 / sqrt(pivot)
+// at float accuracy (it only scales the float32 copy of L).  Writes Lw [r][r] f32:
+// strict lower part L, 1 / L[j][j] on the diagonal.  In pass 0 the pivot spread raises
+// np[i].
+constexpr int kCholThreads = 128;
 template <int RMAX>
-__global__ void __launch_bounds__(128) chol_kernel(const double* __restrict__ Gw, float* __restrict__ Lw,
-                                                   int* __restrict__ np, int pass, int r) {
-  constexpr int NT = 128;
+__global__ void __launch_bounds__(kCholThreads) chol_kernel(const double* __restrict__ Gw, float* __restrict__ Lw,
+                                                            int* __restrict__ np, int pass, int r) {
+  constexpr int NT = kCholThreads;
   const int i = blockIdx.x, tid = threadIdx.x;
   if (pass > 0 && pass >= np[i]) return;
   const int rp = r | 1;
@@ -1143,55 +843,31 @@ static int run_chain(const spx_rsvd_args* a, const RsvdWs& w, cudaStream_t st) {
   const int64_t ms = a->M_mat_stride > 0 ? a->M_mat_stride : (int64_t)m * n;
   const size_t smx = ((size_t)n * r + 64 * (size_t)(n + 1)) * sizeof(float);
   cudaFuncSetAttribute(gemm_mx_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smx);
-  cudaFuncSetAttribute(orth_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
   const dim3 gmx((m + 63) / 64, Nb), gmty((n + 63) / 64, Nb);
-  // Cholesky-QR when its shared memory fits, classical Gram-Schmidt (CGS2) otherwise
   cudaFuncSetAttribute(trsolve_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
   cudaFuncSetAttribute(gram_kernel<24>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
   cudaFuncSetAttribute(gram_kernel<40>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
   cudaFuncSetAttribute(gram_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-  cudaFuncSetAttribute(cholqr_kernel<24, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-  cudaFuncSetAttribute(cholqr_kernel<40, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-  cudaFuncSetAttribute(cholqr_kernel<64, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-  cudaFuncSetAttribute(cholqr_kernel<24, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-  cudaFuncSetAttribute(cholqr_kernel<40, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-  cudaFuncSetAttribute(cholqr_kernel<64, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-  // npass 2 for the final basis Q (it feeds Bp and the lift), 1 for intermediate ones
+  // Cholesky-QR: npass 2 for the final basis Q (it feeds Bp and the lift), 1 for the
+  // intermediate ones; three kernels per pass (Gram, factor, solve)
   auto orth = [&](float* X, int rows, int npass) {
-    if (rows > 128) {   // tall panel: Gram, factor and solve as three kernels per pass
-      const dim3 gs(Nb, (rows + 127) / 128);
-      const size_t sg = gram_smem(r), ts = trsolve_smem(r);
-      for (int pass = 0; pass < 3; ++pass) {
-        if (r <= 24) {
-          gram_kernel<24><<<Nb, 256, sg, st>>>(X, w.G, w.np, pass, npass, rows, r);
-          chol_kernel<24><<<Nb, 128, 0, st>>>(w.G, w.L, w.np, pass, r);
-          trsolve_kernel<24><<<gs, 128, ts, st>>>(X, w.L, w.np, pass, rows, r);
-        } else if (r <= 40) {
-          gram_kernel<40><<<Nb, 256, sg, st>>>(X, w.G, w.np, pass, npass, rows, r);
-          chol_kernel<40><<<Nb, 128, 0, st>>>(w.G, w.L, w.np, pass, r);
-          trsolve_kernel<40><<<gs, 128, ts, st>>>(X, w.L, w.np, pass, rows, r);
-        } else {
-          gram_kernel<64><<<Nb, 256, sg, st>>>(X, w.G, w.np, pass, npass, rows, r);
-          chol_kernel<64><<<Nb, 128, 0, st>>>(w.G, w.L, w.np, pass, r);
-          trsolve_kernel<64><<<gs, 128, ts, st>>>(X, w.L, w.np, pass, rows, r);
-        }
-      }
-      return;
-    }
-    const size_t cq = cholqr_smem(rows, r);
-    if (cq <= 220 * 1024) {
-      if (rows <= 128) {
-        if (r <= 24) cholqr_kernel<24, 128><<<Nb, 128, cq, st>>>(X, rows, r, npass);
-        else if (r <= 40) cholqr_kernel<40, 128><<<Nb, 128, cq, st>>>(X, rows, r, npass);
-        else cholqr_kernel<64, 128><<<Nb, 128, cq, st>>>(X, rows, r, npass);
+    const dim3 gs(Nb, (rows + 127) / 128);
+    const size_t sg = gram_smem(r), ts = trsolve_smem(r);
+    for (int pass = 0; pass < 3; ++pass) {
+      if (r <= 24) {
+        gram_kernel<24><<<Nb, 256, sg, st>>>(X, w.G, w.np, pass, npass, rows, r);
+        chol_kernel<24><<<Nb, kCholThreads, 0, st>>>(w.G, w.L, w.np, pass, r);
+        trsolve_kernel<24><<<gs, 128, ts, st>>>(X, w.L, w.np, pass, rows, r);
+      } else if (r <= 40) {
+        gram_kernel<40><<<Nb, 256, sg, st>>>(X, w.G, w.np, pass, npass, rows, r);
+        chol_kernel<40><<<Nb, kCholThreads, 0, st>>>(w.G, w.L, w.np, pass, r);
+        trsolve_kernel<40><<<gs, 128, ts, st>>>(X, w.L, w.np, pass, rows, r);
       } else {
-        if (r <= 24) cholqr_kernel<24, 256><<<Nb, 256, cq, st>>>(X, rows, r, npass);
-        else if (r <= 40) cholqr_kernel<40, 256><<<Nb, 256, cq, st>>>(X, rows, r, npass);
-        else cholqr_kernel<64, 256><<<Nb, 256, cq, st>>>(X, rows, r, npass);
+        gram_kernel<64><<<Nb, 256, sg, st>>>(X, w.G, w.np, pass, npass, rows, r);
+        chol_kernel<64><<<Nb, kCholThreads, 0, st>>>(w.G, w.L, w.np, pass, r);
+        trsolve_kernel<64><<<gs, 128, ts, st>>>(X, w.L, w.np, pass, rows, r);
       }
     }
-    else
-      orth_kernel<<<Nb, 256, ((size_t)rows * r + r) * sizeof(float), st>>>(X, rows, r);
   };
   // 16-bit inputs of 128 columns run the products on the tensor cores (spx_rsvd_tc.cu)
   const bool tc = rsvd_tc_supported(a->in_dtype, a->M, ms, m, n, r);
