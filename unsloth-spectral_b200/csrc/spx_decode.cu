@@ -138,8 +138,20 @@ __global__ void __launch_bounds__(256) cold_generic_kernel(DecodeParams p) {
 }
 
 // ------------------------------------------------------------- hot tier + merge ---
-template <typename T>
+// Shared memory of hot_merge_kernel before the staged copies (floats; a multiple of 4,
+// so the staged region starts 16-byte aligned): q, scores, (weight, 1/L), merge weights,
+// partial value sums of 256 / D slices, clamped table rows.
+__host__ __device__ inline size_t hot_merge_base_floats(const DecodeParams& p) {
+  const size_t f = (size_t)p.nrep * p.D + (size_t)p.nrep * p.hot + 2 * p.nrep + (size_t)p.nrep * (p.nblk + 1) +
+                   (size_t)(256 / p.D) * p.nrep * p.D + (size_t)p.hot;
+  return (f + 3) & ~(size_t)3;
+}
+
+template <typename T, bool STAGE>
 __global__ void __launch_bounds__(256) hot_merge_kernel(DecodeParams p) {
+  // STAGE: the hot K and V rows and the cold partial records are first copied to shared
+  // memory with 16-byte asynchronous copies, all in flight at once, instead of being
+  // read in many dependent rounds of global loads
   const int g = blockIdx.x, lb = blockIdx.y;
   const int b = lb % p.B;
   const int D = p.D, half = D / 2, nrep = p.nrep, hot = p.hot, nb = p.nblk, nc = p.ncold;
@@ -152,6 +164,26 @@ __global__ void __launch_bounds__(256) hot_merge_kernel(DecodeParams p) {
   float* sred = swt + nrep * (nc + 1);   // [slices][nrep][D] partial value sums
   int* spos = reinterpret_cast<int*>(sred + (blockDim.x / D) * nrep * D);   // [hot] clamped table rows
   const int64_t lbg = (int64_t)lb * p.H + g;
+  // staged copies (STAGE): K rows [hot][D], V rows [hot][D] (T), records [nc][nrep][D + 4] f32
+  uint8_t* stg = reinterpret_cast<uint8_t*>(sm) + hot_merge_base_floats(p) * sizeof(float);
+  T* sK = reinterpret_cast<T*>(stg);
+  T* sV = sK + (size_t)hot * D;
+  float* sR = reinterpret_cast<float*>(sV + (size_t)hot * D);
+  if (STAGE) {
+    const uint8_t* gk = reinterpret_cast<const uint8_t*>(reinterpret_cast<const T*>(p.hk) + lbg * p.HC * D);
+    const uint8_t* gv = reinterpret_cast<const uint8_t*>(reinterpret_cast<const T*>(p.hv) + lbg * p.HC * D);
+    const uint8_t* gr = reinterpret_cast<const uint8_t*>(p.ws + (lbg * p.nparts) * nrep * (int64_t)(D + 4));
+    const int nkv = hot * D * (int)sizeof(T) / 16, nr = nc * nrep * (D + 4) * 4 / 16;
+    const uint32_t dk = (uint32_t)__cvta_generic_to_shared(sK), dv = (uint32_t)__cvta_generic_to_shared(sV),
+                   dr = (uint32_t)__cvta_generic_to_shared(sR);
+    for (int e = tid; e < nkv; e += blockDim.x) {
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dk + 16 * e), "l"(gk + 16 * e) : "memory");
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dv + 16 * e), "l"(gv + 16 * e) : "memory");
+    }
+    for (int e = tid; e < nr; e += blockDim.x)
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dr + 16 * e), "l"(gr + 16 * e) : "memory");
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+  }
   const T* q = reinterpret_cast<const T*>(p.q) + ((int64_t)lb * p.Hq + (int64_t)g * nrep) * D;
   for (int i = tid; i < nrep * D; i += blockDim.x) sq[i] = to_f(q[i]);
   for (int t = tid; t < hot; t += blockDim.x) {
@@ -161,8 +193,8 @@ __global__ void __launch_bounds__(256) hot_merge_kernel(DecodeParams p) {
   // a cold-tier kernel that gave up waiting marks the workspace header: report NaN
   const bool cold_failed = nb > 0 && reinterpret_cast<const int*>(p.ws)[-64] != 0;
   __syncthreads();
-  const T* hk = reinterpret_cast<const T*>(p.hk) + lbg * p.HC * D;
-  const T* hv = reinterpret_cast<const T*>(p.hv) + lbg * p.HC * D;
+  const T* hk = STAGE ? sK : reinterpret_cast<const T*>(p.hk) + lbg * p.HC * D;
+  const T* hv = STAGE ? sV : reinterpret_cast<const T*>(p.hv) + lbg * p.HC * D;
   const bool second_half = (p.mode == SPX_ROPE_ABSOLUTE) && !p.tied;
   // scores: one warp per hot token, lanes over the rotation pairs (coalesced rows)
 #pragma unroll 2
@@ -208,7 +240,7 @@ __global__ void __launch_bounds__(256) hot_merge_kernel(DecodeParams p) {
     }
     l = warp_sum(l);
     // merge weights over the cold partials and the hot partial
-    const float* recs = p.ws + (lbg * p.nparts) * nrep * (int64_t)(D + 4);
+    const float* recs = STAGE ? sR : p.ws + (lbg * p.nparts) * nrep * (int64_t)(D + 4);
     float M = m;
     for (int jj = lane; jj < nc; jj += 32) M = fmaxf(M, recs[((int64_t)jj * nrep + h) * (D + 4)]);
     M = warp_max(M);
@@ -229,7 +261,7 @@ __global__ void __launch_bounds__(256) hot_merge_kernel(DecodeParams p) {
   }
   __syncthreads();
   T* out = reinterpret_cast<T*>(p.out) + ((int64_t)lb * p.Hq + (int64_t)g * nrep) * D;
-  const float* recs = p.ws + (lbg * p.nparts) * nrep * (int64_t)(D + 4);
+  const float* recs = STAGE ? sR : p.ws + (lbg * p.nparts) * nrep * (int64_t)(D + 4);
   // hot values: thread (slice, d) reads each V element once for every head of the group
   {
     const int slices = blockDim.x / D;
@@ -285,14 +317,23 @@ static int launch_cold(const DecodeParams& p, cudaStream_t st) {
 
 template <typename T>
 static int launch_hot_merge(const DecodeParams& p, cudaStream_t st) {
-  const size_t smem = ((size_t)p.nrep * p.D + (size_t)p.nrep * p.hot + 2 * p.nrep + (size_t)p.nrep * (p.nblk + 1) +
-                       (size_t)(256 / p.D) * p.nrep * p.D + (size_t)p.hot) *
-                      sizeof(float);
+  const size_t smem = hot_merge_base_floats(p) * sizeof(float);
   SPX_REQUIRE(smem <= kMaxSmem, SPX_ERR_UNSUPPORTED,
               "hot tier of %d tokens with %d blocks needs %zu bytes of shared memory", p.hot, p.nblk, smem);
-  cudaFuncSetAttribute(hot_merge_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  // staging when it fits in a modest footprint (several CTAs per SM) and every copy is
+  // whole, aligned 16-byte chunks
+  const size_t stage = 2 * (size_t)p.hot * p.D * sizeof(T) + (size_t)p.ncold * p.nrep * (p.D + 4) * sizeof(float);
+  const bool aligned = ((reinterpret_cast<uintptr_t>(p.hk) | reinterpret_cast<uintptr_t>(p.hv) |
+                         reinterpret_cast<uintptr_t>(p.ws)) & 15u) == 0 &&
+                       ((size_t)p.HC * p.D * sizeof(T)) % 16 == 0 && ((size_t)p.hot * p.D * sizeof(T)) % 16 == 0;
   dim3 grid(p.H, p.L * p.B);
-  hot_merge_kernel<T><<<grid, 256, smem, st>>>(p);
+  if (aligned && smem + stage <= 64 * 1024) {
+    cudaFuncSetAttribute(hot_merge_kernel<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(smem + stage));
+    hot_merge_kernel<T, true><<<grid, 256, smem + stage, st>>>(p);
+  } else {
+    cudaFuncSetAttribute(hot_merge_kernel<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    hot_merge_kernel<T, false><<<grid, 256, smem, st>>>(p);
+  }
   return launch_status("hot_merge_kernel");
 }
 
