@@ -289,6 +289,54 @@ def test_rsvd_matches_reference_error(i):
     assert torch.allclose(Vc @ Vc.transpose(1, 2), torch.eye(k, dtype=torch.float64, device="cuda")[None], atol=1e-4)
 
 
+@pytest.mark.parametrize("case", ["rank6", "steep", "rank6_q0"])
+def test_rsvd_ill_conditioned_sketches(case):
+    """Sketches the orthonormalisation has to work for: an exactly rank-6 block (r = 24
+    sketch columns, so Cholesky-QR meets zero pivots and leaves zero columns) and a
+    spectrum decaying as 0.5^i (pivot spreads far beyond 1e12, so the extra passes run).
+    The reconstruction error must match the reference algorithm's float64 run on the
+    same sketch within 1e-3, as for the golden cases."""
+    from unsloth_spectral import _ops
+    g = torch.Generator().manual_seed(11)
+    k, q = 16, 0 if case == "rank6_q0" else 2
+    if case.startswith("rank6"):
+        A = torch.randn(6, 512, 6, generator=g)
+        Bm = torch.randn(6, 6, 128, generator=g)
+        M16 = (A @ Bm).to(torch.float16)
+    else:
+        sig = 0.5 ** torch.arange(48, dtype=torch.float32)
+        A = torch.randn(6, 512, 48, generator=g) * sig
+        M16 = (A @ torch.randn(6, 48, 128, generator=g)).to(torch.float16)
+    Omega = torch.randn(6, 128, k + 8, generator=g)
+    U, S, Vh = _ops.rsvd(M16.cuda(), Omega.cuda(), k, q)
+    for x in (U, S, Vh):
+        assert torch.isfinite(x).all()
+    M = M16.float().numpy()
+    err = so.relative_reconstruction_error(M, U.cpu().numpy(), S.cpu().numpy(), Vh.cpu().numpy())
+    U64, S64, Vh64 = so.batched_randomized_svd(M, k, q, 8, Omega.numpy())
+    err64 = so.relative_reconstruction_error(M, U64, S64, Vh64)
+    assert np.abs(err - err64).max() <= 1e-3, (err, err64)
+    S_np = S.cpu().numpy()
+    big = S64 >= 1e-3 * S64[:, :1]
+    np.testing.assert_allclose(S_np[big], S64[big], rtol=2e-3)
+    if case.startswith("rank6"):   # nothing beyond the rank
+        assert (S_np[:, 6:] <= 1e-4 * S_np[:, :1]).all()
+
+
+def test_rsvd_zero_block():
+    """An all-zero block compresses to zero singular values and zero codes, no NaN."""
+    from unsloth_spectral import _ops
+    M = torch.zeros(3, 512, 128, dtype=torch.float16, device="cuda")
+    Omega = torch.randn(3, 128, 24, device="cuda")
+    codes = torch.full((3, 512, 16), 7, dtype=torch.int8, device="cuda")
+    qscale = torch.zeros(3, device="cuda")
+    U, S, Vh = _ops.rsvd(M, Omega, 16, 2, codes=codes, codes_strides=(512 * 16, 16, 1), qscale=qscale)
+    for x in (U, S, Vh, qscale):
+        assert torch.isfinite(x).all()
+    assert (S == 0).all()
+    assert (codes == 0).all()
+
+
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
 def test_public_rsvd_draws_the_reference_sketch(dtype):
     """batched_randomized_svd draws its sketch as rsvd.py:95 does; with the same seed the
