@@ -322,7 +322,7 @@ __global__ void __launch_bounds__(256) gram_kernel(const float* __restrict__ X, 
 // np[i].
 constexpr int kCholThreads = 128;
 template <int RMAX>
-__global__ void __launch_bounds__(kCholThreads) chol_kernel(const double* __restrict__ Gw, float* __restrict__ Lw,
+__global__ void __launch_bounds__(kCholThreads, 8) chol_kernel(const double* __restrict__ Gw, float* __restrict__ Lw,
                                                             int* __restrict__ np, int pass, int r) {
   constexpr int NT = kCholThreads;
   const int i = blockIdx.x, tid = threadIdx.x;
@@ -648,21 +648,26 @@ __global__ void __launch_bounds__(256) small_svd_kernel(const float* __restrict_
 // ------------------------------------------------- lift, C = U S, INT8 quantisation
 // Shared memory of lift_quant_kernel: W^T [k][r4], C [m][k + 1] (odd pitch: the
 // row-per-thread writes are bank-conflict free).
-size_t lift_smem(int m, int r, int k) {
+// Shared memory of lift_quant_kernel: W^T [k][r4] f32, a chunk of INT8 codes [256][kp].
+size_t lift_smem(int m, int r, int k, int kp) {
   const int r4 = (r + 3) & ~3;
-  return ((size_t)k * r4 + (size_t)m * (k + 1)) * sizeof(float);
+  return (size_t)k * r4 * sizeof(float) + (size_t)256 * kp;
 }
 
-// One CTA per matrix.  U = Q W row by row: a thread holds a row of Q in registers and
-// reads W^T from shared memory four entries at a time; C = U S stays in shared memory
-// for the INT8 pass.
+// One CTA per matrix, two passes over the rows of U = Q W (a thread holds a row of Q in
+// registers and reads W^T from shared memory four entries at a time).  Pass 1 writes U
+// (when asked for) and reduces min / max / absmax of C = U S; pass 2 recomputes the rows
+// with the same instruction sequence - so C is bit-identical - and quantises them, the
+// codes of 256 rows at a time staged in shared memory and written out in the
+// destination's element order.  Holding C between the passes instead would take
+// m (k + 1) floats of shared memory and cap the kernel at three CTAs per SM.
 template <int RMAX>
 __global__ void __launch_bounds__(256) lift_quant_kernel(LiftParams p) {
   extern __shared__ float sm[];
   const int m = p.m, r = p.r, k = p.k, n = p.n;
-  const int r4 = (r + 3) & ~3, kc = k + 1;
-  float* swt = sm;                // [k][r4] W^T, zero padded
-  float* sc = swt + k * r4;       // [m][kc]  C = U * S
+  const int r4 = (r + 3) & ~3;
+  float* swt = sm;                                           // [k][r4] W^T, zero padded
+  int8_t* scodes = reinterpret_cast<int8_t*>(swt + k * r4);  // [256][kp]
   __shared__ float ss[64];
   __shared__ float red[3][32];
   const int i = blockIdx.x;
@@ -673,9 +678,7 @@ __global__ void __launch_bounds__(256) lift_quant_kernel(LiftParams p) {
   if (threadIdx.x < k) ss[threadIdx.x] = p.Sw[(int64_t)i * k + threadIdx.x];
   __syncthreads();
   const float* Qi = p.Q + (int64_t)i * m * r;
-  float mn = INFINITY, mx = -INFINITY, am = 0.f;
-  for (int t = threadIdx.x; t < m; t += blockDim.x) {
-    float q[RMAX];
+  auto load_row = [&](int t, float (&q)[RMAX]) {
     if ((r & 3) == 0) {   // rows of 16-byte multiples: float4 loads
       const float4* q4 = reinterpret_cast<const float4*>(Qi + (int64_t)t * r);
 #pragma unroll
@@ -690,23 +693,30 @@ __global__ void __launch_bounds__(256) lift_quant_kernel(LiftParams p) {
 #pragma unroll
       for (int a = 0; a < RMAX; ++a) q[a] = a < r ? __ldg(Qi + (int64_t)t * r + a) : 0.f;
     }
-    for (int j = 0; j < k; ++j) {
-      const float4* w4 = reinterpret_cast<const float4*>(swt + j * r4);
-      float u0 = 0.f, u1 = 0.f;
+  };
+  auto u_of = [&](const float (&q)[RMAX], int j) {
+    const float4* w4 = reinterpret_cast<const float4*>(swt + j * r4);
+    float u0 = 0.f, u1 = 0.f;
 #pragma unroll
-      for (int a = 0; a < RMAX; a += 4) {
-        if (a < r) {
-          const float4 w = w4[a >> 2];
-          u0 = fmaf(q[a], w.x, u0);
-          u1 = fmaf(q[a + 1], w.y, u1);
-          u0 = fmaf(q[a + 2], w.z, u0);
-          u1 = fmaf(q[a + 3], w.w, u1);
-        }
+    for (int a = 0; a < RMAX; a += 4) {
+      if (a < r) {
+        const float4 w = w4[a >> 2];
+        u0 = fmaf(q[a], w.x, u0);
+        u1 = fmaf(q[a + 1], w.y, u1);
+        u0 = fmaf(q[a + 2], w.z, u0);
+        u1 = fmaf(q[a + 3], w.w, u1);
       }
-      const float u = u0 + u1;
+    }
+    return u0 + u1;
+  };
+  float mn = INFINITY, mx = -INFINITY, am = 0.f;
+  for (int t = threadIdx.x; t < m; t += blockDim.x) {
+    float q[RMAX];
+    load_row(t, q);
+    for (int j = 0; j < k; ++j) {
+      const float u = u_of(q, j);
       if (p.U) p.U[(int64_t)i * m * k + (int64_t)t * k + j] = u;
       const float c = u * ss[j];
-      sc[t * kc + j] = c;
       mn = fminf(mn, c);
       mx = fmaxf(mx, c);
       am = fmaxf(am, fabsf(c));
@@ -746,15 +756,29 @@ __global__ void __launch_bounds__(256) lift_quant_kernel(LiftParams p) {
   if (p.codes) {
     const int kp = p.rank_pad;
     int8_t* ci = p.codes + (int64_t)i * p.codes_mat_stride;
-    for (int e = threadIdx.x; e < m * kp; e += blockDim.x) {
-      int t, j;
-      if (p.codes_j_stride == 1 || p.codes_tiled) { t = e / kp; j = e - t * kp; }
-      else { j = e / m; t = e - j * m; }
-      const int8_t v = j < k ? (int8_t)(int)rintf(__fdiv_rn(sc[t * kc + j], scale)) : (int8_t)0;
-      if (p.codes_tiled)
-        ci[vtile_offset(j, t, kp)] = v;
-      else
-        ci[(int64_t)t * p.codes_t_stride + (int64_t)j * p.codes_j_stride] = v;
+    for (int t0 = 0; t0 < m; t0 += 256) {
+      const int nrow = min(256, m - t0);
+      if ((int)threadIdx.x < nrow) {
+        const int t = t0 + threadIdx.x;
+        float q[RMAX];
+        load_row(t, q);
+        for (int j = 0; j < kp; ++j)
+          scodes[threadIdx.x * kp + j] =
+              j < k ? (int8_t)(int)rintf(__fdiv_rn(u_of(q, j) * ss[j], scale)) : (int8_t)0;
+      }
+      __syncthreads();
+      for (int e = threadIdx.x; e < nrow * kp; e += blockDim.x) {
+        int tl, j;
+        if (p.codes_j_stride == 1 || p.codes_tiled) { tl = e / kp; j = e - tl * kp; }
+        else { j = e / nrow; tl = e - j * nrow; }
+        const int t = t0 + tl;
+        const int8_t v = scodes[tl * kp + j];
+        if (p.codes_tiled)
+          ci[vtile_offset(j, t, kp)] = v;
+        else
+          ci[(int64_t)t * p.codes_t_stride + (int64_t)j * p.codes_j_stride] = v;
+      }
+      __syncthreads();
     }
   }
   if (p.S && threadIdx.x < k) p.S[(int64_t)i * k + threadIdx.x] = ss[threadIdx.x];
@@ -815,7 +839,8 @@ static int validate(const spx_rsvd_args* a) {
   SPX_REQUIRE(a->n_iter >= 0 && a->n_iter <= 8, SPX_ERR_SHAPE, "n_iter %d outside [0, 8]", a->n_iter);
   SPX_REQUIRE(dtype_ok(a->in_dtype), SPX_ERR_UNSUPPORTED, "bad input dtype");
   SPX_REQUIRE((size_t)a->m * a->r * 4 + 4 * 64 <= 200 * 1024, SPX_ERR_UNSUPPORTED, "m*r too large for one CTA");
-  SPX_REQUIRE(lift_smem(a->m, a->r, a->k) <= 200 * 1024, SPX_ERR_UNSUPPORTED, "m*k too large for one CTA");
+  SPX_REQUIRE(lift_smem(a->m, a->r, a->k, a->codes_rank_pad > a->k ? a->codes_rank_pad : a->k) <= 200 * 1024,
+              SPX_ERR_UNSUPPORTED, "rank too large for one CTA");
   if (a->num_mats == 0) return SPX_OK;
   SPX_REQUIRE(a->M && a->omega, SPX_ERR_NULL, "M and omega are required");
   SPX_REQUIRE(a->M_mat_stride == 0 || a->M_mat_stride >= (int64_t)a->m * a->n, SPX_ERR_SHAPE,
@@ -909,7 +934,7 @@ static int run_chain(const spx_rsvd_args* a, const RsvdWs& w, cudaStream_t st) {
   lp.qscale = a->qscale; lp.scale_mat_stride = a->scale_mat_stride;
   lp.qminmax = a->qminmax; lp.minmax_mat_stride = a->minmax_mat_stride;
   lp.basis = a->basis; lp.basis_dtype = a->basis_dtype; lp.basis_mat_stride = a->basis_mat_stride;
-  const size_t slq = lift_smem(m, r, k);
+  const size_t slq = lift_smem(m, r, k, lp.rank_pad);
   cudaFuncSetAttribute(lift_quant_kernel<24>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)slq);
   cudaFuncSetAttribute(lift_quant_kernel<40>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)slq);
   cudaFuncSetAttribute(lift_quant_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)slq);
