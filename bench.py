@@ -427,7 +427,9 @@ def run_ours(args, c):
                              "sample": f"{max(1, args.cpu_calls)} (sequence, layer) decodes of the workload shape "
                                        f"by the numpy port of the reference, extrapolated to a full step"},
             "clocks": clk.summary(),
-            "gpu_launches": 2 * args.steps,
+            # per decode call: RoPE packing, the cold tier and the hot-tier merge (the
+            # workspace-header memset is a runtime copy, not a kernel of this library)
+            "gpu_launches": 3 * args.steps,
             "setup_s": setup_s, "rsvd_setup_s": rsvd_setup_s,
         }
         print(json.dumps(line), flush=True)
