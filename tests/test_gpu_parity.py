@@ -323,6 +323,28 @@ def test_rsvd_ill_conditioned_sketches(case):
         assert (S_np[:, 6:] <= 1e-4 * S_np[:, :1]).all()
 
 
+@pytest.mark.parametrize("m,n,k,dtype", [(200, 96, 13, torch.float16), (384, 128, 10, torch.float32),
+                                         (256, 128, 13, torch.bfloat16)])
+def test_rsvd_odd_shapes(m, n, k, dtype):
+    """Shapes off the tensor-core fast path: m not a multiple of 128, n != 128, float32
+    input (CUDA-core products), and r = k + 8 not a multiple of 4 (the scalar branches of
+    the Gram, solve and lift kernels).  Error parity with the float64 reference algorithm
+    on the same sketch, within 1e-3."""
+    from unsloth_spectral import _ops
+    g = torch.Generator().manual_seed(21)
+    sig = 0.85 ** torch.arange(24, dtype=torch.float32)
+    M = ((torch.randn(5, m, 24, generator=g) * sig) @ torch.randn(5, 24, n, generator=g)
+         + 0.05 * torch.randn(5, m, n, generator=g)).to(dtype)
+    Omega = torch.randn(5, n, k + 8, generator=g)
+    U, S, Vh = _ops.rsvd(M.cuda(), Omega.cuda(), k, 2)
+    Mf = M.float().numpy()
+    err = so.relative_reconstruction_error(Mf, U.cpu().numpy(), S.cpu().numpy(), Vh.cpu().numpy())
+    U64, S64, Vh64 = so.batched_randomized_svd(Mf, k, 2, 8, Omega.numpy())
+    err64 = so.relative_reconstruction_error(Mf, U64, S64, Vh64)
+    assert np.abs(err - err64).max() <= 1e-3, (err, err64)
+    np.testing.assert_allclose(S.cpu().numpy(), S64, rtol=2e-3)
+
+
 def test_rsvd_zero_block():
     """An all-zero block compresses to zero singular values and zero codes, no NaN."""
     from unsloth_spectral import _ops
