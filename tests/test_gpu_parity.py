@@ -208,7 +208,9 @@ def test_decode_random_shapes_fp32(case, mode):
     _close(out, ref, 5e-4)
 
 
-@pytest.mark.parametrize("case", CASES[:3])
+# a 300-token hot tier (a warm buffer plus the hot tail) is too large to stage in shared
+# memory: the merge reads it directly from global memory
+@pytest.mark.parametrize("case", CASES[:3] + [(8, 2, 4, 4, 128, 512, 2, 16, 16, 300, False)])
 def test_decode_random_shapes_fp16(case):
     r = _random_case(*case)
     out, ref = _run_random(r, torch.float16, "decode")
