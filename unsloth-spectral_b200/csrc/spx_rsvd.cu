@@ -14,6 +14,8 @@
 // bases unless their conditioning asks for more.
 #include <math.h>
 
+#include <algorithm>
+
 #include "spx_common.cuh"
 #include "spx_rsvd.cuh"
 
@@ -167,8 +169,10 @@ __device__ __forceinline__ double recip_pos(double x) {
 // Cholesky-only kernel (one small CTA per matrix, many per SM: the 40-odd dependent
 // column steps of many matrices overlap) and a row-parallel triangular solve.  np[i]
 // holds the number of passes matrix i needs: the Gram kernel of pass 0 sets it to the
-// requested count, the Cholesky of pass 0 raises it from the pivot spread, and every
-// kernel of a later pass returns at once for a matrix that needs no more.
+// requested count npass0 and zeroes the list count, and the Cholesky of pass 0 raises it
+// from the pivot spread and appends i to a list when it does.  Passes below npass0 run
+// one CTA per matrix; a later pass (usually needed by no matrix) runs small grids that
+// stride over the listed matrices and skip those that need no more.
 constexpr int kGramChunk = 128;
 // Gram tiling: 4 x 4 tiles of the upper triangle, each split over S interleaved row
 // subsets (rows t = s mod S of every chunk) so that ~256 threads are busy; 4 x 4 tiles
@@ -190,14 +194,13 @@ size_t gram_smem(int r) {
 
 template <int RMAX>
 __global__ void __launch_bounds__(256) gram_kernel(const float* __restrict__ X, double* __restrict__ Gw,
-                                                   int* __restrict__ np, int pass, int npass0, int rows, int r) {
+                                                   int* __restrict__ np, const int* __restrict__ list,
+                                                   int* __restrict__ cnt, int pass, int npass0, int rows, int r) {
   using GT = GramTiling<RMAX>;
-  const int i = blockIdx.x, tid = threadIdx.x;
-  if (pass == 0) {
-    if (tid == 0) np[i] = npass0;
-  } else if (pass >= np[i]) {
-    return;
-  }
+  const int tid = threadIdx.x;
+  const bool listed = pass >= npass0;
+  if (pass == 0 && blockIdx.x == 0 && tid == 0) *cnt = 0;
+  if (listed && (int)blockIdx.x >= *cnt) return;   // nothing listed for this CTA
   extern __shared__ __align__(16) float gsm[];
   const int rp = r | 1;
   float* sxc = gsm;                                                        // [kGramChunk][rp]
@@ -222,187 +225,217 @@ __global__ void __launch_bounds__(256) gram_kernel(const float* __restrict__ X, 
       it_s[q] = 0;
     }
   }
-  double g[GT::TPT][16];
+  const int nk = listed ? *cnt : gridDim.x;
+  for (int kk = blockIdx.x; kk < nk; kk += gridDim.x) {
+    const int i = listed ? list[kk] : kk;
+    if (pass == 0) {
+      if (tid == 0) np[i] = npass0;
+    } else if (listed && pass >= np[i]) {
+      continue;
+    }
+    double g[GT::TPT][16];
 #pragma unroll
-  for (int q = 0; q < GT::TPT; ++q)
+    for (int q = 0; q < GT::TPT; ++q)
 #pragma unroll
-    for (int e = 0; e < 16; ++e) g[q][e] = 0.0;
-  const float* Xi = X + (int64_t)i * rows * r;
-  for (int c0 = 0; c0 < rows; c0 += kGramChunk) {
-    const int nrow = min(kGramChunk, rows - c0);
-    __syncthreads();
-    if ((r & 3) == 0) {   // float4 loads, all of a thread's in flight at once
-      const int n4 = nrow * r / 4;
-      const float4* X4 = reinterpret_cast<const float4*>(Xi + (int64_t)c0 * r);
-      constexpr int U = (kGramChunk * RMAX / 4 + 255) / 256;
-      float4 v[U];
+      for (int e = 0; e < 16; ++e) g[q][e] = 0.0;
+    const float* Xi = X + (int64_t)i * rows * r;
+    for (int c0 = 0; c0 < rows; c0 += kGramChunk) {
+      const int nrow = min(kGramChunk, rows - c0);
+      __syncthreads();
+      if ((r & 3) == 0) {   // float4 loads, all of a thread's in flight at once
+        const int n4 = nrow * r / 4;
+        const float4* X4 = reinterpret_cast<const float4*>(Xi + (int64_t)c0 * r);
+        constexpr int U = (kGramChunk * RMAX / 4 + 255) / 256;
+        float4 v[U];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int e = tid + 256 * u;
-        v[u] = e < n4 ? __ldg(X4 + e) : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
+        for (int u = 0; u < U; ++u) {
+          const int e = tid + 256 * u;
+          v[u] = e < n4 ? __ldg(X4 + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int e = 4 * (tid + 256 * u);
-        if (e < nrow * r) {
-          const int t = e / r, c = e - t * r;   // r % 4 == 0: the four stay in row t
-          float* d = sxc + t * rp + c;
-          d[0] = v[u].x;
-          d[1] = v[u].y;
-          d[2] = v[u].z;
-          d[3] = v[u].w;
+        for (int u = 0; u < U; ++u) {
+          const int e = 4 * (tid + 256 * u);
+          if (e < nrow * r) {
+            const int t = e / r, c = e - t * r;   // r % 4 == 0: the four stay in row t
+            float* d = sxc + t * rp + c;
+            d[0] = v[u].x;
+            d[1] = v[u].y;
+            d[2] = v[u].z;
+            d[3] = v[u].w;
+          }
+        }
+      } else {
+        for (int e = tid; e < nrow * r; e += 256) {
+          const int t = e / r, c = e - t * r;
+          sxc[t * rp + c] = Xi[(int64_t)c0 * r + e];
         }
       }
-    } else {
-      for (int e = tid; e < nrow * r; e += 256) {
-        const int t = e / r, c = e - t * r;
-        sxc[t * rp + c] = Xi[(int64_t)c0 * r + e];
+      // zero the columns past r of the last 4-block (read by edge tiles, never stored)
+      for (int e = tid; e < nrow * (4 * GT::NB4 - r); e += 256) {
+        const int w4 = 4 * GT::NB4 - r, t = e / w4, c = r + (e - t * w4);
+        if (c < rp) sxc[t * rp + c] = 0.f;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int q = 0; q < GT::TPT; ++q) {
+        if (it_ta[q] < 0) continue;
+        const int a0 = 4 * it_ta[q], b0 = 4 * it_tb[q];
+        for (int t = it_s[q]; t < nrow; t += GT::S) {
+          const float* xr = sxc + t * rp;
+          double xa[4], xb[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            xa[u] = a0 + u < rp ? xr[a0 + u] : 0.0;
+            xb[u] = b0 + u < rp ? xr[b0 + u] : 0.0;
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int v = 0; v < 4; ++v) g[q][4 * u + v] = fma(xa[u], xb[v], g[q][4 * u + v]);
+        }
       }
     }
-    // zero the columns past r of the last 4-block (read by edge tiles, never stored)
-    for (int e = tid; e < nrow * (4 * GT::NB4 - r); e += 256) {
-      const int w4 = 4 * GT::NB4 - r, t = e / w4, c = r + (e - t * w4);
-      if (c < rp) sxc[t * rp + c] = 0.f;
-    }
-    __syncthreads();
+    // partial sums -> shared memory; fixed-order sum over the S row subsets
 #pragma unroll
     for (int q = 0; q < GT::TPT; ++q) {
       if (it_ta[q] < 0) continue;
-      const int a0 = 4 * it_ta[q], b0 = 4 * it_tb[q];
-      for (int t = it_s[q]; t < nrow; t += GT::S) {
-        const float* xr = sxc + t * rp;
-        double xa[4], xb[4];
+      const int tile = (tid + 256 * q) / GT::S;
+      double* dst = red + ((int64_t)it_s[q] * GT::NTILE + tile) * 16;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          xa[u] = a0 + u < rp ? xr[a0 + u] : 0.0;
-          xb[u] = b0 + u < rp ? xr[b0 + u] : 0.0;
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-#pragma unroll
-          for (int v = 0; v < 4; ++v) g[q][4 * u + v] = fma(xa[u], xb[v], g[q][4 * u + v]);
+      for (int e = 0; e < 16; ++e) dst[e] = g[q][e];
+    }
+    __syncthreads();
+    double* Gi = Gw + (int64_t)i * r * r;
+    for (int e = tid; e < GT::NTILE * 16; e += 256) {
+      const int tile = e >> 4, u = (e >> 2) & 3, v = e & 3;
+      double sum = 0.0;
+      for (int s2 = 0; s2 < GT::S; ++s2) sum += red[((int64_t)s2 * GT::NTILE + tile) * 16 + (e & 15)];
+      // tile index -> (ta, tb)
+      int tb = tile, ta = 0;
+      while (tb >= GT::NB4 - ta) {
+        tb -= GT::NB4 - ta;
+        ++ta;
       }
+      tb += ta;
+      const int col = 4 * ta + u, row = 4 * tb + v;   // entry (a, b) = (col, row), a <= b for lower storage
+      if (row < r && col < r && col <= row) Gi[row * r + col] = sum;
     }
-  }
-  // partial sums -> shared memory; fixed-order sum over the S row subsets
-#pragma unroll
-  for (int q = 0; q < GT::TPT; ++q) {
-    if (it_ta[q] < 0) continue;
-    const int tile = (tid + 256 * q) / GT::S;
-    double* dst = red + ((int64_t)it_s[q] * GT::NTILE + tile) * 16;
-#pragma unroll
-    for (int e = 0; e < 16; ++e) dst[e] = g[q][e];
-  }
-  __syncthreads();
-  double* Gi = Gw + (int64_t)i * r * r;
-  for (int e = tid; e < GT::NTILE * 16; e += 256) {
-    const int tile = e >> 4, u = (e >> 2) & 3, v = e & 3;
-    double sum = 0.0;
-    for (int s2 = 0; s2 < GT::S; ++s2) sum += red[((int64_t)s2 * GT::NTILE + tile) * 16 + (e & 15)];
-    // tile index -> (ta, tb)
-    int tb = tile, ta = 0;
-    while (tb >= GT::NB4 - ta) {
-      tb -= GT::NB4 - ta;
-      ++ta;
-    }
-    tb += ta;
-    const int col = 4 * ta + u, row = 4 * tb + v;   // entry (a, b) = (col, row), a <= b for lower storage
-    if (row < r && col < r && col <= row) Gi[row * r + col] = sum;
+    __syncthreads();   // red is rewritten for the next matrix of a listed pass
   }
 }
 
 // Factor G = L L^T of one matrix per CTA, right-looking with one block barrier per
-// column: each thread owns fixed lower-triangle entries (a, c) and in step j updates
-// those with c > j from the still unscaled column j, G[a][c] -= G[a][j] G[c][j] / G[j][j],
-// and scales its entries of column j - 1 by 1 / sqrt(pivot j - 1); column j is only
-// read during step j.  The owner of diagonal entry j + 1 publishes 1 / pivot (float64,
-// a Newton-refined reciprocal) for the next step; thread NT - 1 computes 1 / sqrt(pivot)
-// at float accuracy (it only scales the float32 copy of L).  Writes Lw [r][r] f32:
-// strict lower part L, 1 / L[j][j] on the diagonal.  In pass 0 the pivot spread raises
-// np[i].
+// column.  Each thread owns fixed lower-triangle entries (a, c) and keeps them in
+// registers; in step j it updates those with c > j from the still unscaled column j,
+// G[a][c] -= G[a][j] G[c][j] / G[j][j], reading column j from a shared copy that the
+// owners of its entries published in step j - 1 (two alternating buffers, so one
+// barrier per step suffices).  The owner of diagonal entry j + 1 publishes 1 / pivot
+// (float64, a Newton-refined reciprocal) for the next step; thread NT - 1 computes
+// 1 / sqrt(pivot) at float accuracy (it only scales the float32 copy of L).  Writes
+// Lw [r][r] f32: strict lower part L (each entry times the 1 / sqrt(pivot) of its
+// column), 1 / L[j][j] on the diagonal.  In pass 0 the pivot spread raises np[i] and
+// appends i to the list of matrices that need more passes than requested.
 constexpr int kCholThreads = 128;
 template <int RMAX>
-__global__ void __launch_bounds__(kCholThreads, 8) chol_kernel(const double* __restrict__ Gw, float* __restrict__ Lw,
-                                                            int* __restrict__ np, int pass, int r) {
+__global__ void __launch_bounds__(kCholThreads, RMAX <= 24 ? 10 : RMAX <= 40 ? 8 : 6)
+    chol_kernel(const double* __restrict__ Gw, float* __restrict__ Lw, int* __restrict__ np,
+                int* __restrict__ list, int* __restrict__ cnt, int pass, int npass0, int r) {
   constexpr int NT = kCholThreads;
-  const int i = blockIdx.x, tid = threadIdx.x;
-  if (pass > 0 && pass >= np[i]) return;
-  const int rp = r | 1;
-  __shared__ double G[RMAX * (RMAX | 1)];
+  constexpr int OWN = (RMAX * (RMAX + 1) / 2 + NT - 1) / NT;
+  const int tid = threadIdx.x;
+  const bool listed = pass >= npass0;
+  if (listed && (int)blockIdx.x >= *cnt) return;   // nothing listed for this CTA
+  __shared__ double colj[2][RMAX];   // unscaled column j (rows > j), published in step j - 1
+  __shared__ double diag[RMAX];
   __shared__ double dmax_s;
   __shared__ double pivs[RMAX], coef_s[RMAX], scale_s[RMAX];
-  const double* Gi = Gw + (int64_t)i * r * r;
-  for (int e = tid; e < r * r; e += NT) {
-    const int a = e / r, c = e - a * r;
-    if (c <= a) G[a * rp + c] = Gi[e];
-  }
-  __syncthreads();
-  if (tid == 0) {
-    double dm = 0.0;
-    for (int j = 0; j < r; ++j) dm = fmax(dm, G[j * rp + j]);
-    dmax_s = dm;
-    const double p0 = G[0];
-    const bool ok = p0 > 1e-30 * dm && dm > 0.0;
-    pivs[0] = ok ? p0 : 0.0;
-    coef_s[0] = ok ? recip_pos(p0) : 0.0;
-  }
-  __syncthreads();
-  const double dmax = dmax_s;
-  constexpr int OWN = (RMAX * (RMAX + 1) / 2 + NT - 1) / NT;
-  int oa[OWN], oc[OWN];
+  int own[OWN];   // a * 256 + c, or -1
   const int ntri = r * (r + 1) / 2;
 #pragma unroll
   for (int q = 0; q < OWN; ++q) {
-    int e = tid + NT * q, a = 0;
+    const int e = tid + NT * q;
     if (e < ntri) {
-      a = (int)((sqrt(8.0 * e + 1.0) - 1.0) * 0.5);
+      int a = (int)((sqrt(8.0 * e + 1.0) - 1.0) * 0.5);
       while (a * (a + 1) / 2 > e) --a;
       while ((a + 1) * (a + 2) / 2 <= e) ++a;
-      oa[q] = a;
-      oc[q] = e - a * (a + 1) / 2;
+      own[q] = a * 256 + (e - a * (a + 1) / 2);
     } else {
-      oa[q] = -1;
-      oc[q] = -1;
+      own[q] = -1;
     }
   }
-  for (int j = 0; j < r; ++j) {
-    const double coef = coef_s[j], prev_scale = j > 0 ? scale_s[j - 1] : 0.0;
+  const int nk = listed ? *cnt : gridDim.x;
+  for (int kk = blockIdx.x; kk < nk; kk += gridDim.x) {
+    const int i = listed ? list[kk] : kk;
+    if (listed && pass >= np[i]) continue;
+    const double* Gi = Gw + (int64_t)i * r * r;
+    double g[OWN];
 #pragma unroll
     for (int q = 0; q < OWN; ++q) {
-      const int a = oa[q], c = oc[q];
-      if (c > j) {
-        const double v = fma(-G[a * rp + j] * coef, G[c * rp + j], G[a * rp + c]);
-        G[a * rp + c] = v;
-        if (a == j + 1 && c == j + 1) {
-          const bool ok = v > 1e-30 * dmax && dmax > 0.0;
-          pivs[j + 1] = ok ? v : 0.0;
-          coef_s[j + 1] = ok ? recip_pos(v) : 0.0;
-        }
-      } else if (c == j - 1 && a > c) {
-        G[a * rp + c] *= prev_scale;
+      const int a = own[q] >> 8, c = own[q] & 255;
+      g[q] = 0.0;
+      if (own[q] >= 0) {
+        g[q] = Gi[a * r + c];
+        if (c == 0) colj[0][a] = g[q];
+        if (c == a) diag[a] = g[q];
       }
     }
-    if (tid == NT - 1) scale_s[j] = pivs[j] > 0.0 ? (double)rsqrt_pos_f(pivs[j]) : 0.0;
     __syncthreads();
-  }
-  float* Li = Lw + (int64_t)i * r * r;
+    if (tid == 0) {
+      double dm = 0.0;
+      for (int j = 0; j < r; ++j) dm = fmax(dm, diag[j]);
+      dmax_s = dm;
+      const double p0 = diag[0];
+      const bool ok = p0 > 1e-30 * dm && dm > 0.0;
+      pivs[0] = ok ? p0 : 0.0;
+      coef_s[0] = ok ? recip_pos(p0) : 0.0;
+    }
+    __syncthreads();
+    const double dmax = dmax_s;
+    for (int j = 0; j < r; ++j) {
+      const double coef = coef_s[j];
+      const double* cj = colj[j & 1];
+      double* cn = colj[(j + 1) & 1];
 #pragma unroll
-  for (int q = 0; q < OWN; ++q) {
-    const int a = oa[q], c = oc[q];
-    if (c >= 0 && a > c) Li[a * r + c] = (float)G[a * rp + c];
-  }
-  for (int j = tid; j < r; j += NT) Li[j * r + j] = (float)scale_s[j];
-  if (tid == 0 && pass == 0) {
-    double pmin = 1e300, pmax = 0.0;
-    for (int j = 0; j < r; ++j)
-      if (pivs[j] > 0.0) {
-        pmin = fmin(pmin, pivs[j]);
-        pmax = fmax(pmax, pivs[j]);
+      for (int q = 0; q < OWN; ++q) {
+        const int a = own[q] >> 8, c = own[q] & 255;
+        if (own[q] >= 0 && c > j) {
+          const double v = fma(-cj[a] * coef, cj[c], g[q]);
+          g[q] = v;
+          if (c == j + 1) {
+            cn[a] = v;
+            if (a == j + 1) {
+              const bool ok = v > 1e-30 * dmax && dmax > 0.0;
+              pivs[j + 1] = ok ? v : 0.0;
+              coef_s[j + 1] = ok ? recip_pos(v) : 0.0;
+            }
+          }
+        }
       }
-    int n = np[i];
-    if (pmax > 1e6 * pmin && n < 2) n = 2;
-    if (pmax > 1e12 * pmin) n = 3;
-    np[i] = n;
+      if (tid == NT - 1) scale_s[j] = pivs[j] > 0.0 ? (double)rsqrt_pos_f(pivs[j]) : 0.0;
+      __syncthreads();
+    }
+    float* Li = Lw + (int64_t)i * r * r;
+#pragma unroll
+    for (int q = 0; q < OWN; ++q) {
+      const int a = own[q] >> 8, c = own[q] & 255;
+      if (own[q] >= 0 && a > c) Li[a * r + c] = (float)(g[q] * scale_s[c]);
+    }
+    for (int j = tid; j < r; j += NT) Li[j * r + j] = (float)scale_s[j];
+    if (tid == 0 && pass == 0) {
+      double pmin = 1e300, pmax = 0.0;
+      for (int j = 0; j < r; ++j)
+        if (pivs[j] > 0.0) {
+          pmin = fmin(pmin, pivs[j]);
+          pmax = fmax(pmax, pivs[j]);
+        }
+      const int n0 = np[i];
+      int n = n0;
+      if (pmax > 1e6 * pmin && n < 2) n = 2;
+      if (pmax > 1e12 * pmin) n = 3;
+      np[i] = n;
+      if (n > n0) list[atomicAdd(cnt, 1)] = i;
+    }
+    __syncthreads();   // shared state is rewritten for the next matrix of a listed pass
   }
 }
 
@@ -414,107 +447,115 @@ size_t trsolve_smem(int r) { return ((size_t)r * ((r + 3) & ~3) + 128 * (size_t)
 
 template <int RMAX>
 __global__ void __launch_bounds__(128) trsolve_kernel(float* __restrict__ X, const float* __restrict__ Lw,
-                                                      const int* __restrict__ np, int pass, int rows, int r) {
-  const int i = blockIdx.x, tid = threadIdx.x;
-  if (pass > 0 && pass >= np[i]) return;
+                                                      const int* __restrict__ np, const int* __restrict__ list,
+                                                      const int* __restrict__ cnt, int pass, int npass0, int rows,
+                                                      int r) {
+  const int tid = threadIdx.x;
   constexpr int R4 = (RMAX + 3) & ~3;
   extern __shared__ __align__(16) float tsm[];
   const int r4 = (r + 3) & ~3, rp = r | 1;
   float* Ls = tsm;             // [r][r4]
   float* sx = tsm + r * r4;    // [128][rp]
-  const float* Li = Lw + (int64_t)i * r * r;
-  const int t0 = blockIdx.y * 128, nrow = min(128, rows - t0);
-  float* Xc = X + ((int64_t)i * rows + t0) * r;
-  const bool vec = (r & 3) == 0;
-  if (vec) {   // r4 == r: L and the chunk are contiguous; float4 loads, all in flight at once
-    constexpr int UL = (RMAX * RMAX / 4 + 127) / 128, UX = (128 * RMAX / 4 + 127) / 128;
-    const float4* L4 = reinterpret_cast<const float4*>(Li);
-    const float4* X4 = reinterpret_cast<const float4*>(Xc);
-    const int nl4 = r * r / 4, nx4 = nrow * r / 4;
-    float4 vl[UL], vx[UX];
+  const bool listed = pass >= npass0;
+  const int nk = listed ? *cnt : gridDim.x;
+  for (int kk = blockIdx.x; kk < nk; kk += gridDim.x) {
+    const int i = listed ? list[kk] : kk;
+    if (listed && pass >= np[i]) continue;
+    const float* Li = Lw + (int64_t)i * r * r;
+    const int t0 = blockIdx.y * 128, nrow = min(128, rows - t0);
+    float* Xc = X + ((int64_t)i * rows + t0) * r;
+    const bool vec = (r & 3) == 0;
+    if (vec) {   // r4 == r: L and the chunk are contiguous; float4 loads, all in flight at once
+      constexpr int UL = (RMAX * RMAX / 4 + 127) / 128, UX = (128 * RMAX / 4 + 127) / 128;
+      const float4* L4 = reinterpret_cast<const float4*>(Li);
+      const float4* X4 = reinterpret_cast<const float4*>(Xc);
+      const int nl4 = r * r / 4, nx4 = nrow * r / 4;
+      float4 vl[UL], vx[UX];
 #pragma unroll
-    for (int u = 0; u < UL; ++u) {
-      const int e = tid + 128 * u;
-      vl[u] = e < nl4 ? __ldg(L4 + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int u = 0; u < UL; ++u) {
+        const int e = tid + 128 * u;
+        vl[u] = e < nl4 ? __ldg(L4 + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < UX; ++u) {
+        const int e = tid + 128 * u;
+        vx[u] = e < nx4 ? X4[e] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < UL; ++u) {
+        const int e = tid + 128 * u;
+        if (e < nl4) reinterpret_cast<float4*>(Ls)[e] = vl[u];
+      }
+#pragma unroll
+      for (int u = 0; u < UX; ++u) {
+        const int e = tid + 128 * u;
+        if (e < nx4) {
+          const int t = (4 * e) / r, c = 4 * e - t * r;
+          float* d = sx + t * rp + c;
+          d[0] = vx[u].x;
+          d[1] = vx[u].y;
+          d[2] = vx[u].z;
+          d[3] = vx[u].w;
+        }
+      }
+    } else {
+      for (int e = tid; e < r * r4; e += 128) {
+        const int j = e / r4, c = e - j * r4;
+        Ls[e] = c < r ? Li[j * r + c] : 0.f;
+      }
+      for (int e = tid; e < nrow * r; e += 128) {
+        const int t = e / r, c = e - t * r;
+        sx[t * rp + c] = Xc[e];
+      }
     }
+    __syncthreads();
+    if (tid < nrow) {
+      float* xr = sx + tid * rp;
+      float x[R4];
 #pragma unroll
-    for (int u = 0; u < UX; ++u) {
-      const int e = tid + 128 * u;
-      vx[u] = e < nx4 ? X4[e] : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int c = 0; c < R4; ++c) x[c] = c < r ? xr[c] : 0.f;
+#pragma unroll
+      for (int j = 0; j < RMAX; ++j) {
+        if (j < r) {
+          const float4* lj = reinterpret_cast<const float4*>(Ls + j * r4);
+          float a0 = x[j], a1 = 0.f;
+#pragma unroll
+          for (int c = 0; c < (j & ~3); c += 4) {   // entries c < j in whole quads
+            const float4 l = lj[c >> 2];
+            a0 = fmaf(-x[c], l.x, a0);
+            a1 = fmaf(-x[c + 1], l.y, a1);
+            a0 = fmaf(-x[c + 2], l.z, a0);
+            a1 = fmaf(-x[c + 3], l.w, a1);
+          }
+          if (j & 3) {   // the partial quad holding columns (j & ~3) .. j - 1 and the diagonal
+            const float4 l = lj[j >> 2];
+            const int c = j & ~3;
+            a0 = fmaf(-x[c], l.x, a0);
+            if ((j & 3) > 1) a1 = fmaf(-x[c + 1], l.y, a1);
+            if ((j & 3) > 2) a0 = fmaf(-x[c + 2], l.z, a0);
+          }
+          x[j] = (a0 + a1) * Ls[j * r4 + j];
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < R4; ++c)
+        if (c < r) xr[c] = x[c];
     }
-#pragma unroll
-    for (int u = 0; u < UL; ++u) {
-      const int e = tid + 128 * u;
-      if (e < nl4) reinterpret_cast<float4*>(Ls)[e] = vl[u];
-    }
-#pragma unroll
-    for (int u = 0; u < UX; ++u) {
-      const int e = tid + 128 * u;
-      if (e < nx4) {
+    __syncthreads();
+    if (vec) {
+      float4* X4 = reinterpret_cast<float4*>(Xc);
+      for (int e = tid; e < nrow * r / 4; e += 128) {
         const int t = (4 * e) / r, c = 4 * e - t * r;
-        float* d = sx + t * rp + c;
-        d[0] = vx[u].x;
-        d[1] = vx[u].y;
-        d[2] = vx[u].z;
-        d[3] = vx[u].w;
+        const float* d = sx + t * rp + c;
+        X4[e] = make_float4(d[0], d[1], d[2], d[3]);
+      }
+    } else {
+      for (int e = tid; e < nrow * r; e += 128) {
+        const int t = e / r, c = e - t * r;
+        Xc[e] = sx[t * rp + c];
       }
     }
-  } else {
-    for (int e = tid; e < r * r4; e += 128) {
-      const int j = e / r4, c = e - j * r4;
-      Ls[e] = c < r ? Li[j * r + c] : 0.f;
-    }
-    for (int e = tid; e < nrow * r; e += 128) {
-      const int t = e / r, c = e - t * r;
-      sx[t * rp + c] = Xc[e];
-    }
-  }
-  __syncthreads();
-  if (tid < nrow) {
-    float* xr = sx + tid * rp;
-    float x[R4];
-#pragma unroll
-    for (int c = 0; c < R4; ++c) x[c] = c < r ? xr[c] : 0.f;
-#pragma unroll
-    for (int j = 0; j < RMAX; ++j) {
-      if (j < r) {
-        const float4* lj = reinterpret_cast<const float4*>(Ls + j * r4);
-        float a0 = x[j], a1 = 0.f;
-#pragma unroll
-        for (int c = 0; c < (j & ~3); c += 4) {   // entries c < j in whole quads
-          const float4 l = lj[c >> 2];
-          a0 = fmaf(-x[c], l.x, a0);
-          a1 = fmaf(-x[c + 1], l.y, a1);
-          a0 = fmaf(-x[c + 2], l.z, a0);
-          a1 = fmaf(-x[c + 3], l.w, a1);
-        }
-        if (j & 3) {   // the partial quad holding columns (j & ~3) .. j - 1 and the diagonal
-          const float4 l = lj[j >> 2];
-          const int c = j & ~3;
-          a0 = fmaf(-x[c], l.x, a0);
-          if ((j & 3) > 1) a1 = fmaf(-x[c + 1], l.y, a1);
-          if ((j & 3) > 2) a0 = fmaf(-x[c + 2], l.z, a0);
-        }
-        x[j] = (a0 + a1) * Ls[j * r4 + j];
-      }
-    }
-#pragma unroll
-    for (int c = 0; c < R4; ++c)
-      if (c < r) xr[c] = x[c];
-  }
-  __syncthreads();
-  if (vec) {
-    float4* X4 = reinterpret_cast<float4*>(Xc);
-    for (int e = tid; e < nrow * r / 4; e += 128) {
-      const int t = (4 * e) / r, c = 4 * e - t * r;
-      const float* d = sx + t * rp + c;
-      X4[e] = make_float4(d[0], d[1], d[2], d[3]);
-    }
-  } else {
-    for (int e = tid; e < nrow * r; e += 128) {
-      const int t = e / r, c = e - t * r;
-      Xc[e] = sx[t * rp + c];
-    }
+    __syncthreads();   // shared memory is rewritten for the next matrix of a listed pass
   }
 }
 
@@ -805,6 +846,8 @@ struct RsvdWs {
   double* G;   // [Nb][r][r] Gram matrices of the split Cholesky-QR
   float* L;    // [Nb][r][r] its factors
   int* np;     // [Nb] passes each matrix needs
+  int* list;   // [Nb] matrices that need more passes than requested
+  int* cnt;    // [1] entries of list
   size_t bytes;
 };
 
@@ -825,6 +868,8 @@ static RsvdWs carve(const spx_rsvd_args* a, char* base) {
   w.G = reinterpret_cast<double*>(take(Nb * a->r * a->r * sizeof(double)));
   w.L = take(Nb * a->r * a->r * sizeof(float));
   w.np = reinterpret_cast<int*>(take(Nb * sizeof(int)));
+  w.list = reinterpret_cast<int*>(take(Nb * sizeof(int)));
+  w.cnt = reinterpret_cast<int*>(take(sizeof(int)));
   w.bytes = off;
   return w;
 }
@@ -874,23 +919,31 @@ static int run_chain(const spx_rsvd_args* a, const RsvdWs& w, cudaStream_t st) {
   cudaFuncSetAttribute(gram_kernel<40>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
   cudaFuncSetAttribute(gram_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
   // Cholesky-QR: npass 2 for the final basis Q (it feeds Bp and the lift), 1 for the
-  // intermediate ones; three kernels per pass (Gram, factor, solve)
+  // intermediate ones; three kernels per pass (Gram, factor, solve).  A pass past the
+  // requested count runs grids of about one wave that stride over the listed matrices.
+  int dev = 0, nsm = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   auto orth = [&](float* X, int rows, int npass) {
-    const dim3 gs(Nb, (rows + 127) / 128);
+    const int nch = (rows + 127) / 128;
     const size_t sg = gram_smem(r), ts = trsolve_smem(r);
     for (int pass = 0; pass < 3; ++pass) {
+      const bool listed = pass >= npass;
+      const int gg = listed ? std::min(Nb, 4 * nsm) : Nb;
+      const int gc = listed ? std::min(Nb, 8 * nsm) : Nb;
+      const dim3 gs(listed ? std::min(Nb, std::max(nsm, 8 * nsm / nch)) : Nb, nch);
       if (r <= 24) {
-        gram_kernel<24><<<Nb, 256, sg, st>>>(X, w.G, w.np, pass, npass, rows, r);
-        chol_kernel<24><<<Nb, kCholThreads, 0, st>>>(w.G, w.L, w.np, pass, r);
-        trsolve_kernel<24><<<gs, 128, ts, st>>>(X, w.L, w.np, pass, rows, r);
+        gram_kernel<24><<<gg, 256, sg, st>>>(X, w.G, w.np, w.list, w.cnt, pass, npass, rows, r);
+        chol_kernel<24><<<gc, kCholThreads, 0, st>>>(w.G, w.L, w.np, w.list, w.cnt, pass, npass, r);
+        trsolve_kernel<24><<<gs, 128, ts, st>>>(X, w.L, w.np, w.list, w.cnt, pass, npass, rows, r);
       } else if (r <= 40) {
-        gram_kernel<40><<<Nb, 256, sg, st>>>(X, w.G, w.np, pass, npass, rows, r);
-        chol_kernel<40><<<Nb, kCholThreads, 0, st>>>(w.G, w.L, w.np, pass, r);
-        trsolve_kernel<40><<<gs, 128, ts, st>>>(X, w.L, w.np, pass, rows, r);
+        gram_kernel<40><<<gg, 256, sg, st>>>(X, w.G, w.np, w.list, w.cnt, pass, npass, rows, r);
+        chol_kernel<40><<<gc, kCholThreads, 0, st>>>(w.G, w.L, w.np, w.list, w.cnt, pass, npass, r);
+        trsolve_kernel<40><<<gs, 128, ts, st>>>(X, w.L, w.np, w.list, w.cnt, pass, npass, rows, r);
       } else {
-        gram_kernel<64><<<Nb, 256, sg, st>>>(X, w.G, w.np, pass, npass, rows, r);
-        chol_kernel<64><<<Nb, kCholThreads, 0, st>>>(w.G, w.L, w.np, pass, r);
-        trsolve_kernel<64><<<gs, 128, ts, st>>>(X, w.L, w.np, pass, rows, r);
+        gram_kernel<64><<<gg, 256, sg, st>>>(X, w.G, w.np, w.list, w.cnt, pass, npass, rows, r);
+        chol_kernel<64><<<gc, kCholThreads, 0, st>>>(w.G, w.L, w.np, w.list, w.cnt, pass, npass, r);
+        trsolve_kernel<64><<<gs, 128, ts, st>>>(X, w.L, w.np, w.list, w.cnt, pass, npass, rows, r);
       }
     }
   };
@@ -915,7 +968,6 @@ static int run_chain(const spx_rsvd_args* a, const RsvdWs& w, cudaStream_t st) {
   mty(w.Y, w.Z);
   int rc = launch_status("rsvd gemm/orth chain");
   if (rc != SPX_OK) return rc;
-  const int rp = (r + 1) & ~1;
   const size_t ssvd = small_svd_smem(n, r);
   cudaFuncSetAttribute(small_svd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssvd);
   small_svd_kernel<<<Nb, 256, ssvd, st>>>(w.Z, w.Wk, w.S, w.Vh, n, r, k);
