@@ -347,6 +347,35 @@ def test_rsvd_odd_shapes(m, n, k, dtype):
     np.testing.assert_allclose(S.cpu().numpy(), S64, rtol=2e-3)
 
 
+@pytest.mark.parametrize("nb,m,dtype", [(700, 512, torch.float16), (650, 128, torch.bfloat16)])
+def test_rsvd_many_blocks(nb, m, dtype):
+    """Batches of several waves of CTAs (two resident per SM), including single-tile
+    blocks (m = 128).  The tensor-core path on 16-bit input must agree with the CUDA-core
+    path on the same values as float32 (both products are float32 accurate), and blocks
+    around the wave boundaries match the float64 reference algorithm's error within 1e-3."""
+    from unsloth_spectral import _ops
+    g = torch.Generator().manual_seed(33)
+    k = 16
+    sig = 0.8 ** torch.arange(32, dtype=torch.float32)
+    M16 = ((torch.randn(nb, m, 32, generator=g) * sig) @ torch.randn(nb, 32, 128, generator=g)
+           + 0.02 * torch.randn(nb, m, 128, generator=g)).to(dtype)
+    Omega = torch.randn(nb, 128, k + 8, generator=g)
+    U, S, Vh = _ops.rsvd(M16.cuda(), Omega.cuda(), k, 2)
+    U32, S32, Vh32 = _ops.rsvd(M16.float().cuda(), Omega.cuda(), k, 2)
+    assert torch.isfinite(S).all() and torch.isfinite(U).all() and torch.isfinite(Vh).all()
+    torch.testing.assert_close(S, S32, rtol=1e-4, atol=1e-5 * S32[:, :1].max().item())
+    R = (U * S[:, None, :]) @ Vh
+    R32 = (U32 * S32[:, None, :]) @ Vh32
+    rel = (R - R32).norm(dim=(1, 2)) / R32.norm(dim=(1, 2))
+    assert rel.max().item() <= 1e-4, rel.max().item()
+    idx = [0, 1, 147, 148, 295, 296, 297, 591, 592, nb - 1]
+    Mf = M16[idx].float().numpy()
+    err = so.relative_reconstruction_error(Mf, U[idx].cpu().numpy(), S[idx].cpu().numpy(), Vh[idx].cpu().numpy())
+    U64, S64, Vh64 = so.batched_randomized_svd(Mf, k, 2, 8, Omega[idx].numpy())
+    err64 = so.relative_reconstruction_error(Mf, U64, S64, Vh64)
+    assert np.abs(err - err64).max() <= 1e-3, (err, err64)
+
+
 def test_rsvd_zero_block():
     """An all-zero block compresses to zero singular values and zero codes, no NaN."""
     from unsloth_spectral import _ops
