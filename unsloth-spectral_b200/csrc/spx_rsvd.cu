@@ -174,55 +174,71 @@ __device__ __forceinline__ double recip_pos(double x) {
 // one CTA per matrix; a later pass (usually needed by no matrix) runs small grids that
 // stride over the listed matrices and skip those that need no more.
 constexpr int kGramChunk = 128;
-// Gram tiling: 4 x 4 tiles of the upper triangle, each split over S interleaved row
-// subsets (rows t = s mod S of every chunk) so that ~256 threads are busy; 4 x 4 tiles
-// halve the float32 -> float64 conversions per FMA of 2 x 2 tiles.  The S partial sums
-// of an entry are added in a fixed order, so the result is deterministic.
+// Gram tiling: 4 x 4 tiles of the upper triangle, taken in pairs (ta, tb), (ta, tb + 1)
+// that share the a-block, so a row converts 12 float32 values to float64 per 32 FMAs (16
+// for two separate tiles; the float32 -> float64 conversion issues at a quarter of the
+// float64 FMA rate).  A pair is split over S interleaved row subsets (rows t = s mod S of
+// every chunk) so that most threads are busy; the S partial sums of an entry are added in
+// a fixed order, so the result is deterministic.  The chunk's row pitch P covers every
+// column a tile reads (columns r .. 4 NB4 - 1 are zero), so the inner loop has no bounds
+// tests.  The last pair of an odd row of tiles computes a dummy second tile, not stored.
+__host__ __device__ constexpr int gram_npair(int nb4) {
+  int n = 0;
+  for (int ta = 0; ta < nb4; ++ta) n += (nb4 - ta + 1) / 2;
+  return n;
+}
 template <int RMAX>
 struct GramTiling {
   static constexpr int NB4 = (RMAX + 3) / 4;
   static constexpr int NTILE = NB4 * (NB4 + 1) / 2;
-  static constexpr int S = NTILE * 8 <= 256 ? 8 : NTILE * 4 <= 256 ? 4 : NTILE * 2 <= 256 ? 2 : 1;
-  static constexpr int TPT = (NTILE * S + 255) / 256;   // items per thread
+  static constexpr int NPAIR = gram_npair(NB4);
+  static constexpr int NT = RMAX > 40 ? 256 : 128;   // threads
+  static constexpr int S = NT / NPAIR >= 8 ? 8 : NT / NPAIR >= 1 ? NT / NPAIR : 1;
+  static constexpr int TPT = (NPAIR * S + NT - 1) / NT;   // items per thread
+  static constexpr int P = (4 * NB4) | 1;                 // chunk row pitch (floats)
+  static constexpr int CHUNK_FLOATS = (kGramChunk * P + 3) & ~3;
+  static constexpr size_t SMEM = (size_t)CHUNK_FLOATS * sizeof(float) + (size_t)S * NTILE * 16 * sizeof(double);
 };
 size_t gram_smem(int r) {
-  const int rmax = r <= 24 ? 24 : r <= 40 ? 40 : 64;
-  const int nb4 = (rmax + 3) / 4, ntile = nb4 * (nb4 + 1) / 2;
-  const int S = ntile * 8 <= 256 ? 8 : ntile * 4 <= 256 ? 4 : ntile * 2 <= 256 ? 2 : 1;
-  return (size_t)kGramChunk * (r | 1) * sizeof(float) + (size_t)S * ntile * 16 * sizeof(double);
+  return r <= 24 ? GramTiling<24>::SMEM : r <= 40 ? GramTiling<40>::SMEM : GramTiling<64>::SMEM;
 }
+int gram_threads(int r) { return r <= 24 ? GramTiling<24>::NT : r <= 40 ? GramTiling<40>::NT : GramTiling<64>::NT; }
 
 template <int RMAX>
-__global__ void __launch_bounds__(256) gram_kernel(const float* __restrict__ X, double* __restrict__ Gw,
+__global__ void __launch_bounds__(GramTiling<RMAX>::NT, RMAX > 40 ? 1 : 4) gram_kernel(const float* __restrict__ X, double* __restrict__ Gw,
                                                    int* __restrict__ np, const int* __restrict__ list,
                                                    int* __restrict__ cnt, int pass, int npass0, int rows, int r) {
   using GT = GramTiling<RMAX>;
+  constexpr int NT = GT::NT, P = GT::P;
   const int tid = threadIdx.x;
   const bool listed = pass >= npass0;
   if (pass == 0 && blockIdx.x == 0 && tid == 0) *cnt = 0;
   if (listed && (int)blockIdx.x >= *cnt) return;   // nothing listed for this CTA
   extern __shared__ __align__(16) float gsm[];
-  const int rp = r | 1;
-  float* sxc = gsm;                                                        // [kGramChunk][rp]
-  double* red = reinterpret_cast<double*>(gsm + ((kGramChunk * rp + 3) & ~3));   // [S][NTILE][16]
-  // items: (tile, row subset); tile (ta, tb), ta <= tb, of 4 x 4 blocks
-  int it_ta[GT::TPT], it_tb[GT::TPT], it_s[GT::TPT];
+  float* sxc = gsm;                                                   // [kGramChunk][P]
+  double* red = reinterpret_cast<double*>(gsm + GT::CHUNK_FLOATS);    // [S][NTILE][16]
+  // items: (pair, row subset); pair (ta, tb), (ta, tb + 1) of 4 x 4 blocks, ta <= tb
+  int it_a[GT::TPT], it_b[GT::TPT], it_c[GT::TPT], it_s[GT::TPT], it_t0[GT::TPT];
+  bool it_two[GT::TPT];
 #pragma unroll
   for (int q = 0; q < GT::TPT; ++q) {
-    const int item = tid + 256 * q;
-    if (item < GT::NTILE * GT::S) {
-      int tb = item / GT::S, ta = 0;
-      it_s[q] = item - tb * GT::S;
-      while (tb >= GT::NB4 - ta) {
-        tb -= GT::NB4 - ta;
+    const int item = tid + NT * q;
+    it_a[q] = -1;
+    it_b[q] = it_c[q] = it_s[q] = it_t0[q] = 0;
+    it_two[q] = false;
+    if (item < GT::NPAIR * GT::S) {
+      int p = item / GT::S, ta = 0;
+      it_s[q] = item - p * GT::S;
+      while (p >= (GT::NB4 - ta + 1) / 2) {
+        p -= (GT::NB4 - ta + 1) / 2;
         ++ta;
       }
-      it_ta[q] = ta;
-      it_tb[q] = ta + tb;
-    } else {
-      it_ta[q] = -1;
-      it_tb[q] = -1;
-      it_s[q] = 0;
+      const int tb = ta + 2 * p;
+      it_two[q] = tb + 1 < GT::NB4;
+      it_a[q] = 4 * ta;
+      it_b[q] = 4 * tb;
+      it_c[q] = it_two[q] ? 4 * (tb + 1) : 4 * ta;   // dummy second tile: any valid columns
+      it_t0[q] = ta * GT::NB4 - ta * (ta - 1) / 2 + (tb - ta);   // tile index of (ta, tb)
     }
   }
   const int nk = listed ? *cnt : gridDim.x;
@@ -233,11 +249,11 @@ __global__ void __launch_bounds__(256) gram_kernel(const float* __restrict__ X, 
     } else if (listed && pass >= np[i]) {
       continue;
     }
-    double g[GT::TPT][16];
+    double g[GT::TPT][2][16];
 #pragma unroll
     for (int q = 0; q < GT::TPT; ++q)
 #pragma unroll
-      for (int e = 0; e < 16; ++e) g[q][e] = 0.0;
+      for (int e = 0; e < 16; ++e) g[q][0][e] = g[q][1][e] = 0.0;
     const float* Xi = X + (int64_t)i * rows * r;
     for (int c0 = 0; c0 < rows; c0 += kGramChunk) {
       const int nrow = min(kGramChunk, rows - c0);
@@ -245,19 +261,19 @@ __global__ void __launch_bounds__(256) gram_kernel(const float* __restrict__ X, 
       if ((r & 3) == 0) {   // float4 loads, all of a thread's in flight at once
         const int n4 = nrow * r / 4;
         const float4* X4 = reinterpret_cast<const float4*>(Xi + (int64_t)c0 * r);
-        constexpr int U = (kGramChunk * RMAX / 4 + 255) / 256;
+        constexpr int U = (kGramChunk * RMAX / 4 + NT - 1) / NT;
         float4 v[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-          const int e = tid + 256 * u;
+          const int e = tid + NT * u;
           v[u] = e < n4 ? __ldg(X4 + e) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-          const int e = 4 * (tid + 256 * u);
+          const int e = 4 * (tid + NT * u);
           if (e < nrow * r) {
             const int t = e / r, c = e - t * r;   // r % 4 == 0: the four stay in row t
-            float* d = sxc + t * rp + c;
+            float* d = sxc + t * P + c;
             d[0] = v[u].x;
             d[1] = v[u].y;
             d[2] = v[u].z;
@@ -265,48 +281,57 @@ __global__ void __launch_bounds__(256) gram_kernel(const float* __restrict__ X, 
           }
         }
       } else {
-        for (int e = tid; e < nrow * r; e += 256) {
+        for (int e = tid; e < nrow * r; e += NT) {
           const int t = e / r, c = e - t * r;
-          sxc[t * rp + c] = Xi[(int64_t)c0 * r + e];
+          sxc[t * P + c] = Xi[(int64_t)c0 * r + e];
         }
       }
-      // zero the columns past r of the last 4-block (read by edge tiles, never stored)
-      for (int e = tid; e < nrow * (4 * GT::NB4 - r); e += 256) {
-        const int w4 = 4 * GT::NB4 - r, t = e / w4, c = r + (e - t * w4);
-        if (c < rp) sxc[t * rp + c] = 0.f;
+      // zero the columns r .. 4 NB4 - 1 (read by edge tiles, never stored)
+      for (int e = tid; e < nrow * (4 * GT::NB4 - r); e += NT) {
+        const int w4 = 4 * GT::NB4 - r, t = e / w4;
+        sxc[t * P + r + (e - t * w4)] = 0.f;
       }
       __syncthreads();
 #pragma unroll
       for (int q = 0; q < GT::TPT; ++q) {
-        if (it_ta[q] < 0) continue;
-        const int a0 = 4 * it_ta[q], b0 = 4 * it_tb[q];
+        if (it_a[q] < 0) continue;
+        const float* xa_p = sxc + it_a[q];
+        const float* xb_p = sxc + it_b[q];
+        const float* xc_p = sxc + it_c[q];
+#pragma unroll 2
         for (int t = it_s[q]; t < nrow; t += GT::S) {
-          const float* xr = sxc + t * rp;
-          double xa[4], xb[4];
+          double xa[4], xb[4], xc[4];
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
-            xa[u] = a0 + u < rp ? xr[a0 + u] : 0.0;
-            xb[u] = b0 + u < rp ? xr[b0 + u] : 0.0;
+            xa[u] = xa_p[t * P + u];
+            xb[u] = xb_p[t * P + u];
+            xc[u] = xc_p[t * P + u];
           }
 #pragma unroll
           for (int u = 0; u < 4; ++u)
 #pragma unroll
-            for (int v = 0; v < 4; ++v) g[q][4 * u + v] = fma(xa[u], xb[v], g[q][4 * u + v]);
+            for (int v = 0; v < 4; ++v) {
+              g[q][0][4 * u + v] = fma(xa[u], xb[v], g[q][0][4 * u + v]);
+              g[q][1][4 * u + v] = fma(xa[u], xc[v], g[q][1][4 * u + v]);
+            }
         }
       }
     }
     // partial sums -> shared memory; fixed-order sum over the S row subsets
 #pragma unroll
     for (int q = 0; q < GT::TPT; ++q) {
-      if (it_ta[q] < 0) continue;
-      const int tile = (tid + 256 * q) / GT::S;
-      double* dst = red + ((int64_t)it_s[q] * GT::NTILE + tile) * 16;
+      if (it_a[q] < 0) continue;
+      double* dst = red + ((int64_t)it_s[q] * GT::NTILE + it_t0[q]) * 16;
 #pragma unroll
-      for (int e = 0; e < 16; ++e) dst[e] = g[q][e];
+      for (int e = 0; e < 16; ++e) dst[e] = g[q][0][e];
+      if (it_two[q]) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) dst[16 + e] = g[q][1][e];   // tile (ta, tb + 1) is the next index
+      }
     }
     __syncthreads();
     double* Gi = Gw + (int64_t)i * r * r;
-    for (int e = tid; e < GT::NTILE * 16; e += 256) {
+    for (int e = tid; e < GT::NTILE * 16; e += NT) {
       const int tile = e >> 4, u = (e >> 2) & 3, v = e & 3;
       double sum = 0.0;
       for (int s2 = 0; s2 < GT::S; ++s2) sum += red[((int64_t)s2 * GT::NTILE + tile) * 16 + (e & 15)];
@@ -933,15 +958,15 @@ static int run_chain(const spx_rsvd_args* a, const RsvdWs& w, cudaStream_t st) {
       const int gc = listed ? std::min(Nb, 8 * nsm) : Nb;
       const dim3 gs(listed ? std::min(Nb, std::max(nsm, 8 * nsm / nch)) : Nb, nch);
       if (r <= 24) {
-        gram_kernel<24><<<gg, 256, sg, st>>>(X, w.G, w.np, w.list, w.cnt, pass, npass, rows, r);
+        gram_kernel<24><<<gg, gram_threads(r), sg, st>>>(X, w.G, w.np, w.list, w.cnt, pass, npass, rows, r);
         chol_kernel<24><<<gc, kCholThreads, 0, st>>>(w.G, w.L, w.np, w.list, w.cnt, pass, npass, r);
         trsolve_kernel<24><<<gs, 128, ts, st>>>(X, w.L, w.np, w.list, w.cnt, pass, npass, rows, r);
       } else if (r <= 40) {
-        gram_kernel<40><<<gg, 256, sg, st>>>(X, w.G, w.np, w.list, w.cnt, pass, npass, rows, r);
+        gram_kernel<40><<<gg, gram_threads(r), sg, st>>>(X, w.G, w.np, w.list, w.cnt, pass, npass, rows, r);
         chol_kernel<40><<<gc, kCholThreads, 0, st>>>(w.G, w.L, w.np, w.list, w.cnt, pass, npass, r);
         trsolve_kernel<40><<<gs, 128, ts, st>>>(X, w.L, w.np, w.list, w.cnt, pass, npass, rows, r);
       } else {
-        gram_kernel<64><<<gg, 256, sg, st>>>(X, w.G, w.np, w.list, w.cnt, pass, npass, rows, r);
+        gram_kernel<64><<<gg, gram_threads(r), sg, st>>>(X, w.G, w.np, w.list, w.cnt, pass, npass, rows, r);
         chol_kernel<64><<<gc, kCholThreads, 0, st>>>(w.G, w.L, w.np, w.list, w.cnt, pass, npass, r);
         trsolve_kernel<64><<<gs, 128, ts, st>>>(X, w.L, w.np, w.list, w.cnt, pass, npass, rows, r);
       }
