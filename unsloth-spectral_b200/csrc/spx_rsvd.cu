@@ -598,6 +598,11 @@ __global__ void __launch_bounds__(128) trsolve_kernel(float* __restrict__ X, con
 // relations |a_p'|^2 = |a_p|^2 - t a_p.a_q, |a_q'|^2 = |a_q|^2 + t a_p.a_q, so a rotation
 // needs one reduction (a_p . a_q) instead of three.
 // Outputs Wk f32 [r][k], S f32 [k], Vh f32 [k][n] (descending singular values).
+__device__ __forceinline__ float sqrt_approx(float x) {
+  float y;
+  asm("sqrt.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 size_t small_svd_smem(int n, int r) {
   const int rp = (r + 1) & ~1;
   return ((size_t)rp * 128 + (size_t)rp * rp + 2 * rp) * sizeof(float) + rp * sizeof(int);
@@ -635,8 +640,11 @@ __global__ void __launch_bounds__(256) small_svd_kernel(const float* __restrict_
     __syncthreads();
     for (int round = 0; round < nn; ++round) {
       for (int u = 4 * warp + grp; u < np; u += 4 * nw) {
-        int p = u == 0 ? round : (round + u) % nn;
-        int q = u == 0 ? nn : (round - u + nn) % nn;
+        // pair u of the round: 0 <= round < nn and 1 <= u < np <= nn, so one wrap suffices
+        int p = round + u, q = round - u;
+        if (p >= nn) p -= nn;
+        if (q < 0) q += nn;
+        if (u == 0) q = nn;
         if (p > q) { const int tmp = p; p = q; q = tmp; }
         if (q >= r) continue;   // the padding column (uniform across the group)
         float4* cp = reinterpret_cast<float4*>(A + p * 128);
@@ -652,10 +660,12 @@ __global__ void __launch_bounds__(256) small_svd_kernel(const float* __restrict_
 #pragma unroll
         for (int o = 4; o > 0; o >>= 1) ga += __shfl_xor_sync(gmask, ga, o);
         const float al = n2[p], be = n2[q];
-        if (!(fabsf(ga) > 2e-6f * sqrtf(al * be)) || ga == 0.f) continue;
-        const float zeta = (be - al) / (2.f * ga);
-        const float t = (zeta >= 0.f ? 1.f : -1.f) / (fabsf(zeta) + sqrtf(1.f + zeta * zeta));
-        const float c = rsqrtf(1.f + t * t), sn = t * c;
+        if (!(ga * ga > 4e-12f * (al * be)) || ga == 0.f) continue;   // |ga| > 2e-6 sqrt(al be)
+        // the rotation: approximate division and square root are enough, since c and s
+        // are formed as rsqrt(1 + t^2) and t c, a rotation whatever the rounding of t
+        const float zeta = __fdividef(be - al, 2.f * ga);
+        const float t = __fdividef(zeta >= 0.f ? 1.f : -1.f, fabsf(zeta) + sqrt_approx(fmaf(zeta, zeta, 1.f)));
+        const float c = rsqrtf(fmaf(t, t, 1.f)), sn = t * c;
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
           float4 np4, nq4;
