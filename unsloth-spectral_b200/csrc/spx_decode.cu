@@ -17,6 +17,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <type_traits>
+
 #include "spx_common.cuh"
 #include "spx_decode.cuh"
 
@@ -147,14 +149,17 @@ __host__ __device__ inline size_t hot_merge_base_floats(const DecodeParams& p) {
   return (f + 3) & ~(size_t)3;
 }
 
-template <typename T, bool STAGE>
+template <typename T, bool STAGE, int NREP>
 __global__ void __launch_bounds__(256) hot_merge_kernel(DecodeParams p) {
   // STAGE: the hot K and V rows and the cold partial records are first copied to shared
   // memory with 16-byte asynchronous copies, all in flight at once, instead of being
-  // read in many dependent rounds of global loads
+  // read in many dependent rounds of global loads.  NREP: the query heads per KV head
+  // when it is one of the compiled counts (the per-head loops then carry no tests), 0
+  // for any other count (loops over kMaxRep heads, tested against p.nrep).
+  constexpr int RR = NREP > 0 ? NREP : kMaxRep;
   const int g = blockIdx.x, lb = blockIdx.y;
   const int b = lb % p.B;
-  const int D = p.D, half = D / 2, nrep = p.nrep, hot = p.hot, nb = p.nblk, nc = p.ncold;
+  const int D = p.D, half = D / 2, nrep = NREP > 0 ? NREP : p.nrep, hot = p.hot, nb = p.nblk, nc = p.ncold;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   extern __shared__ float sm[];
   float* sq = sm;                   // [nrep][D]
@@ -203,9 +208,9 @@ __global__ void __launch_bounds__(256) hot_merge_kernel(DecodeParams p) {
     const float* cr = p.cosT + a * D;
     const float* sr = p.sinT + a * D;
     const T* krow = hk + (int64_t)t * D;
-    float s[kMaxRep];
+    float s[RR];
 #pragma unroll
-    for (int h = 0; h < kMaxRep; ++h) s[h] = 0.f;
+    for (int h = 0; h < RR; ++h) s[h] = 0.f;
     for (int i = lane; i < half; i += 32) {
       const float k1 = to_f(krow[i]), k2 = to_f(krow[i + half]);
       const float c1 = cr[i], s1 = sr[i];
@@ -214,12 +219,12 @@ __global__ void __launch_bounds__(256) hot_merge_kernel(DecodeParams p) {
       const float kp1 = k1 * c1 - k2 * s1;   // apply_rope: x1*cos1 - x2*sin1
       const float kp2 = k2 * c2 + k1 * s2;   //             x2*cos2 + x1*sin2
 #pragma unroll
-      for (int h = 0; h < kMaxRep; ++h)
-        if (h < nrep) s[h] = fmaf(sq[h * D + i], kp1, fmaf(sq[h * D + i + half], kp2, s[h]));
+      for (int h = 0; h < RR; ++h)
+        if (NREP > 0 || h < nrep) s[h] = fmaf(sq[h * D + i], kp1, fmaf(sq[h * D + i + half], kp2, s[h]));
     }
 #pragma unroll
-    for (int h = 0; h < kMaxRep; ++h) {
-      if (h < nrep) {
+    for (int h = 0; h < RR; ++h) {
+      if (NREP > 0 || h < nrep) {
         float v = warp_sum(s[h]) * p.scale;
         if (p.mask && p.mask[((int64_t)b * p.Hq + g * nrep + h) * p.mask_stride + (int64_t)nb * p.Tb + t] == 0)
           v = -INFINITY;
@@ -267,19 +272,19 @@ __global__ void __launch_bounds__(256) hot_merge_kernel(DecodeParams p) {
     const int slices = blockDim.x / D;
     const int sl = tid / D, d = tid - sl * D;
     if (sl < slices) {
-      float acc[kMaxRep];
+      float acc[RR];
 #pragma unroll
-      for (int h = 0; h < kMaxRep; ++h) acc[h] = 0.f;
+      for (int h = 0; h < RR; ++h) acc[h] = 0.f;
 #pragma unroll 4
       for (int t = sl; t < hot; t += slices) {
         const float v = to_f(hv[(int64_t)t * D + d]);
 #pragma unroll
-        for (int h = 0; h < kMaxRep; ++h)
-          if (h < nrep) acc[h] = fmaf(ssc[h * hot + t], v, acc[h]);
+        for (int h = 0; h < RR; ++h)
+          if (NREP > 0 || h < nrep) acc[h] = fmaf(ssc[h * hot + t], v, acc[h]);
       }
 #pragma unroll
-      for (int h = 0; h < kMaxRep; ++h)
-        if (h < nrep) sred[(sl * nrep + h) * D + d] = acc[h];
+      for (int h = 0; h < RR; ++h)
+        if (NREP > 0 || h < nrep) sred[(sl * nrep + h) * D + d] = acc[h];
     }
   }
   __syncthreads();
@@ -327,13 +332,25 @@ static int launch_hot_merge(const DecodeParams& p, cudaStream_t st) {
                          reinterpret_cast<uintptr_t>(p.ws)) & 15u) == 0 &&
                        ((size_t)p.HC * p.D * sizeof(T)) % 16 == 0 && ((size_t)p.hot * p.D * sizeof(T)) % 16 == 0;
   dim3 grid(p.H, p.L * p.B);
-  if (aligned && smem + stage <= 64 * 1024) {
-    cudaFuncSetAttribute(hot_merge_kernel<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(smem + stage));
-    hot_merge_kernel<T, true><<<grid, 256, smem + stage, st>>>(p);
-  } else {
-    cudaFuncSetAttribute(hot_merge_kernel<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    hot_merge_kernel<T, false><<<grid, 256, smem, st>>>(p);
-  }
+  auto go = [&](auto stage_tag, auto nrep_tag) {
+    constexpr bool S = decltype(stage_tag)::value;
+    constexpr int R = decltype(nrep_tag)::value;
+    const size_t bytes = S ? smem + stage : smem;
+    cudaFuncSetAttribute(hot_merge_kernel<T, S, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    hot_merge_kernel<T, S, R><<<grid, 256, bytes, st>>>(p);
+  };
+  auto by_nrep = [&](auto stage_tag) {
+    switch (p.nrep) {
+      case 1: go(stage_tag, std::integral_constant<int, 1>()); break;
+      case 2: go(stage_tag, std::integral_constant<int, 2>()); break;
+      case 4: go(stage_tag, std::integral_constant<int, 4>()); break;
+      case 8: go(stage_tag, std::integral_constant<int, 8>()); break;
+      case 16: go(stage_tag, std::integral_constant<int, 16>()); break;
+      default: go(stage_tag, std::integral_constant<int, 0>()); break;
+    }
+  };
+  if (aligned && smem + stage <= 64 * 1024) by_nrep(std::true_type());
+  else by_nrep(std::false_type());
   return launch_status("hot_merge_kernel");
 }
 
