@@ -458,6 +458,41 @@ def test_cache_compression_codes_bit_exact_and_error_parity():
     assert cache.hot_position_ids.cpu().tolist() == [[512, 513, 514, 515, 516]]
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_cache_prompt_compression_batched_equals_blockwise(dtype):
+    """A prompt that fills several blocks is compressed with one rSVD launch for the keys
+    and one for the values; with the same seed it must give exactly the cold tier (codes,
+    scales, min/max, bases, block positions) and hot tier that appending the prompt one
+    block at a time gives (the per-block path, two launches per block)."""
+    from unsloth_spectral import SpectralCache
+    from unsloth_spectral import synthetic as syn
+    B, H, D, T, nfull, extra = 2, 4, 128, 512, 4, 100
+    K, V = syn.kv_per_head(3, 0, B, H, nfull * T + extra, D, 24, 0.85)
+    K, V = K.to(dtype).cuda(), V.to(dtype).cuda()
+
+    def build(chunks):
+        cache = SpectralCache(H, D, block_size=T, k_rank_keys=16, k_rank_values=32, device="cuda",
+                              dtype=dtype, oversampling=8)
+        torch.manual_seed(19)
+        for c0, c1 in chunks:
+            cache.append(K[:, :, c0:c1], V[:, :, c0:c1])
+        return cache
+
+    whole = build([(0, nfull * T + extra)])
+    steps = [(c0, min(c0 + T, nfull * T + extra)) for c0 in range(0, nfull * T + extra, T)]
+    blockwise = build(steps)
+    assert whole.num_cold_blocks == blockwise.num_cold_blocks == nfull
+    assert whole.compression_count == blockwise.compression_count == nfull
+    a, b = whole.tiers, blockwise.tiers
+    for name in ("codes_k", "codes_v", "scale_k", "scale_v", "minmax_k", "minmax_v", "basis_k", "basis_v"):
+        x, y = getattr(a, name)[:, :, :nfull], getattr(b, name)[:, :, :nfull]
+        assert torch.equal(x, y), name
+    assert torch.equal(a.block_pos[:nfull], b.block_pos[:nfull])
+    assert a.block_pos[:nfull].tolist() == [i * T for i in range(nfull)]
+    assert torch.equal(whole.hot_K, blockwise.hot_K) and torch.equal(whole.hot_V, blockwise.hot_V)
+    assert torch.equal(whole.hot_position_ids, blockwise.hot_position_ids)
+
+
 # ------------------------------------------------- fast cold-tier kernel vs generic
 FAST_CASES = [
     # seed, B, H, nrep, D, T, nblk, kK, kV, hot, masked   (FP16, D=128, tied, no mask)

@@ -236,13 +236,15 @@ class SpectralCache:
         if nfull == 0:
             return
         t.ensure_blocks(t.num_blocks + nfull)
-        for i in range(nfull):
-            j = t.num_blocks
-            self._compress_into(t.hot_k, i * T, j, keys=True)
-            self._compress_into(t.hot_v, i * T, j, keys=False)
-            t.block_pos[j] = t.hot_pos[i * T]
-            t.num_blocks += 1
-            self.compression_count += 1
+        j0 = t.num_blocks
+        if nfull == 1:
+            self._compress_into(t.hot_k, 0, j0, keys=True)
+            self._compress_into(t.hot_v, 0, j0, keys=False)
+        else:
+            self._compress_blocks(nfull, j0)
+        t.block_pos[j0:j0 + nfull] = t.hot_pos[0:nfull * T:T]
+        t.num_blocks += nfull
+        self.compression_count += nfull
         rem = t.hot_len - nfull * T
         if rem:
             t.hot_k[:, :, :rem] = t.hot_k[:, :, nfull * T:nfull * T + rem].clone()
@@ -277,6 +279,63 @@ class SpectralCache:
                   qminmax=mm[:, :, j], minmax_stride=2 * t.block_capacity,
                   basis=basis[:, :, j], basis_stride=t.block_capacity * kp * D,
                   M_mat_stride=HC * D, num_mats=nm, m=T, n=D, codes_tiled=not keys)
+
+    def _compress_blocks(self, nfull: int, j0: int):
+        """Compress the first ``nfull`` blocks of the hot tier (a long prompt) with one
+        rSVD launch for the keys and one for the values, instead of two per block.  The
+        sketches are drawn first, in the order of the per-block path (K then V of each
+        block, as the reference draws them), and every matrix is computed independently
+        of the others in its launch, so the cold tier comes out bit-identical to
+        compressing block by block.  The blocks are staged contiguously (one copy of the
+        prompt's K and V) and the outputs go to contiguous buffers that are then copied
+        into block slots ``j0 .. j0 + nfull - 1``."""
+        t = self.tiers
+        B, H, HC, D = t.hot_k.shape
+        T = self.block_size
+        nm = B * H
+        dev = t.hot_k.device
+        spec = []
+        for keys in (True, False):
+            k = self.k_rank_keys if keys else self.k_rank_values
+            r = min(k + self.oversampling, min(T, D))
+            if r >= min(T, D) - 1:
+                raise ValueError(f"rank {k} + oversampling {self.oversampling} too large for {T}x{D} blocks")
+            spec.append((keys, k, r))
+        omegas = {True: [], False: []}
+        for _ in range(nfull):
+            for keys, _k, r in spec:
+                # drawn as rsvd.py:95 does: float32 randn of [mats, n, r] from the global RNG
+                omegas[keys].append(torch.randn(nm, D, r, device=dev, dtype=torch.float32))
+        for keys, k, r in spec:
+            hot = t.hot_k if keys else t.hot_v
+            X = hot[:, :, :nfull * T].reshape(B, H, nfull, T, D).permute(2, 0, 1, 3, 4).contiguous()
+            omega = torch.cat(omegas[keys], dim=0)   # matrices ordered (block, sequence, head)
+            kp = t.rank_k_pad if keys else t.rank_v_pad
+            if keys:
+                codes = torch.empty(nfull, B, H, T, kp, dtype=torch.int8, device=dev)
+                cstr = (T * kp, kp, 1)                 # token-major
+            else:
+                codes = torch.empty(nfull, B, H, kp * T, dtype=torch.int8, device=dev)
+                cstr = (kp * T, 0, 0)                  # value-tile layout
+            scale = torch.empty(nfull, B, H, dtype=torch.float32, device=dev)
+            mm = torch.empty(nfull, B, H, 2, dtype=torch.float32, device=dev)
+            basis = torch.empty(nfull, B, H, kp, D, dtype=t.dtype, device=dev)
+            _ops.rsvd(X, omega, k, self.n_iter, want_factors=False,
+                      codes=codes, codes_strides=cstr, rank_pad=kp,
+                      qscale=scale, scale_stride=1, qminmax=mm, minmax_stride=2,
+                      basis=basis, basis_stride=kp * D,
+                      M_mat_stride=T * D, num_mats=nfull * nm, m=T, n=D, codes_tiled=not keys)
+            dst = slice(j0, j0 + nfull)
+            if keys:
+                t.codes_k[:, :, dst] = codes.permute(1, 2, 0, 3, 4)
+                t.scale_k[:, :, dst] = scale.permute(1, 2, 0)
+                t.minmax_k[:, :, dst] = mm.permute(1, 2, 0, 3)
+                t.basis_k[:, :, dst] = basis.permute(1, 2, 0, 3, 4)
+            else:
+                t.codes_v[:, :, dst] = codes.permute(1, 2, 0, 3)
+                t.scale_v[:, :, dst] = scale.permute(1, 2, 0)
+                t.minmax_v[:, :, dst] = mm.permute(1, 2, 0, 3)
+                t.basis_v[:, :, dst] = basis.permute(1, 2, 0, 3, 4)
 
     # -- reference-layout views -------------------------------------------------------
     @property
