@@ -493,6 +493,33 @@ def test_cache_prompt_compression_batched_equals_blockwise(dtype):
     assert torch.equal(whole.hot_position_ids, blockwise.hot_position_ids)
 
 
+def test_cache_state_dict_decodes_identically():
+    """A compressed cache saved with state_dict (torch.save / torch.load) and loaded into
+    a fresh cache decodes to exactly the same output."""
+    import io
+    from unsloth_spectral import SpectralCache, spectral_attention_forward
+    from unsloth_spectral import synthetic as syn
+    B, H, nrep, D, T = 2, 4, 4, 128, 512
+    K, V = syn.kv_per_head(4, 0, B, H, 2 * T + 70, D, 24, 0.85)
+    cache = SpectralCache(H, D, block_size=T, k_rank_keys=16, k_rank_values=32, device="cuda",
+                          dtype=torch.float16, oversampling=8)
+    torch.manual_seed(23)
+    cache.append(K.half().cuda(), V.half().cuda())
+    buf = io.BytesIO()
+    torch.save(cache.state_dict(), buf)
+    buf.seek(0)
+    other = SpectralCache(H, D, block_size=T, k_rank_keys=16, k_rank_values=32, device="cuda",
+                          dtype=torch.float16, oversampling=8)
+    other.load_state_dict(torch.load(buf))
+    qpos = 2 * T + 70
+    cos, sin = syn.rope_tables(qpos + 8, D, 1e6, device=torch.device("cuda"))
+    Q = (torch.randn(B, H * nrep, 1, D, generator=torch.Generator().manual_seed(2)) / math.sqrt(D)).half().cuda()
+    a = spectral_attention_forward(Q, cache, cos, sin, qpos)
+    b = spectral_attention_forward(Q, other, cos, sin, qpos)
+    assert torch.isfinite(a).all()
+    assert torch.equal(a, b)
+
+
 # ------------------------------------------------- fast cold-tier kernel vs generic
 FAST_CASES = [
     # seed, B, H, nrep, D, T, nblk, kK, kV, hot, masked   (FP16, D=128, tied, no mask)

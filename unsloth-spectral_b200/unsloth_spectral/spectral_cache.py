@@ -192,6 +192,63 @@ class SpectralCache:
         self.compression_count = 0
         self._blocks_view = None
 
+    # -- serialisation -----------------------------------------------------------------
+    _COLD = ("codes_k", "codes_v", "scale_k", "scale_v", "minmax_k", "minmax_v", "basis_k", "basis_v")
+    _GEOMETRY = ("num_heads", "head_dim", "block_size", "k_rank_keys", "k_rank_values")
+
+    def state_dict(self) -> dict:
+        """The cache's contents as tensors and numbers, for checkpointing a compressed
+        cache (e.g. with ``torch.save``): the used part of every tier - INT8 codes (value
+        codes in their stored tile layout), scales, min/max, bases and start positions of
+        the cold blocks, the hot tier's K, V and positions - plus the geometry and the
+        counters.  The tensors are copies on the cache's device.  The reference keeps its
+        cache in memory only (spectral_cache.py:49-705 has no serialisation)."""
+        sd = {name: getattr(self, name) for name in self._GEOMETRY}
+        sd.update(version=1, dtype=str(self.dtype), oversampling=self.oversampling, n_iter=self.n_iter,
+                  current_position=self.current_position, total_tokens=self.total_tokens,
+                  compression_count=self.compression_count, batch=0)
+        t = self.tiers
+        if t is not None:
+            n, h = t.num_blocks, t.hot_len
+            sd["batch"] = t.batch
+            for name in self._COLD:
+                sd[name] = getattr(t, name)[:, :, :n].clone()
+            sd["block_pos"] = t.block_pos[:n].clone()
+            sd["hot_k"] = t.hot_k[:, :, :h].clone()
+            sd["hot_v"] = t.hot_v[:, :, :h].clone()
+            sd["hot_pos"] = t.hot_pos[:h].clone()
+        return sd
+
+    def load_state_dict(self, sd: dict):
+        """Restore what ``state_dict`` returned.  The geometry (heads, head dim, block size,
+        ranks) and dtype must match this cache's (ValueError otherwise); the tensors are
+        copied to the cache's device, replacing its contents."""
+        for name in self._GEOMETRY:
+            if sd[name] != getattr(self, name):
+                raise ValueError(f"state has {name}={sd[name]}, cache has {getattr(self, name)}")
+        if sd["dtype"] != str(self.dtype):
+            raise ValueError(f"state has dtype {sd['dtype']}, cache has {self.dtype}")
+        self.reset()
+        if self.tiers is not None and self.tiers.batch != sd["batch"]:
+            self.tiers = None
+        if sd["batch"]:
+            t = self._tiers_for(sd["batch"], self.device)
+            n, h = sd["block_pos"].shape[0], sd["hot_pos"].shape[0]
+            t.ensure_blocks(n)
+            for name in self._COLD:
+                getattr(t, name)[:, :, :n].copy_(sd[name])
+            t.block_pos[:n].copy_(sd["block_pos"])
+            t.num_blocks = n
+            t.ensure_hot(h)
+            t.hot_k[:, :, :h].copy_(sd["hot_k"])
+            t.hot_v[:, :, :h].copy_(sd["hot_v"])
+            t.hot_pos[:h].copy_(sd["hot_pos"])
+            t.hot_len = h
+        self.oversampling, self.n_iter = sd["oversampling"], sd["n_iter"]
+        self.current_position, self.total_tokens = sd["current_position"], sd["total_tokens"]
+        self.compression_count = sd["compression_count"]
+        self._blocks_view = None
+
     # -- append / compression ------------------------------------------------------
     def append(self, K_new: torch.Tensor, V_new: torch.Tensor, position_ids: Optional[torch.Tensor] = None):
         """Append pre-RoPE ``K_new``/``V_new`` ``[B, H, T_new, D]`` (spectral_cache.py:164-241).
