@@ -11,17 +11,24 @@ step exceeds the 126 MB L2, so no flush is needed between steps.
 
 Reported: decode tokens/s (value: inputs resident; e2e: through the C ABI with the
 queries copied from pinned host memory and the outputs copied back every step), the
-roofline of the decode launch against measured HBM bandwidth, rSVD blocks/s on
-config 3's largest batch (4096 blocks of 512x128 FP16, k=32, 2 power iterations), and
-the CPU oracle port timed on a bounded sample.
+roofline of the decode launch against measured HBM bandwidth, a parity block (sampled
+(layer, sequence, KV head) units of the timed configuration checked against the CPU
+oracle, cos >= 0.9999 and max-abs <= 1e-2, the run exits non-zero otherwise), rSVD
+blocks/s on config 3's largest batch (4096 blocks of 512x128 FP16, k=32, 2 power
+iterations) with its mean reconstruction error, and the reference's own CPU code
+(installed under baseline/_ref) timed on a bounded sample as the CPU baseline.
 
-Multi-GPU (torchrun): KV heads are sharded across ranks; each rank decodes its head
-slice of every layer and one NCCL all-gather per step assembles the outputs.
+Reference arm (--impl reference): the reference package's own PyTorch CPU functions,
+`kernels.spectral_attention_decode` (one (sequence, layer) decode of the workload per
+step, extrapolated to a full step) and `rsvd.batched_randomized_svd`, on all host cores.
+
+Multi-GPU (torchrun): KV heads are sharded across ranks (unsloth_spectral.sharding);
+each rank decodes its head slice of every layer and one NCCL all-gather per step
+assembles the outputs.
 """
 from __future__ import annotations
 
 import argparse
-import ctypes as C
 import json
 import math
 import os
@@ -32,16 +39,24 @@ import threading
 import time
 
 REPO = os.path.dirname(os.path.abspath(__file__))
-sys.path.insert(0, os.path.join(REPO, "unsloth-spectral_b200"))
+PKG_ROOT = os.path.join(REPO, "unsloth-spectral_b200")
+REF_ROOT = os.path.join(REPO, "baseline", "_ref")
 os.environ.setdefault("UNSLOTH_SPECTRAL_QUIET", "1")
 
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 CFG = dict(layers=32, batch=32, q_heads=32, kv_heads=8, head_dim=128, block=512, blocks=64, rank=32, hot=64,
-           gen_rank=48, rho=0.9, oversampling=8, n_iter=2)
+           gen_rank=48, rho=0.9, oversampling=8, n_iter=2, theta=1e6)
 METRIC = "spectral decode-attn tokens/s & HBM GB/s at 32K ctx; rSVD blocks/s"
 UNIT = "tokens/s"
+WORKLOAD = "config2: 32 layers x B32 x 32/8 heads x 32K ctx (64x512 blocks, k=32) + 64 hot"
+PARITY_COS, PARITY_MAXABS = 0.9999, 1e-2
+
+
+def _use_ours():
+    if PKG_ROOT not in sys.path:
+        sys.path.insert(0, PKG_ROOT)
 
 
 def algorithmic_bytes_per_step(c, kv_heads_local):
@@ -54,24 +69,35 @@ def algorithmic_bytes_per_step(c, kv_heads_local):
     return per_head * c["layers"] * c["batch"] * kv_heads_local
 
 
-def measured_traffic():
-    """Per-launch DRAM bytes of the decode call from the committed ncu summary, if any."""
-    p = os.path.join(REPO, "profiles", "decode_cold_fast_config2.md")
+def measured_traffic(c, world):
+    """DRAM bytes per decode launch from the committed ncu launch-list summary
+    (profiles/decode_traffic.json), when it was taken on this exact workload."""
+    p = os.path.join(REPO, "profiles", "decode_traffic.json")
     try:
-        for line in open(p):
-            if line.startswith("traffic_bytes_per_launch:"):
-                return int(line.split(":")[1])
-    except OSError:
-        pass
-    return None
+        d = json.load(open(p))
+    except (OSError, ValueError):
+        return None, None
+    if d.get("workload") != WORKLOAD or world != 1 or c["layers"] != CFG["layers"]:
+        return None, None
+    return d.get("dram_bytes_per_launch"), d.get("command")
 
 
 def read_peaks():
     p = os.path.join(REPO, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         d = json.load(open(p))
-        return float(d["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+        return float(d["hbm_gbs"]), float(d.get("bf16_tflops", 1590.0)), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 class ClockSampler:
@@ -127,15 +153,192 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-# --------------------------------------------------------------------------- setup
+# =============================================================================
+# Reference arm: the reference package's own CPU code (baseline/_ref)
+# =============================================================================
+_REF_MODS = {}
+
+
+def _import_reference():
+    """Import the unmodified reference package from baseline/_ref (its own import name,
+    so this process must not have imported this repository's package)."""
+    if _REF_MODS:
+        return _REF_MODS
+    if "unsloth_spectral" in sys.modules:
+        raise RuntimeError("the reference arm must run in a process without this repository's package")
+    if not os.path.isdir(os.path.join(REF_ROOT, "unsloth_spectral")):
+        return None
+    sys.path.insert(0, REF_ROOT)
+    import importlib
+    import logging
+    logging.disable(logging.CRITICAL)
+    _REF_MODS.update({n: importlib.import_module(f"unsloth_spectral.{n}")
+                      for n in ("spectral_cache", "rsvd", "kernels.spectral_attention")})
+    return _REF_MODS
+
+
+def _reference_cache(sc, c, seed):
+    """A float32 CPU SpectralCache of one (sequence, layer) of the workload: 64 cold
+    blocks of 512 tokens at k=32 (INT8-valued coefficients times a per-head scale, as
+    the reference stores them) and 64 hot tokens, for 8 KV heads of D=128."""
+    g = torch.Generator().manual_seed(seed)
+    H, D, T, NB, R, hot = c["kv_heads"], c["head_dim"], c["block"], c["blocks"], c["rank"], c["hot"]
+    cache = sc.SpectralCache(num_heads=H, head_dim=D, block_size=T, k_rank_keys=R, k_rank_values=R,
+                             device="cpu", dtype=torch.float32)
+    blocks = []
+    for j in range(NB):
+        parts = []
+        for _ in range(2):
+            codes = torch.randint(-127, 128, (H, T, R), generator=g).float()
+            s = torch.rand(H, generator=g) * 0.01 + 0.01
+            coeffs = codes * s[:, None, None]
+            mm = torch.stack([coeffs.amin(dim=(1, 2)), coeffs.amax(dim=(1, 2))], dim=1)
+            basis = torch.linalg.qr(torch.randn(H, D, R, generator=g))[0].transpose(1, 2).contiguous()
+            parts.append((coeffs, basis, mm))
+        (ck, bk, mk), (cv, bv, mv) = parts
+        blocks.append(sc.SpectralBlock(coeffs_K=ck, basis_K=bk, coeffs_V=cv, basis_V=bv, scales_K=mk, scales_V=mv,
+                                       block_size=T, start_position=j * T))
+    cache.cold_blocks = blocks
+    cache.hot_K = torch.randn(1, H, hot, D, generator=g)
+    cache.hot_V = torch.randn(1, H, hot, D, generator=g)
+    cache.hot_position_ids = torch.arange(NB * T, NB * T + hot).unsqueeze(0)
+    cache.total_tokens = NB * T + hot
+    cache.current_position = NB * T + hot
+    return cache
+
+
+def _rope_tables(n, D, theta):
+    inv = theta ** (-2.0 * torch.arange(0, D, 2, dtype=torch.float64) / D)
+    fr = torch.outer(torch.arange(n, dtype=torch.float64), inv)
+    emb = torch.cat([fr, fr], dim=-1)
+    return emb.cos().float(), emb.sin().float()
+
+
+def reference_decode_sampler(c, seed=0):
+    """Returns (call, threads, kind): ``call()`` runs one (sequence, layer) decode of the
+    workload on the host cores through the reference's own
+    kernels.spectral_attention_decode (kernels/spectral_attention.py:684), or through
+    the numpy oracle port when the reference is not installed."""
+    ncores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(ncores)
+    mods = _import_reference()
+    D, Hq = c["head_dim"], c["q_heads"]
+    qpos = c["blocks"] * c["block"] + c["hot"]
+    cos, sin = _rope_tables(qpos + 8, D, c["theta"])
+    g = torch.Generator().manual_seed(seed + 1)
+    Q = torch.randn(1, Hq, 1, D, generator=g) / math.sqrt(D)
+    if mods is not None:
+        ka = mods["kernels.spectral_attention"]
+        cache = _reference_cache(mods["spectral_cache"], c, seed)
+        cfg = ka.TritonSpectralConfig(enable_logging=False)
+
+        def call():
+            return ka.spectral_attention_decode(Q, cache, cos, sin, qpos, scale=1.0 / math.sqrt(D), config=cfg)
+        return call, ncores, "reference"
+    sys.path.insert(0, REPO)
+    from oracle import spectral_oracle as so
+    rng = np.random.default_rng(seed)
+    H, T, NB, R, hot = c["kv_heads"], c["block"], c["blocks"], c["rank"], c["hot"]
+    basis = np.linalg.qr(rng.standard_normal((H, D, R)))[0].transpose(0, 2, 1).astype(np.float32)
+    blocks = [so.Block(rng.integers(-127, 128, size=(H, T, R)).astype(np.float32) * np.float32(0.01), basis,
+                       rng.integers(-127, 128, size=(H, T, R)).astype(np.float32) * np.float32(0.01), basis, j * T)
+              for j in range(NB)]
+    hk = rng.standard_normal((1, H, hot, D)).astype(np.float32)
+    hv = rng.standard_normal((1, H, hot, D)).astype(np.float32)
+    hp = np.arange(NB * T, NB * T + hot)
+    Qn, cn, sn = Q.numpy(), cos.numpy(), sin.numpy()
+
+    def call():
+        return so.spectral_attention_decode(Qn, blocks, hk, hv, hp, cn, sn, qpos)
+    return call, ncores, "port"
+
+
+def reference_rsvd_sample(c, nblocks=64, seed=3):
+    """Time the reference's batched_randomized_svd (rsvd.py:28) on ``nblocks`` config-3
+    blocks (512 x 128, rank-48 generator, k=32, q=2, p=8) on the host cores; returns
+    (blocks/s, mean relative reconstruction error, threads) or None without the
+    reference."""
+    mods = _import_reference()
+    if mods is None:
+        return None
+    rs = mods["rsvd"]
+    torch.set_num_threads(len(os.sched_getaffinity(0)))
+    g = torch.Generator().manual_seed(seed)
+    M = (torch.randn(nblocks, 512, 48, generator=g) * (0.9 ** torch.arange(48))) @ torch.randn(nblocks, 48, 128,
+                                                                                              generator=g)
+    M = (M + 0.05 * torch.randn(nblocks, 512, 128, generator=g)).half().float()
+    rs.batched_randomized_svd(M[:8], 32, n_iter=2, oversampling=8)   # warm
+    t0 = time.perf_counter()
+    U, S, Vh = rs.batched_randomized_svd(M, 32, n_iter=2, oversampling=8)
+    dt = time.perf_counter() - t0
+    err = (torch.linalg.norm(M - (U * S[:, None, :]) @ Vh, dim=(1, 2)) / torch.linalg.norm(M, dim=(1, 2)))
+    return nblocks / dt, float(err.mean()), len(os.sched_getaffinity(0))
+
+
+def tokens_per_s_from_call(c, per_call_s):
+    """One step = batch tokens, each needing `layers` (sequence, layer) decodes."""
+    return c["batch"] / (per_call_s * c["batch"] * c["layers"])
+
+
+def run_reference(args, c):
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    call, thr, kind = reference_decode_sampler(c)
+    per = []
+    for s in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        call()
+        if s >= args.warmup:
+            per.append(time.perf_counter() - t0)
+    mean = sum(per) / len(per)
+    v = tokens_per_s_from_call(c, mean)
+    what = ("the reference's kernels.spectral_attention_decode (baseline/_ref, float32 PyTorch CPU path)"
+            if kind == "reference" else "the numpy restatement of the reference (reference not installed)")
+    sample = (f"each step: one (sequence, layer) decode of the workload (64 blocks x 512 at k=32 + 64 hot, "
+              f"32/8 heads, D=128) by {what}; tokens/s = batch / (per-call time x batch x layers)")
+    rs = reference_rsvd_sample(c) if not args.no_rsvd else None
+    line = {"metric": METRIC, "value": v, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean * c["batch"] * c["layers"] * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": WORKLOAD},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": thr, "kind": kind, "sample": sample,
+                             "cpu_model": cpu_model(), "seconds_per_call": mean},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if rs is not None:
+        line["rsvd"] = {"blocks_per_s": rs[0], "mean_rel_error": rs[1], "cores": rs[2], "blocks": 64, "k": 32,
+                        "n_iter": 2, "oversampling": 8,
+                        "sample": "64 of config 3's 512x128 blocks through the reference's batched_randomized_svd"}
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline_subprocess(steps=4, warmup=1, timeout=600):
+    """Run the reference arm in a fresh process (the reference shares this repository
+    package's import name) and return its JSON line."""
+    cmd = [sys.executable, os.path.abspath(__file__), "--impl", "reference", "--steps", str(steps), "--warmup",
+           str(warmup)]
+    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK")}
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout, env=env)
+        for ln in reversed(r.stdout.strip().splitlines()):
+            if ln.startswith("{"):
+                return json.loads(ln)
+    except (subprocess.TimeoutExpired, ValueError):
+        pass
+    return None
+
+
+# =============================================================================
+# Our arm
+# =============================================================================
 def build_tiers(c, rank_id, world, dev):
     """Device tiers of this rank's KV-head slice for all layers, built by the library's
     rSVD + INT8 compression of seeded synthetic K/V.  Returns (tiers dict, rsvd seconds)."""
     from unsloth_spectral import _ops, synthetic as syn
+    from unsloth_spectral.sharding import head_slice
     L, B, H, D, T, NB, R, hot = (c["layers"], c["batch"], c["kv_heads"], c["head_dim"], c["block"], c["blocks"],
                                  c["rank"], c["hot"])
-    Hl = H // world
-    h0 = rank_id * Hl
+    h0, h1 = head_slice(H, world, rank_id)
+    Hl = h1 - h0
     t = dict(
         codes_k=torch.empty(L, B, Hl, NB, T, R, dtype=torch.int8, device=dev),
         codes_v=torch.empty(L, B, Hl, NB, R * T, dtype=torch.int8, device=dev),   # value-tile layout
@@ -154,7 +357,7 @@ def build_tiers(c, rank_id, world, dev):
     for l in range(L):
         K, V = syn.kv_layer_batched(2, l, B, H, NB * T + hot, D, c["gen_rank"], c["rho"], dev)
         for X, name in ((K, "k"), (V, "v")):
-            Xl = X[:, h0:h0 + Hl].contiguous()
+            Xl = X[:, h0:h1].contiguous()
             t[f"hot_{name}"][l].copy_(Xl[:, :, NB * T:])
             cold = Xl[:, :, :NB * T]
             g = torch.Generator(device=dev).manual_seed(10_000 + 2 * l + (name == "v"))
@@ -172,10 +375,13 @@ def build_tiers(c, rank_id, world, dev):
     return t, rs
 
 
-def make_queries(c, steps, Hq_l, rank_id, cos, sin):
+def make_queries(c, steps, rank_id, world, cos, sin):
     """[steps][L, B, Hq_local, D] fp16 RoPE'd queries (CPU, float32 generation)."""
     from unsloth_spectral import synthetic as syn
+    from unsloth_spectral.sharding import head_slice
     L, B, Hq, D = c["layers"], c["batch"], c["q_heads"], c["head_dim"]
+    nrep = Hq // c["kv_heads"]
+    h0, h1 = head_slice(c["kv_heads"], world, rank_id)
     qpos = c["blocks"] * c["block"] + c["hot"]
     out = []
     for s in range(steps):
@@ -183,7 +389,7 @@ def make_queries(c, steps, Hq_l, rank_id, cos, sin):
         for l in range(L):
             q = syn.query(2, s * L + l, B, Hq, D)[:, :, 0]
             q = syn.rope_rotate(q, cos[qpos].cpu(), sin[qpos].cpu())
-            qs.append(q[:, rank_id * Hq_l:(rank_id + 1) * Hq_l])
+            qs.append(q[:, h0 * nrep:h1 * nrep])
         out.append(torch.stack(qs).to(torch.float16))
     return out, qpos
 
@@ -204,77 +410,71 @@ def decode_args(c, t, q, out, cos, sin, qpos, ws, Hl):
         workspace=ws.data_ptr() if ws is not None else None, workspace_bytes=ws.numel() if ws is not None else 0)
 
 
-# -------------------------------------------------------------------- CPU baseline
-def cpu_sample_decode(c, n_calls, seed=0):
-    """Time the CPU oracle port on ``n_calls`` (sequence, layer) decodes of the
-    workload's shape with every host core this process may use; returns (seconds per
-    call, threads)."""
+def parity_units(c, Hl, G=32, extra=4, seed=11):
+    """(layer, sequence, local KV head) units to check: the first, middle and last
+    units, both sides of the boundaries between the cold kernel's work items (items of
+    G consecutive units), the last layer, plus a few seeded random ones."""
+    L, B = c["layers"], c["batch"]
+    n = L * B * Hl
+    idx = {0, n // 2, n - 1, min(G - 1, n - 1), min(G, n - 1), min(2 * G - 1, n - 1), (L - 1) * B * Hl}
+    rng = np.random.default_rng(seed)
+    idx.update(int(x) for x in rng.integers(0, n, size=extra))
+    out = []
+    for u in sorted(idx):
+        h = u % Hl
+        b = (u // Hl) % B
+        l = u // (Hl * B)
+        out.append((l, b, h))
+    return out
+
+
+def parity_check(c, t, q_dev, out_dev, cos, sin, qpos, Hl, units):
+    """Compare the decode output of ``units`` with the float32 CPU oracle over the same
+    compressed cache (codes * scale, FP16 bases, FP16 hot tier, FP16 queries)."""
     sys.path.insert(0, REPO)
     from oracle import spectral_oracle as so
-    from threadpoolctl import threadpool_limits
-    ncores = len(os.sched_getaffinity(0))
-    torch.set_num_threads(ncores)
-    with threadpool_limits(limits=ncores):
-        return _cpu_sample_decode(so, c, n_calls, seed), ncores
+    from unsloth_spectral import _ops
+    T, R, NB, D = c["block"], c["rank"], c["blocks"], c["head_dim"]
+    nrep = c["q_heads"] // c["kv_heads"]
+    vidx = _ops.vtile_index(T, R, "cpu")
+    cos_np, sin_np = cos.cpu().numpy(), sin.cpu().numpy()
+    hp = t["hot_pos"].cpu().numpy()
+    bpos = t["block_pos"].cpu().numpy()
+    worst_cos, worst_abs, rows = 1.0, 0.0, []
+    for (l, b, h) in units:
+        ck = t["codes_k"][l, b, h].cpu().float()                          # [NB, T, R]
+        sk = t["scale_k"][l, b, h].cpu()
+        stored = t["codes_v"][l, b, h].cpu()                              # [NB, R*T] value-tile layout
+        nat = torch.empty_like(stored)
+        nat[:, vidx] = stored
+        cv = nat.view(NB, R, T).transpose(1, 2).float()                   # [NB, T, R]
+        sv = t["scale_v"][l, b, h].cpu()
+        bk = t["basis_k"][l, b, h].cpu().float()
+        bv = t["basis_v"][l, b, h].cpu().float()
+        blocks = [so.Block((ck[j] * sk[j]).numpy()[None], bk[j].numpy()[None], (cv[j] * sv[j]).numpy()[None],
+                           bv[j].numpy()[None], int(bpos[j])) for j in range(NB)]
+        hk = t["hot_k"][l, b, h].cpu().float().numpy()[None, None]
+        hv = t["hot_v"][l, b, h].cpu().float().numpy()[None, None]
+        Q = q_dev[l, b, h * nrep:(h + 1) * nrep].cpu().float().numpy()[None, :, None, :]
+        ref = so.spectral_attention_decode(Q, blocks, hk, hv, hp, cos_np, sin_np, qpos,
+                                           scale=1.0 / math.sqrt(D)).reshape(-1)
+        got = out_dev[l, b, h * nrep:(h + 1) * nrep].cpu().float().numpy().reshape(-1)
+        cs = float(got @ ref / (np.linalg.norm(got) * np.linalg.norm(ref) + 1e-30))
+        ma = float(np.abs(got - ref).max())
+        worst_cos, worst_abs = min(worst_cos, cs), max(worst_abs, ma)
+        rows.append([l, b, h, round(cs, 7), ma])
+    ok = bool(worst_cos >= PARITY_COS and worst_abs <= PARITY_MAXABS)
+    return {"units": len(units), "cos_min": worst_cos, "max_abs": worst_abs, "passed": ok,
+            "tolerance": {"cos_min": PARITY_COS, "max_abs": PARITY_MAXABS},
+            "oracle": "oracle/spectral_oracle.py spectral_attention_decode (float32 numpy)",
+            "sampled": rows}
 
 
-def _cpu_sample_decode(so, c, n_calls, seed):
-    rng = np.random.default_rng(seed)
-    H, D, T, NB, R, hot, Hq = (c["kv_heads"], c["head_dim"], c["block"], c["blocks"], c["rank"], c["hot"],
-                               c["q_heads"])
-    basis = np.linalg.qr(rng.standard_normal((H, D, R)))[0].transpose(0, 2, 1).astype(np.float32)
-    blocks = []
-    for j in range(NB):
-        ck = rng.integers(-127, 128, size=(H, T, R)).astype(np.float32) * np.float32(0.01)
-        cv = rng.integers(-127, 128, size=(H, T, R)).astype(np.float32) * np.float32(0.01)
-        blocks.append(so.Block(ck, basis, cv, basis, j * T))
-    hk = rng.standard_normal((1, H, hot, D)).astype(np.float32)
-    hv = rng.standard_normal((1, H, hot, D)).astype(np.float32)
-    hp = np.arange(NB * T, NB * T + hot)
-    qpos = NB * T + hot
-    cos, sin = so.rope_tables(qpos + 8, D, 1e6)
-    Q = (rng.standard_normal((1, Hq, 1, D)) / math.sqrt(D)).astype(np.float32)
-    so.spectral_attention_decode(Q, blocks, hk, hv, hp, cos, sin, qpos)  # warm
-    t0 = time.perf_counter()
-    for _ in range(n_calls):
-        so.spectral_attention_decode(Q, blocks, hk, hv, hp, cos, sin, qpos)
-    return (time.perf_counter() - t0) / n_calls
-
-
-def cpu_tokens_per_s(c, per_call_s):
-    # one step = batch tokens, each needs layers (sequence, layer) decodes
-    return c["batch"] / (per_call_s * c["batch"] * c["layers"])
-
-
-def run_reference(args, c):
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
-        return
-    torch.set_num_threads(len(os.sched_getaffinity(0)))
-    per = []
-    for s in range(args.warmup + args.steps):
-        dt, thr = cpu_sample_decode(c, 1, seed=s)
-        if s >= args.warmup:
-            per.append(dt)
-    mean = sum(per) / len(per)
-    v = cpu_tokens_per_s(c, mean)
-    sample = (f"each step: one (sequence, layer) decode of the workload shape (64 blocks x 512 at k=32 + 64 hot, "
-              f"32/8 heads, D=128) by the float32 numpy port of the reference; tokens/s = batch / "
-              f"(per-call time x batch x layers)")
-    line = {"metric": METRIC, "value": v, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean * c["batch"] * c["layers"] * 1e3,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": "config2: 32 layers x B32 x 32/8 heads x 32K ctx (64x512 "
-                                                        "blocks, k=32) + 64 hot", "sample": "1 sequence-layer per step"},
-            "cpu_baseline": {"value": v, "unit": UNIT, "cores": thr, "kind": "port", "sample": sample},
-            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
-
-
-# ------------------------------------------------------------------------ GPU arm
 def run_ours(args, c):
+    _use_ours()
     from unsloth_spectral import _native as N, _ops
     from unsloth_spectral import synthetic as syn
+    from unsloth_spectral.sharding import HeadShardGather, head_slice
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -287,7 +487,8 @@ def run_ours(args, c):
         torch.distributed.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=600))
     if c["kv_heads"] % world:
         raise SystemExit("kv heads must divide across ranks")
-    Hl = c["kv_heads"] // world
+    h0, h1 = head_slice(c["kv_heads"], world, rank)
+    Hl = h1 - h0
     nrep = c["q_heads"] // c["kv_heads"]
     Hql = Hl * nrep
     lib = N.lib_for(dev)
@@ -296,23 +497,29 @@ def run_ours(args, c):
     t_setup = time.perf_counter()
     tiers, rsvd_setup_s = build_tiers(c, rank, world, dev)
     qpos = c["blocks"] * c["block"] + c["hot"]
-    cos, sin = syn.rope_tables(qpos + 16, D, 1e6, device=dev)
+    cos, sin = syn.rope_tables(qpos + 16, D, c["theta"], device=dev)
     nq = min(args.warmup + args.steps, 16)        # distinct seeded query sets, cycled
-    qs_host, _ = make_queries(c, nq, Hql, rank, cos, sin)
+    qs_host, _ = make_queries(c, nq, rank, world, cos, sin)
     qs_dev = [q.to(dev) for q in qs_host]
-    out = torch.empty(L, B, Hql, D, dtype=torch.float16, device=dev)
+    # two output buffers: the all-gather of step i (side stream) reads one while the
+    # decode of step i + 1 writes the other
+    outs = [torch.empty(L, B, Hql, D, dtype=torch.float16, device=dev) for _ in range(2)]
+    out = outs[0]
     a0 = decode_args(c, tiers, qs_dev[0], out, cos, sin, qpos, None, Hl)
     ws = torch.empty(lib.spx_decode_workspace_size(a0), dtype=torch.uint8, device=dev)
-    gathered = torch.empty(world, L, B, Hql, D, dtype=torch.float16, device=dev) if world > 1 else None
+    gather = HeadShardGather(out, world) if world > 1 else None
     stream = torch.cuda.current_stream(dev)
     sh = stream.cuda_stream
     setup_s = time.perf_counter() - t_setup
 
     def step(i, q_dev):
-        a = decode_args(c, tiers, q_dev, out, cos, sin, qpos, ws, Hl)
+        o = outs[i & 1]
+        if gather is not None:
+            gather.release(o)
+        a = decode_args(c, tiers, q_dev, o, cos, sin, qpos, ws, Hl)
         N.check(lib, lib.spx_decode_attn(a, sh), "spx_decode_attn")
-        if world > 1:
-            torch.distributed.all_gather_into_tensor(gathered, out)
+        if gather is not None:
+            gather.start(o)
 
     def barrier():
         if world > 1:
@@ -328,6 +535,8 @@ def run_ours(args, c):
         ev0.record(stream)
         for i in range(args.steps):
             step(i, qs_dev[(args.warmup + i) % nq])
+        if gather is not None:
+            gather.wait()
         ev1.record(stream)
         barrier()
     dev_ms = ev0.elapsed_time(ev1)
@@ -351,9 +560,10 @@ def run_ours(args, c):
         q_dev.copy_(pinned_in[i % nq], non_blocking=True)
         a = decode_args(c, tiers, q_dev, out, cos, sin, qpos, ws, Hl)
         N.check(lib, lib.spx_decode_attn(a, sh), "spx_decode_attn")
-        if world > 1:
-            torch.distributed.all_gather_into_tensor(gathered, out)
-            out_host.copy_(gathered.permute(1, 2, 0, 3, 4).reshape(L, B, world * Hql, D), non_blocking=True)
+        if gather is not None:
+            gather.start(out)
+            gather.wait()
+            out_host.copy_(gather.assembled(), non_blocking=True)
         else:
             out_host.copy_(out, non_blocking=True)
 
@@ -374,6 +584,33 @@ def run_ours(args, c):
         torch.distributed.all_reduce(times, op=torch.distributed.ReduceOp.MAX)
     dev_ms, kern_ms, e2e_ms = times.tolist()
 
+    # ---- parity of the timed configuration: one more call with query set 0, sampled
+    #      units checked against the CPU oracle (every rank checks its own head slice)
+    a = decode_args(c, tiers, qs_dev[0], out, cos, sin, qpos, ws, Hl)
+    N.check(lib, lib.spx_decode_attn(a, sh), "spx_decode_attn")
+    torch.cuda.synchronize(dev)
+    par = parity_check(c, tiers, qs_dev[0], out, cos, sin, qpos, Hl, parity_units(c, Hl))
+    # multi-GPU: the assembled output of the gathered head slices equals the local
+    # slices at their global head positions
+    gather_ok = None
+    if gather is not None:
+        gather.start(out)
+        gather.wait()
+        full = gather.assembled()
+        gather_ok = bool(torch.equal(full[:, :, h0 * nrep:h1 * nrep], out))
+    flags = torch.tensor([0.0 if par["passed"] else 1.0, 0.0 if gather_ok in (None, True) else 1.0,
+                          par["cos_min"], par["max_abs"]], dtype=torch.float64, device=dev)
+    if world > 1:
+        worst = flags.clone()
+        worst[2] = -worst[2]
+        torch.distributed.all_reduce(worst, op=torch.distributed.ReduceOp.MAX)
+        flags = worst
+        flags[2] = -flags[2]
+    par["passed"] = bool(flags[0].item() == 0.0)
+    par["cos_min"], par["max_abs"] = float(flags[2].item()), float(flags[3].item())
+    if gather is not None:
+        par["gather_equal"] = bool(flags[1].item() == 0.0)
+
     # ---- rSVD blocks/s, config 3's largest batch (4096 blocks, k=32, q=2, p=8)
     nb_rs = 4096 // world
     g = torch.Generator(device=dev).manual_seed(3)
@@ -382,7 +619,7 @@ def run_ours(args, c):
     Mrs = (Mrs + 0.05 * torch.randn(nb_rs, 512, 128, generator=g, device=dev)).half()
     om = torch.randn(nb_rs, 128, 40, generator=g, device=dev)
     for _ in range(2):
-        _ops.rsvd(Mrs, om, 32, 2, want_factors=True)
+        U, S, Vh = _ops.rsvd(Mrs, om, 32, 2, want_factors=True)
     barrier()
     ev6, ev7 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     reps = 3
@@ -395,47 +632,65 @@ def run_ours(args, c):
     if world > 1:
         torch.distributed.all_reduce(rs_ms, op=torch.distributed.ReduceOp.MAX)
     rs_ms = rs_ms.item()
+    Mf = Mrs.float()
+    rs_err = float((torch.linalg.norm(Mf - (U * S[:, None, :]) @ Vh, dim=(1, 2))
+                    / torch.linalg.norm(Mf, dim=(1, 2))).mean())
+    del Mf, Mrs, om, U, S, Vh
 
     if rank == 0:
         tokens = B * args.steps
         value = tokens / (dev_ms / 1e3)
         e2e = tokens / (e2e_ms / 1e3)
-        peak, peak_kind = read_peaks()
+        peak, _, peak_kind = read_peaks()
         bytes_launch = algorithmic_bytes_per_step(c, Hl)
         achieved = bytes_launch / (kern_ms / 1e3) / 1e9
-        cpu_per_call, cpu_thr = cpu_sample_decode(c, max(1, args.cpu_calls))
-        cpu_v = cpu_tokens_per_s(c, cpu_per_call)
+        traffic, traffic_cmd = measured_traffic(c, world)
+        cpu = None
+        if world == 1 and not args.no_cpu:
+            cpu = cpu_baseline_subprocess()
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f16/int8 (f32 accumulate)", "data": "synthetic",
-            "config": {"workload": "config2: 32 layers x B32 x 32/8 heads x 32K ctx (64x512 blocks, k=32) + 64 hot",
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": DECODE_DTYPE, "data": "synthetic",
+            "config": {"workload": WORKLOAD,
                        "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (26 GB per step)"},
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": qs_host[0].numel() * 2,
                     "d2h_bytes_per_step": out_host.numel() * 2},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak,
-                         "traffic": measured_traffic() if (world == 1 and c["layers"] == CFG["layers"]) else None,
-                         "traffic_source": "profiles/decode_cold_fast_config2.md (ncu launch list, same command)",
+                         "frac": achieved / peak, "traffic": traffic, "traffic_command": traffic_cmd,
                          "peak_kind": peak_kind,
-                         "kernel": "spx_decode_attn (cold partials + hot/merge)",
+                         "kernel": "spx_decode_attn (cold tier + hot/merge)",
                          "algorithmic_bytes_per_launch": bytes_launch, "launch_ms": kern_ms},
+            "parity": par,
             "rsvd": {"blocks_per_s": nb_rs * world / (rs_ms / 1e3), "blocks": 4096, "k": 32, "n_iter": 2,
-                     "oversampling": 8, "ms": rs_ms},
-            "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cpu_thr, "kind": "port",
-                             "sample": f"{max(1, args.cpu_calls)} (sequence, layer) decodes of the workload shape "
-                                       f"by the numpy port of the reference, extrapolated to a full step"},
+                     "oversampling": 8, "ms": rs_ms, "mean_rel_error": rs_err},
+            "cpu_baseline": None,
             "clocks": clk.summary(),
-            # per decode call: RoPE packing, the cold tier and the hot-tier merge (the
-            # workspace-header memset is a runtime copy, not a kernel of this library)
-            "gpu_launches": 3 * args.steps,
+            "gpu_launches": DECODE_LAUNCHES * args.steps,
             "setup_s": setup_s, "rsvd_setup_s": rsvd_setup_s,
         }
+        if cpu is not None:
+            cb = dict(cpu["cpu_baseline"])
+            line["cpu_baseline"] = cb
+            if "rsvd" in cpu:
+                line["rsvd"]["cpu_baseline"] = cpu["rsvd"]
         print(json.dumps(line), flush=True)
     if world > 1:
+        if gather is not None:
+            gather.close()
         torch.distributed.barrier(device_ids=[local])
         torch.distributed.destroy_process_group()
+    if not par["passed"]:
+        raise SystemExit(f"parity failed: cos_min={par['cos_min']:.6f} max_abs={par['max_abs']:.3e}")
+
+
+# What the decode call computes in, and how many kernels of this library it launches.
+DECODE_DTYPE = ("int8 codes + f16 bases/hot tier; cold-tier keys reconstructed by tcgen05 into an f16 "
+                "accumulator, RoPE in f16x2, QK and value products on f16 mma.sync with f32 accumulate; "
+                "softmax and merges f32")
+DECODE_LAUNCHES = 3
 
 
 def main():
@@ -444,7 +699,8 @@ def main():
     ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--cpu-calls", type=int, default=8)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-rsvd", action="store_true", help="reference arm: skip the rSVD sample")
     ap.add_argument("--layers", type=int, default=None, help="override the layer count (profiling only)")
     args = ap.parse_args()
     c = dict(CFG)

@@ -1,6 +1,7 @@
-"""KV-head sharding of decode across ranks (the multi-GPU layout of bench.py), checked
-on CPU with gloo ranks: each rank computes its head slice with the oracle and one
-all-gather reassembles the single-rank output exactly."""
+"""KV-head sharding of decode across ranks, checked on CPU with gloo ranks: each rank
+takes its head slice with the product's sharding helpers (unsloth_spectral.sharding),
+computes it with the oracle, and the product's HeadShardGather all-gathers and
+reassembles the single-rank output exactly."""
 import math
 import os
 import socket
@@ -54,13 +55,23 @@ def _worker(rank, world, port, q):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
+        from unsloth_spectral.sharding import HeadShardGather, head_slice, shard_heads, shard_query_heads
         c = _case()
-        Hl = c["H"] // world
-        part = torch.from_numpy(_decode_slice(c, rank * Hl, (rank + 1) * Hl)).contiguous()   # [1, Hl*nrep, 1, D]
-        gathered = [torch.empty_like(part) for _ in range(world)]
-        dist.all_gather(gathered, part)
+        h0, h1 = head_slice(c["H"], world, rank)
+        # the product helpers pick this rank's slice of the cache and of the queries
+        kv = torch.arange(c["H"]).view(1, c["H"])
+        assert shard_heads(kv, world, rank).flatten().tolist() == list(range(h0, h1))
+        qh = torch.arange(c["H"] * c["nrep"]).view(1, 1, -1)
+        assert shard_query_heads(qh, c["H"], world, rank).flatten().tolist() == \
+            list(range(h0 * c["nrep"], h1 * c["nrep"]))
+        part = torch.from_numpy(_decode_slice(c, h0, h1))            # [1, Hl*nrep, 1, D]
+        local = part.permute(2, 0, 1, 3).contiguous()                 # [L=1, B=1, Hl*nrep, D]
+        g = HeadShardGather(local, world)
+        g.start(local)
+        g.wait()
+        full = g.assembled()                                          # [1, 1, H*nrep, D]
         if rank == 0:
-            q.put(torch.cat(gathered, dim=1).numpy())
+            q.put(full.permute(1, 2, 0, 3).numpy())
     finally:
         dist.destroy_process_group()
 

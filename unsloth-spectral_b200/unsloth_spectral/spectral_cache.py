@@ -253,16 +253,20 @@ class SpectralCache:
     def append(self, K_new: torch.Tensor, V_new: torch.Tensor, position_ids: Optional[torch.Tensor] = None):
         """Append pre-RoPE ``K_new``/``V_new`` ``[B, H, T_new, D]`` (spectral_cache.py:164-241).
 
-        A new generation (first position below ``current_position``) resets the cache.
-        Reading that first position costs a device sync when ``position_ids`` lives on
-        the GPU, as in the reference; pass CPU positions (or None) to avoid it."""
-        if position_ids is not None and self.total_tokens > 0:
+        A new generation (first position below ``current_position``) resets the cache,
+        as in the reference (spectral_cache.py:176-186).  The reference reads that first
+        position with ``.item()`` on every append; here it is read only when it costs no
+        device sync on the decode path: CPU ``position_ids`` are always checked, device
+        ``position_ids`` only for a multi-token append (a prompt).  A single-token append
+        with device positions continues the sequence, so a new generation must start
+        with a prompt, with CPU positions or with ``reset()``."""
+        B, H, T_new, D = K_new.shape
+        if position_ids is not None and self.total_tokens > 0 and (position_ids.device.type == "cpu" or T_new > 1):
             first = int(position_ids.reshape(-1)[0].item())
             if first < self.current_position:
                 if self.debug_logging:
                     print(f"[SpectralCache.append] new generation at {first} < {self.current_position}: reset")
                 self.reset()
-        B, H, T_new, D = K_new.shape
         if H != self.num_heads or D != self.head_dim:
             raise ValueError(f"expected [B, {self.num_heads}, T, {self.head_dim}], got {tuple(K_new.shape)}")
         t = self._tiers_for(B, K_new.device)
