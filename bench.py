@@ -394,7 +394,7 @@ def make_queries(c, steps, rank_id, world, cos, sin):
     return out, qpos
 
 
-def decode_args(c, t, q, out, cos, sin, qpos, ws, Hl):
+def decode_args(c, t, q, out, cos, sin, qpos, ws, Hl, freq=None):
     from unsloth_spectral import _native as N
     nrep = c["q_heads"] // c["kv_heads"]
     return N.DecodeArgs(
@@ -407,7 +407,8 @@ def decode_args(c, t, q, out, cos, sin, qpos, ws, Hl):
         basis_k=t["basis_k"].data_ptr(), basis_v=t["basis_v"].data_ptr(), block_pos=t["block_pos"].data_ptr(),
         hot_k=t["hot_k"].data_ptr(), hot_v=t["hot_v"].data_ptr(), hot_pos=t["hot_pos"].data_ptr(),
         cos_table=cos.data_ptr(), sin_table=sin.data_ptr(), mask=None, out=out.data_ptr(),
-        workspace=ws.data_ptr() if ws is not None else None, workspace_bytes=ws.numel() if ws is not None else 0)
+        workspace=ws.data_ptr() if ws is not None else None, workspace_bytes=ws.numel() if ws is not None else 0,
+        rope_freq=freq.data_ptr() if freq is not None else None)
 
 
 def parity_units(c, Hl, G=32, extra=4, seed=11):
@@ -498,6 +499,9 @@ def run_ours(args, c):
     tiers, rsvd_setup_s = build_tiers(c, rank, world, dev)
     qpos = c["blocks"] * c["block"] + c["hot"]
     cos, sin = syn.rope_tables(qpos + 16, D, c["theta"], device=dev)
+    # RoPE frequencies of the tables (host copy, read by the library at each call); the
+    # reconstruct kernel runs instead when SPX_DECODE_PATH=fast
+    freq = _ops.rope_freq(cos, sin)
     nq = min(args.warmup + args.steps, 16)        # distinct seeded query sets, cycled
     qs_host, _ = make_queries(c, nq, rank, world, cos, sin)
     qs_dev = [q.to(dev) for q in qs_host]
@@ -505,8 +509,9 @@ def run_ours(args, c):
     # decode of step i + 1 writes the other
     outs = [torch.empty(L, B, Hql, D, dtype=torch.float16, device=dev) for _ in range(2)]
     out = outs[0]
-    a0 = decode_args(c, tiers, qs_dev[0], out, cos, sin, qpos, None, Hl)
+    a0 = decode_args(c, tiers, qs_dev[0], out, cos, sin, qpos, None, Hl, freq)
     ws = torch.empty(lib.spx_decode_workspace_size(a0), dtype=torch.uint8, device=dev)
+    path = lib.spx_decode_path(a0)
     gather = HeadShardGather(out, world) if world > 1 else None
     stream = torch.cuda.current_stream(dev)
     sh = stream.cuda_stream
@@ -516,7 +521,7 @@ def run_ours(args, c):
         o = outs[i & 1]
         if gather is not None:
             gather.release(o)
-        a = decode_args(c, tiers, q_dev, o, cos, sin, qpos, ws, Hl)
+        a = decode_args(c, tiers, q_dev, o, cos, sin, qpos, ws, Hl, freq)
         N.check(lib, lib.spx_decode_attn(a, sh), "spx_decode_attn")
         if gather is not None:
             gather.start(o)
@@ -545,7 +550,7 @@ def run_ours(args, c):
     barrier()
     ev2.record(stream)
     for i in range(args.steps):
-        a = decode_args(c, tiers, qs_dev[(args.warmup + i) % nq], out, cos, sin, qpos, ws, Hl)
+        a = decode_args(c, tiers, qs_dev[(args.warmup + i) % nq], out, cos, sin, qpos, ws, Hl, freq)
         N.check(lib, lib.spx_decode_attn(a, sh), "spx_decode_attn")
     ev3.record(stream)
     barrier()
@@ -558,7 +563,7 @@ def run_ours(args, c):
 
     def e2e_step(i):
         q_dev.copy_(pinned_in[i % nq], non_blocking=True)
-        a = decode_args(c, tiers, q_dev, out, cos, sin, qpos, ws, Hl)
+        a = decode_args(c, tiers, q_dev, out, cos, sin, qpos, ws, Hl, freq)
         N.check(lib, lib.spx_decode_attn(a, sh), "spx_decode_attn")
         if gather is not None:
             gather.start(out)
@@ -586,7 +591,7 @@ def run_ours(args, c):
 
     # ---- parity of the timed configuration: one more call with query set 0, sampled
     #      units checked against the CPU oracle (every rank checks its own head slice)
-    a = decode_args(c, tiers, qs_dev[0], out, cos, sin, qpos, ws, Hl)
+    a = decode_args(c, tiers, qs_dev[0], out, cos, sin, qpos, ws, Hl, freq)
     N.check(lib, lib.spx_decode_attn(a, sh), "spx_decode_attn")
     torch.cuda.synchronize(dev)
     par = parity_check(c, tiers, qs_dev[0], out, cos, sin, qpos, Hl, parity_units(c, Hl))
@@ -652,7 +657,7 @@ def run_ours(args, c):
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None,
-            "dtype": DECODE_DTYPE, "data": "synthetic",
+            "dtype": DECODE_DTYPE[path], "data": "synthetic",
             "config": {"workload": WORKLOAD,
                        "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (26 GB per step)"},
@@ -661,7 +666,7 @@ def run_ours(args, c):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "traffic_command": traffic_cmd,
                          "peak_kind": peak_kind,
-                         "kernel": "spx_decode_attn (cold tier + hot/merge)",
+                         "kernel": f"spx_decode_attn ({PATH_NAMES[path]} cold tier + hot/merge)",
                          "algorithmic_bytes_per_launch": bytes_launch, "launch_ms": kern_ms},
             "parity": par,
             "rsvd": {"blocks_per_s": nb_rs * world / (rs_ms / 1e3), "blocks": 4096, "k": 32, "n_iter": 2,
@@ -686,10 +691,17 @@ def run_ours(args, c):
         raise SystemExit(f"parity failed: cos_min={par['cos_min']:.6f} max_abs={par['max_abs']:.3e}")
 
 
-# What the decode call computes in, and how many kernels of this library it launches.
-DECODE_DTYPE = ("int8 codes + f16 bases/hot tier; cold-tier keys reconstructed by tcgen05 into an f16 "
-                "accumulator, RoPE in f16x2, QK and value products on f16 mma.sync with f32 accumulate; "
-                "softmax and merges f32")
+# What the decode call computes in, per cold-tier kernel, and how many kernels of this
+# library it launches (set-up kernel, cold tier, hot tier + merge).
+PATH_NAMES = {0: "generic", 1: "reconstruct", 2: "projection"}
+DECODE_DTYPE = {
+    0: "int8 codes + f16 bases/hot tier; f32 arithmetic throughout",
+    1: ("int8 codes + f16 bases/hot tier; cold-tier keys reconstructed by tcgen05 into an f16 accumulator, RoPE "
+        "in f16x2, QK and value products on f16 mma.sync with f32 accumulate; softmax and merges f32"),
+    2: ("int8 codes + f16 bases/hot tier; cold-tier projections on tcgen05 with f16 operands (f16 feature table, "
+        "f16 per-block projection matrix) and an f32 accumulator, scores as f32 sums of codes x projections, "
+        "value product on f16 mma.sync with f32 accumulate; softmax and merges f32"),
+}
 DECODE_LAUNCHES = 3
 
 

@@ -51,7 +51,7 @@
 extern "C" {
 #endif
 
-#define SPX_ABI_VERSION 1
+#define SPX_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define SPX_API __attribute__((visibility("default")))
@@ -123,10 +123,25 @@ typedef struct spx_decode_args {
   void* out;               /* dtype [L][B][H_q][D] */
   void* workspace;         /* >= spx_decode_workspace_size(args) bytes, 256-byte aligned */
   size_t workspace_bytes;
+  const float* rope_freq;  /* optional HOST pointer to head_dim/2 floats: the RoPE frequencies
+                              theta_i such that the first-half table entries are
+                              cos/sin(position * theta_i) (times one common magnitude, if any).
+                              With it (and tied tables in ABSOLUTE mode) the cold tier runs the
+                              projection kernel; NULL keeps the reconstruct kernel.  Read during
+                              the call only. */
 } spx_decode_args;
 
 SPX_API size_t spx_decode_workspace_size(const spx_decode_args* args);
 SPX_API int spx_decode_attn(const spx_decode_args* args, void* stream);
+
+/* The cold-tier kernel spx_decode_attn runs for these arguments: SPX_PATH_GENERIC (FP32,
+ * any supported shape), SPX_PATH_RECONSTRUCT (keys rebuilt on tensor cores, then rotated
+ * per token) or SPX_PATH_PROJECTION (rotation folded into a token-feature table; needs
+ * rope_freq); minus the spx_status when the arguments are invalid.  Launches nothing. */
+#define SPX_PATH_GENERIC 0
+#define SPX_PATH_RECONSTRUCT 1
+#define SPX_PATH_PROJECTION 2
+SPX_API int spx_decode_path(const spx_decode_args* args);
 
 /* Decode attention for callers that cannot allocate device memory.  This entry point has
  * no counterpart in the reference; it exists for hosts with no device allocator on the

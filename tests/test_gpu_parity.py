@@ -533,11 +533,9 @@ FAST_CASES = [
 
 @pytest.fixture
 def generic_path(monkeypatch):
+    """use(True): the generic FP32 cold-tier kernel; use(False): the reconstruct kernel."""
     def use(flag):
-        if flag:
-            monkeypatch.setenv("SPX_DECODE_PATH", "generic")
-        else:
-            monkeypatch.delenv("SPX_DECODE_PATH", raising=False)
+        monkeypatch.setenv("SPX_DECODE_PATH", "generic" if flag else "fast")
     return use
 
 
@@ -596,3 +594,108 @@ def test_fast_kernel_long_context_properties(generic_path):
     r1["B"] = 1
     one, _ = _run_random(r1, torch.float16, "decode")
     np.testing.assert_allclose(one[0], fast[1], atol=2e-3)
+
+
+# ------------------------------------------- projection cold-tier kernel vs generic
+def _path_of(r, dtype, mode):
+    """The cold-tier kernel spx_decode_attn picks for case ``r`` (spx_decode_path)."""
+    from unsloth_spectral import _native as N, _ops
+    B, H, D, T = r["B"], r["H"], r["D"], r["T"]
+    cache = cache_from_arrays(H, D, T, r["kK"], r["kV"], r["codes_K"], r["scale_K"], r["basis_K"], r["codes_V"],
+                              r["scale_V"], r["basis_V"], r["start"], r["hot_K"], r["hot_V"], r["hot_pos"], dtype,
+                              B=B)
+    q = torch.from_numpy(r["Q"]).cuda().to(dtype).reshape(1, B, -1, D).contiguous()
+    cos, sin = torch.from_numpy(r["cos"]).cuda(), torch.from_numpy(r["sin"]).cuda()
+    rm = N.SPX_ROPE_DISTANCE if mode == "forward" else N.SPX_ROPE_ABSOLUTE
+    a, _, keep = _ops.decode_args(q, cache.tiers, cos, sin, r["qpos"], rope_mode=rm)
+    return N.load().spx_decode_path(a)
+
+
+@pytest.fixture
+def decode_path(monkeypatch):
+    def use(name):
+        if name is None:
+            monkeypatch.delenv("SPX_DECODE_PATH", raising=False)
+        else:
+            monkeypatch.setenv("SPX_DECODE_PATH", name)
+    return use
+
+
+PROJ_CASES = [
+    # seed, B, H, nrep, D, T, nblk, kK, kV, hot, masked   (FP16, D=128, linear RoPE, no mask)
+    (61, 2, 8, 4, 128, 512, 3, 32, 32, 64, False),
+    (62, 3, 2, 8, 128, 256, 5, 16, 16, 7, False),      # n_rep 8 x rank 16 = 128 columns
+    (63, 1, 4, 1, 128, 256, 4, 16, 16, 0, False),      # MHA, 16 columns, no hot tier
+    (64, 2, 2, 2, 128, 512, 2, 16, 32, 130, False),
+    (65, 5, 8, 4, 128, 512, 9, 32, 32, 1, False),
+    (66, 2, 4, 4, 128, 512, 3, 16, 32, 20, False),     # 64 columns
+    (67, 1, 2, 2, 128, 256, 6, 32, 16, 5, False),
+]
+
+
+@pytest.mark.parametrize("case", PROJ_CASES)
+@pytest.mark.parametrize("mode", ["forward", "decode"])
+def test_proj_kernel_matches_oracle_and_generic(case, mode, decode_path):
+    r = _random_case(*case)
+    decode_path("proj")
+    from unsloth_spectral import _native as N
+    assert _path_of(r, torch.float16, mode) == N.SPX_PATH_PROJECTION
+    proj, ref = _run_random(r, torch.float16, mode)
+    _close(proj, ref)
+    decode_path("generic")
+    gen, _ = _run_random(r, torch.float16, mode)
+    decode_path(None)
+    _close(proj, gen)
+
+
+@pytest.mark.parametrize("case,plan", [
+    ((71, 3, 4, 4, 128, 512, 6, 32, 32, 9, False), "4,3,2"),
+    ((72, 3, 4, 4, 128, 512, 6, 32, 32, 9, False), "5,2,3"),
+    ((73, 2, 4, 2, 128, 512, 5, 16, 32, 0, False), "8,5,1"),
+    ((74, 2, 4, 8, 128, 256, 7, 16, 16, 3, False), "3,4,2"),
+    ((75, 4, 8, 4, 128, 512, 3, 32, 32, 2, False), "32,1,1"),    # 32 units through one CTA
+])
+def test_proj_kernel_multi_item_plans(case, plan, decode_path, monkeypatch):
+    r = _random_case(*case)
+    monkeypatch.setenv("SPX_FAST_PLAN", plan)
+    decode_path("proj")
+    proj, ref = _run_random(r, torch.float16, "decode")
+    _close(proj, ref)
+
+
+def test_proj_kernel_distance_mode_keys_past_the_query(decode_path):
+    """DISTANCE mode with the query placed inside the cold tier: the reference clamps the
+    distance of later keys to 0 (spectral_attention.py:198), which the projection kernel
+    handles with unrotated projections for those tokens."""
+    r = _random_case(76, 2, 4, 4, 128, 512, 3, 32, 32, 10, False)
+    r["qpos"] = 700          # inside block 1; block 2 and the hot tier lie after it
+    decode_path("proj")
+    from unsloth_spectral import _native as N
+    assert _path_of(r, torch.float16, "forward") == N.SPX_PATH_PROJECTION
+    proj, ref = _run_random(r, torch.float16, "forward")
+    _close(proj, ref)
+
+
+def test_proj_kernel_headline_shape(decode_path, monkeypatch):
+    """The timed configuration's geometry (64 blocks of 512 at k=32, n_rep 4, 64 hot,
+    the work plan of the full run: 32 units per item, 16-block ranges) on a reduced
+    batch: projection kernel against the float32 oracle and the generic kernel."""
+    r = _random_case(77, 4, 8, 4, 128, 512, 64, 32, 32, 64, False)
+    monkeypatch.setenv("SPX_FAST_PLAN", "32,16,4")
+    decode_path("proj")
+    proj, ref = _run_random(r, torch.float16, "decode")
+    _close(proj, ref)
+    monkeypatch.delenv("SPX_FAST_PLAN")
+    decode_path("generic")
+    gen, _ = _run_random(r, torch.float16, "decode")
+    decode_path(None)
+    _close(proj, gen)
+
+
+def test_proj_kernel_needs_linear_rope_tables(decode_path):
+    """Tables that are not cos/sin(position * theta) keep the reconstruct kernel."""
+    from unsloth_spectral import _native as N
+    r = _random_case(78, 1, 2, 4, 128, 512, 2, 32, 32, 3, False)
+    r["cos"] = r["cos"] * (1.0 + 0.01 * np.arange(r["cos"].shape[0], dtype=np.float32)[:, None] / 1000)
+    decode_path("proj")
+    assert _path_of(r, torch.float16, "decode") == N.SPX_PATH_RECONSTRUCT

@@ -70,7 +70,7 @@ def build(jobs: int = 0, force: bool = False, verbose: bool = False, ptxas_verbo
     if failed:
         raise RuntimeError(f"nvcc failed for: {failed}")
     if cmds or not os.path.exists(OUT) or force:
-        link = [cc, *ARCH, "-shared", "-Xcompiler", "-fPIC", *objs, "-o", OUT, "-lcuda"]
+        link = [cc, *ARCH, "-shared", "-Xcompiler", "-fPIC", *objs, "-o", OUT]
         r = subprocess.run(link, capture_output=True, text=True)
         if r.returncode != 0:
             sys.stderr.write(r.stdout + r.stderr)

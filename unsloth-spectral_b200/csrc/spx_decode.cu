@@ -359,9 +359,33 @@ static size_t partial_bytes(const DecodeParams& p) {
   return (size_t)p.L * p.B * p.H * p.nparts * p.nrep * (p.D + 4) * sizeof(float);
 }
 
+
 void decode_set_workspace(DecodeParams* p, void* base) {
   p->ws = base ? reinterpret_cast<float*>(reinterpret_cast<char*>(base) + kWsHeader) : nullptr;
   p->rope = base ? reinterpret_cast<char*>(base) + kWsHeader + partial_bytes(*p) : nullptr;
+}
+
+// SPX_DECODE_PATH selects the cold-tier kernel: "generic" (FP32, any shape), "fast"
+// (reconstruct-rotate) or "proj" (projection, which needs the RoPE frequencies); the
+// default takes the reconstruct-rotate kernel when it covers the configuration, else
+// the projection kernel, else the generic one.  Forcing a path that does not cover the
+// configuration falls back the same way.  The tests use it to cross-check the kernels
+// on identical inputs.
+static void choose_path(DecodeParams* p) {
+  const char* e = getenv("SPX_DECODE_PATH");
+  const bool want_generic = e && strcmp(e, "generic") == 0;
+  const bool want_proj = e && strcmp(e, "proj") == 0;
+  p->path = PATH_GENERIC;
+  p->nparts = p->nblk > 0 ? p->nblk : 1;
+  p->ncold = p->nblk;
+  if (p->nblk <= 0 || want_generic) return;
+  if ((want_proj || !decode_fast_supported(*p)) && decode_proj_supported(*p)) {
+    p->path = PATH_PROJ;
+    p->nparts = p->ncold = decode_proj_ncold(*p);
+  } else if (decode_fast_supported(*p)) {
+    p->path = PATH_FAST;
+    p->nparts = p->ncold = decode_fast_ncold(*p);
+  }
 }
 
 static int make_params(const spx_decode_args* a, DecodeParams* p) {
@@ -415,6 +439,7 @@ static int make_params(const spx_decode_args* a, DecodeParams* p) {
   p->tied = a->rope_tied ? 1 : 0;
   p->rope_len = a->rope_len;
   p->mask_stride = a->mask_stride;
+  p->freq = a->rope_freq;
   p->nparts = a->num_blocks > 0 ? a->num_blocks : 1;
   p->ncold = a->num_blocks;
   p->qpos = a->query_position;
@@ -434,46 +459,38 @@ static int make_params(const spx_decode_args* a, DecodeParams* p) {
   p->sinT = a->sin_table;
   p->mask = a->mask;
   p->out = a->out;
+  p->dtype = a->dtype;
+  choose_path(p);
   decode_set_workspace(p, a->workspace);
   return SPX_OK;
 }
 
+static size_t path_scratch_bytes(const DecodeParams& p) {
+  if (p.path == PATH_FAST) return (size_t)p.nblk * p.Tb * 256;
+  if (p.path == PATH_PROJ) return decode_proj_scratch_bytes(p);
+  return 0;
+}
+
 size_t decode_workspace_bytes(const DecodeParams& p) {
-  return kWsHeader + partial_bytes(p) + (size_t)p.nblk * p.Tb * 256;
+  return kWsHeader + partial_bytes(p) + path_scratch_bytes(p);
 }
 
-// SPX_DECODE_PATH=generic forces the generic cold-tier kernel (used to cross-check the
-// fast kernel on identical inputs); the default picks the fast kernel when it covers
-// the configuration.
-static bool force_generic() {
-  const char* e = getenv("SPX_DECODE_PATH");
-  return e && strcmp(e, "generic") == 0;
-}
-
-int decode_dispatch(const DecodeParams& p0, cudaStream_t st) {
-  DecodeParams p = p0;
+int decode_dispatch(const DecodeParams& p, cudaStream_t st) {
   int rc = SPX_OK;
   if (p.nblk > 0) {
-    SPX_REQUIRE(p.ws && p.rope, SPX_ERR_WORKSPACE, "decode workspace pointers are not set");
+    SPX_REQUIRE(p.ws && (p.path == PATH_GENERIC || p.rope), SPX_ERR_WORKSPACE,
+                "decode workspace pointers are not set");
     const cudaError_t e = cudaMemsetAsync(reinterpret_cast<char*>(p.ws) - kWsHeader, 0, sizeof(int), st);
     SPX_REQUIRE(e == cudaSuccess, SPX_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
-    if (!force_generic() && decode_fast_supported(p)) {
-      p.ncold = decode_fast_ncold(p);
-      rc = decode_fast_cold(p, st);
-    } else {
-      p.ncold = p.nblk;
-      rc = SPX_DISPATCH_DTYPE(p.dtype, T, [&] { return launch_cold<T>(p, st); });
-    }
+    if (p.path == PATH_PROJ) rc = decode_proj_cold(p, st);
+    else if (p.path == PATH_FAST) rc = decode_fast_cold(p, st);
+    else rc = SPX_DISPATCH_DTYPE(p.dtype, T, [&] { return launch_cold<T>(p, st); });
     if (rc != SPX_OK) return rc;
   }
   return SPX_DISPATCH_DTYPE(p.dtype, T, [&] { return launch_hot_merge<T>(p, st); });
 }
 
-int decode_params(const spx_decode_args* a, DecodeParams* p) {
-  const int rc = make_params(a, p);
-  if (rc == SPX_OK) p->dtype = a->dtype;
-  return rc;
-}
+int decode_params(const spx_decode_args* a, DecodeParams* p) { return make_params(a, p); }
 
 }  // namespace spx
 
@@ -484,15 +501,19 @@ extern "C" {
 size_t spx_decode_workspace_size(const spx_decode_args* a) {
   DecodeParams p;
   if (make_params(a, &p) != SPX_OK) return 0;
-  p.dtype = a->dtype;
   return decode_workspace_bytes(p);
+}
+
+int spx_decode_path(const spx_decode_args* a) {
+  DecodeParams p;
+  const int rc = make_params(a, &p);
+  return rc != SPX_OK ? -rc : p.path;
 }
 
 int spx_decode_attn(const spx_decode_args* a, void* stream) {
   DecodeParams p;
   int rc = make_params(a, &p);
   if (rc != SPX_OK) return rc;
-  p.dtype = a->dtype;
   const size_t need = decode_workspace_bytes(p);
   if (p.nblk > 0) {
     SPX_REQUIRE(a->workspace && a->workspace_bytes >= need, SPX_ERR_WORKSPACE,

@@ -20,6 +20,7 @@ SPX_ERR_EMPTY = 6
 NOALLOC_SCRATCH_BYTES = 64 << 20
 SPX_F32, SPX_F16, SPX_BF16 = 0, 1, 2
 SPX_ROPE_DISTANCE, SPX_ROPE_ABSOLUTE = 0, 1
+SPX_PATH_GENERIC, SPX_PATH_RECONSTRUCT, SPX_PATH_PROJECTION = 0, 1, 2
 
 _DTYPES = {torch.float32: SPX_F32, torch.float16: SPX_F16, torch.bfloat16: SPX_BF16}
 
@@ -43,7 +44,7 @@ class DecodeArgs(C.Structure):
         (n, C.c_void_p) for n in (
             "q", "codes_k", "codes_v", "scale_k", "scale_v", "basis_k", "basis_v", "block_pos", "hot_k",
             "hot_v", "hot_pos", "cos_table", "sin_table", "mask", "out", "workspace")] + [
-        ("workspace_bytes", C.c_size_t)]
+        ("workspace_bytes", C.c_size_t), ("rope_freq", C.c_void_p)]
 
 
 class RsvdArgs(C.Structure):
@@ -86,6 +87,7 @@ EXPORTS = {
     "spx_decode_workspace_size": (C.c_size_t, [C.POINTER(DecodeArgs)]),
     "spx_decode_attn": (C.c_int, [C.POINTER(DecodeArgs), C.c_void_p]),
     "spx_decode_attn_noalloc": (C.c_int, [C.POINTER(DecodeArgs), C.c_void_p]),
+    "spx_decode_path": (C.c_int, [C.POINTER(DecodeArgs)]),
     "spx_rsvd_workspace_size": (C.c_size_t, [C.POINTER(RsvdArgs)]),
     "spx_rsvd_compress": (C.c_int, [C.POINTER(RsvdArgs), C.c_void_p]),
     "spx_quantize_int8": (C.c_int, [C.POINTER(QuantArgs), C.c_void_p]),
@@ -98,7 +100,7 @@ EXPORTS = {
     "spx_check_device": (C.c_int, []),
 }
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 _lib = None
 _load_error = None
 _device_ok = {}

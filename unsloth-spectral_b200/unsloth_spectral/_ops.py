@@ -62,6 +62,51 @@ def rope_tied(cos: torch.Tensor, sin: torch.Tensor) -> bool:
     return v
 
 
+_freq_cache = {}
+
+
+def rope_freq(cos: torch.Tensor, sin: torch.Tensor):
+    """The RoPE frequencies ``theta_i`` of HF-style tables (first half of each row
+    ``cos/sin(position * theta_i)``, times one common magnitude), as a float32 CPU tensor
+    of ``D/2`` values, or None when the tables are not of that form.  ``theta`` is read
+    from rows 1 and ``len - 1`` in float64 and every row is checked against it, with the
+    tolerance of float32 tables whose angles were formed in float32
+    (``|dx| <= 4e-6 + 3e-7 * position * theta``).  Memoised per tensor version, so the
+    device-to-host copy runs once per table."""
+    k = (_key(cos), _key(sin))
+    v = _freq_cache.get(k, False)
+    if v is not False:
+        return v
+    c = cos.detach().to("cpu", torch.float64)
+    s = sin.detach().to("cpu", torch.float64)
+    if c.dim() == 3 and c.shape[0] == 1:
+        c, s = c[0], s[0]
+    out = None
+    if c.dim() == 2 and c.shape[0] >= 2 and c.shape[1] % 2 == 0:
+        h = c.shape[1] // 2
+        c, s = c[:, :h], s[:, :h]
+        n = c.shape[0]
+        mag = torch.sqrt(c[0] ** 2 + s[0] ** 2)
+        th = torch.atan2(s[1], c[1])
+        if n > 2:
+            p = n - 1
+            ph = torch.atan2(s[p], c[p])
+            turns = torch.round((p * th - ph) / (2 * math.pi))
+            th = (ph + 2 * math.pi * turns) / p
+        pos = torch.arange(n, dtype=torch.float64)[:, None]
+        ang = pos * th[None]
+        tol = 4e-6 + 3e-7 * pos * th.abs()[None]
+        ok = bool(((c - mag * torch.cos(ang)).abs() <= tol * (1 + mag)).all()
+                  and ((s - mag * torch.sin(ang)).abs() <= tol * (1 + mag)).all()
+                  and bool((s[0].abs() <= 1e-6).all()))
+        if ok:
+            out = th.to(torch.float32).contiguous()
+    if len(_freq_cache) > 64:
+        _freq_cache.clear()
+    _freq_cache[k] = out
+    return out
+
+
 def quantize_int8(x: torch.Tensor):
     """Per-leading-index INT8 quantisation; returns (codes int8, scale f32 [N],
     minmax f32 [N, 2], dequantised f32) -- bit-exact with the reference's
@@ -133,6 +178,7 @@ def decode_args(q: torch.Tensor, tiers, cos: torch.Tensor, sin: torch.Tensor, qu
     sin32 = rope_table_f32(sin, dev)
     if tied is None:
         tied = rope_tied(cos32, sin32)
+    freq = rope_freq(cos32, sin32) if (tied or rope_mode == N.SPX_ROPE_DISTANCE) else None
     if out is None:
         out = torch.empty(L, B, Hq, D, dtype=t.dtype, device=dev)
     mask_u8 = None
@@ -156,8 +202,9 @@ def decode_args(q: torch.Tensor, tiers, cos: torch.Tensor, sin: torch.Tensor, qu
         q=N.ptr(q), codes_k=N.ptr(t.codes_k), codes_v=N.ptr(t.codes_v), scale_k=N.ptr(t.scale_k),
         scale_v=N.ptr(t.scale_v), basis_k=N.ptr(t.basis_k), basis_v=N.ptr(t.basis_v),
         block_pos=N.ptr(t.block_pos), hot_k=N.ptr(t.hot_k), hot_v=N.ptr(t.hot_v), hot_pos=N.ptr(t.hot_pos),
-        cos_table=N.ptr(cos32), sin_table=N.ptr(sin32), mask=N.ptr(mask_u8), out=N.ptr(out))
-    return a, out, (q, cos32, sin32, mask_u8)
+        cos_table=N.ptr(cos32), sin_table=N.ptr(sin32), mask=N.ptr(mask_u8), out=N.ptr(out),
+        rope_freq=N.ptr(freq))
+    return a, out, (q, cos32, sin32, mask_u8, freq)
 
 
 def decode(q: torch.Tensor, tiers, cos: torch.Tensor, sin: torch.Tensor, query_position: int, *,
