@@ -13,10 +13,13 @@ Reported: decode tokens/s (value: inputs resident; e2e: through the C ABI with t
 queries copied from pinned host memory and the outputs copied back every step), the
 roofline of the decode launch against measured HBM bandwidth, a parity block (sampled
 (layer, sequence, KV head) units of the timed configuration checked against the CPU
-oracle, cos >= 0.9999 and max-abs <= 1e-2, the run exits non-zero otherwise), rSVD
-blocks/s on config 3's largest batch (4096 blocks of 512x128 FP16, k=32, 2 power
-iterations) with its mean reconstruction error, and the reference's own CPU code
-(installed under baseline/_ref) timed on a bounded sample as the CPU baseline.
+oracle, cos >= 0.9999 and max-abs <= 1e-2, the run exits non-zero otherwise), the
+config-3 sweep of rSVD + INT8 compression (Nb 8/128/4096 x k 16/32 x 0/2 power
+iterations: blocks/s, reconstruction error before and after INT8, roofline; the
+4096-block k=32 q=2 point is the "rsvd" headline), config 1 on one GPU (one layer,
+batch 16, 8K context: decode plus one block compression per sequence and KV head every
+step, tokens/s), and the reference's own CPU code (installed under baseline/_ref) timed
+on a bounded sample as the CPU baseline.
 
 Reference arm (--impl reference): the reference package's own PyTorch CPU functions,
 `kernels.spectral_attention_decode` (one (sequence, layer) decode of the workload per
@@ -355,7 +358,7 @@ def build_tiers(c, rank_id, world, dev):
     nm = B * Hl * NB
     rs = 0.0
     for l in range(L):
-        K, V = syn.kv_layer_batched(2, l, B, H, NB * T + hot, D, c["gen_rank"], c["rho"], dev)
+        K, V = syn.kv_layer_batched(c.get("seed_cfg", 2), l, B, H, NB * T + hot, D, c["gen_rank"], c["rho"], dev)
         for X, name in ((K, "k"), (V, "v")):
             Xl = X[:, h0:h1].contiguous()
             t[f"hot_{name}"][l].copy_(Xl[:, :, NB * T:])
@@ -469,6 +472,231 @@ def parity_check(c, t, q_dev, out_dev, cos, sin, qpos, Hl, units):
             "tolerance": {"cos_min": PARITY_COS, "max_abs": PARITY_MAXABS},
             "oracle": "oracle/spectral_oracle.py spectral_attention_decode (float32 numpy)",
             "sampled": rows}
+
+
+# ---------------------------------------------------------------- config 3 sweep ---
+# batched rSVD + INT8 quantisation of 512 x 128 FP16 blocks, Nb in
+# {8, 128, 4096}, k in {16, 32}, oversampling 8, power iterations in {0, 2}; blocks are
+# rank-24 (sigma_i = 0.85^i) for k = 16 and rank-48 (0.9^i) for k = 32, plus N(0, 0.05^2).
+SWEEP = [(nb, k, q) for nb in (8, 128, 4096) for k in (16, 32) for q in (0, 2)]
+
+
+def rsvd_blocks(nb, k, dev, seed):
+    rank, rho = (24, 0.85) if k == 16 else (48, 0.9)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    M = (torch.randn(nb, 512, rank, generator=g, device=dev) * (rho ** torch.arange(rank, device=dev))) @ \
+        torch.randn(nb, rank, 128, generator=g, device=dev)
+    return (M + 0.05 * torch.randn(nb, 512, 128, generator=g, device=dev)).half()
+
+
+def rsvd_roofline(nb, k, q, ms, peaks):
+    """Roofline of one compression call: algorithmic bytes (M read, sketch read, INT8
+    codes + FP16 basis + scale written) against measured HBM bandwidth, and the
+    products' FLOPs (2 + 2q products of 512 x 128 x r) against the measured bf16 peak."""
+    r = k + 8
+    byts = nb * (512 * 128 * 2 + 128 * r * 4 + 512 * k + k * 128 * 2 + 4)
+    flops = nb * 2.0 * 512 * 128 * r * (2 + 2 * q)
+    hbm, tflops = peaks
+    t_hbm, t_tc = byts / (hbm * 1e9), flops / (tflops * 1e12)
+    achieved = byts / (ms / 1e3) / 1e9
+    return {"bound": "hbm" if t_hbm >= t_tc else "tensor", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+            "frac": achieved / hbm, "algorithmic_bytes": byts, "product_flops": flops,
+            "tensor_frac": flops / (ms / 1e3) / (tflops * 1e12), "floor_ms": max(t_hbm, t_tc) * 1e3}
+
+
+def rsvd_sweep(dev, world, stream, barrier, peaks):
+    """Config 3 through spx_rsvd_compress with the cache's outputs (token-major INT8
+    codes, scale, FP16 basis).  Each rank compresses nb / world blocks; time = max over
+    ranks.  Errors: the rSVD's relative Frobenius reconstruction error (U S Vh) and the
+    error after INT8 quantisation (codes x scale x basis), means over the blocks."""
+    from unsloth_spectral import _ops
+    rows = []
+    for nb, k, q in SWEEP:
+        nbl = nb // world
+        M = rsvd_blocks(nbl, k, dev, 1000 + nb + k + q + 7 * int(os.environ.get("RANK", "0")))
+        om = torch.randn(nbl, 128, k + 8, generator=torch.Generator(device=dev).manual_seed(5 + k), device=dev)
+        codes = torch.empty(nbl, 512, k, dtype=torch.int8, device=dev)
+        qscale = torch.empty(nbl, dtype=torch.float32, device=dev)
+        basis = torch.empty(nbl, k, 128, dtype=torch.float16, device=dev)
+
+        def call():
+            _ops.rsvd(M, om, k, q, want_factors=False, codes=codes, codes_strides=(512 * k, k, 1), rank_pad=k,
+                      qscale=qscale, scale_stride=1, basis=basis, basis_stride=k * 128)
+
+        reps = 3 if nb >= 4096 else 20
+        for _ in range(2):
+            call()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            call()
+        e1.record(stream)
+        barrier()
+        ms = torch.tensor([e0.elapsed_time(e1) / reps], dtype=torch.float64, device=dev)
+        if world > 1:
+            torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
+        ms = ms.item()
+        U, S, Vh = _ops.rsvd(M, om, k, q, want_factors=True)
+        Mf = M.float()
+        den = torch.linalg.norm(Mf, dim=(1, 2))
+        err = (torch.linalg.norm(Mf - (U * S[:, None, :]) @ Vh, dim=(1, 2)) / den).mean()
+        Rq = (codes.float() * qscale[:, None, None]) @ basis.float()
+        errq = (torch.linalg.norm(Mf - Rq, dim=(1, 2)) / den).mean()
+        errs = torch.stack([err, errq]).double()
+        if world > 1:
+            torch.distributed.all_reduce(errs)
+            errs /= world
+        rows.append({"blocks": nb, "k": k, "n_iter": q, "oversampling": 8, "ms": ms,
+                     "blocks_per_s": nb / (ms / 1e3), "mean_rel_error": errs[0].item(),
+                     "mean_rel_error_int8": errs[1].item(), "l2": "inputs larger than L2" if nb * 131072 > 126e6
+                     else "inputs fit in L2 (repeated calls)",
+                     "roofline": rsvd_roofline(nb, k, q, ms, peaks)})
+        del M, om, codes, qscale, basis, U, S, Vh, Mf, Rq
+    return rows
+
+
+# ---------------------------------------------------------------- config 1 ---------
+# BASELINE config 1: one layer, batch 16, 32/8 heads, 8K context = 16 cold blocks at
+# k=16 + 448 warm + 64 hot tokens (512 uncompressed), rank-24 (0.85^i) + noise K/V;
+# every step decodes one token per sequence AND compresses one newly full 512-token
+# block per (sequence, KV head) for K and V (256 rSVDs + INT8), as SpectralCache.append
+# does when its hot tier fills (spectral_cache.py:237-241).
+CFG1 = dict(layers=1, batch=16, q_heads=32, kv_heads=8, head_dim=128, block=512, blocks=16, rank=16, hot=512,
+            gen_rank=24, rho=0.85, oversampling=8, n_iter=2, theta=1e6, seed_cfg=1)
+
+
+def run_config1(args, dev, stream, barrier):
+    """Config 1 on one GPU: tokens/s of decode + per-step block compression.  The
+    compression reads the 512 uncompressed tokens of every (sequence, KV head) and writes
+    a spare cold slot (keys token-major, values in the value-tile layout), so the cache
+    the decode reads stays the same from step to step."""
+    from unsloth_spectral import _native as N, _ops
+    from unsloth_spectral import synthetic as syn
+    c = CFG1
+    lib = N.lib_for(dev)
+    L, B, H, D, T, R = c["layers"], c["batch"], c["kv_heads"], c["head_dim"], c["block"], c["rank"]
+    t, _ = build_tiers(c, 0, 1, dev)
+    qpos = c["blocks"] * T + c["hot"]
+    cos, sin = syn.rope_tables(qpos + 16, D, c["theta"], device=dev)
+    freq = _ops.rope_freq(cos, sin)
+    qs, _ = make_queries(c, 4, 0, 1, cos, sin)
+    qs = [q.to(dev) for q in qs]
+    out = torch.empty(L, B, c["q_heads"], D, dtype=torch.float16, device=dev)
+    a0 = decode_args(c, t, qs[0], out, cos, sin, qpos, None, H, freq)
+    ws = torch.empty(lib.spx_decode_workspace_size(a0), dtype=torch.uint8, device=dev)
+    nm = B * H
+    spare = {n: dict(codes=torch.empty(nm, T * R, dtype=torch.int8, device=dev),
+                     scale=torch.empty(nm, dtype=torch.float32, device=dev),
+                     basis=torch.empty(nm, R, D, dtype=torch.float16, device=dev)) for n in ("k", "v")}
+    om = {n: torch.randn(nm, D, R + 8, generator=torch.Generator(device=dev).manual_seed(77 + i), device=dev)
+          for i, n in enumerate(("k", "v"))}
+    sh = stream.cuda_stream
+
+    def decode(i):
+        a = decode_args(c, t, qs[i % 4], out, cos, sin, qpos, ws, H, freq)
+        N.check(lib, lib.spx_decode_attn(a, sh), "spx_decode_attn")
+
+    def compress():
+        for n in ("k", "v"):
+            sp = spare[n]
+            cs = (T * R, R, 1) if n == "k" else (R * T, 0, 0)
+            _ops.rsvd(t[f"hot_{n}"][0], om[n], R, c["n_iter"], want_factors=False, codes=sp["codes"],
+                      codes_strides=cs, rank_pad=R, qscale=sp["scale"], scale_stride=1, basis=sp["basis"],
+                      basis_stride=R * D, M_mat_stride=c["hot"] * D, num_mats=nm, m=T, n=D, codes_tiled=(n == "v"))
+
+    def timed(fn, n):
+        for i in range(3):
+            fn(i)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(n):
+            fn(i)
+        e1.record(stream)
+        barrier()
+        return e0.elapsed_time(e1) / n
+
+    steps = max(args.steps, 10)
+    step_ms = timed(lambda i: (decode(i), compress()), steps)
+    dec_ms = timed(decode, steps)
+    comp_ms = timed(lambda i: compress(), steps)
+    decode(0)
+    torch.cuda.synchronize(dev)
+    par = parity_check(c, t, qs[0], out, cos, sin, qpos, H, parity_units(c, H, G=8, extra=2))
+    return {"workload": "config1: 1 layer x B16 x 32/8 heads x 8K ctx (16x512 blocks, k=16) + 512 uncompressed; "
+                        "per step 1 decode token per sequence + 256 block compressions (K and V, k=16, q=2)",
+            "tokens_per_s": B / (step_ms / 1e3), "ms_per_step": step_ms, "decode_ms": dec_ms,
+            "compress_ms": comp_ms, "blocks_compressed_per_step": 2 * nm, "steps": steps, "parity": par}
+
+
+# ---------------------------------------------------------------- config 4 ---------
+def run_config4(args):
+    """the end-to-end greedy loop of a random-init Mistral-7B-shaped
+    model (32 layers, hidden 4096, 32/8 heads, SwiGLU 14336, vocab 32768, RoPE 1e6, BF16
+    weights ~ N(0, 0.02^2)) patched with patch_unsloth_attention (k=16, 512-token blocks,
+    64-token hot tier): batch 8, a 4096-token random prompt, then 512 greedy tokens through
+    the patched per-layer forwards (unsloth_spectral.llama_loop).  Data parallel: every
+    rank runs its own replica and batch; value = all ranks' new tokens / the slowest
+    rank's time (prefill + decode), timed with CUDA events."""
+    _use_ours()
+    from unsloth_spectral import get_cache_stats
+    from unsloth_spectral.llama_loop import MISTRAL_7B, SpectralLlama
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=900))
+    B, T, NEW = 8, 4096, args.new_tokens
+    t0 = time.perf_counter()
+    model = SpectralLlama(MISTRAL_7B, device=dev, dtype=torch.bfloat16, seed=1234)
+    model.patch(block_size=512, k_rank_keys=16, k_rank_values=16, hot_buffer_size=64)
+    g = torch.Generator(device=dev).manual_seed(99 + rank)
+    prompt = torch.randint(0, MISTRAL_7B.vocab, (B, T), generator=g, device=dev)
+    setup_s = time.perf_counter() - t0
+    stream = torch.cuda.current_stream(dev)
+    model.generate(prompt, 4)   # warm-up: the same kernels, a short tail
+    torch.cuda.synchronize(dev)
+    ev = {k: torch.cuda.Event(enable_timing=True) for k in ("start", "prefill", "decode")}
+    if world > 1:
+        torch.distributed.barrier(device_ids=[local])
+    with ClockSampler(local) as clk:
+        ev["start"].record(stream)
+        toks = model.generate(prompt, NEW, timer=lambda name: ev[name].record(stream))
+        out_host = toks.cpu()
+    torch.cuda.synchronize(dev)
+    times = torch.tensor([ev["start"].elapsed_time(ev["decode"]), ev["start"].elapsed_time(ev["prefill"]),
+                          ev["prefill"].elapsed_time(ev["decode"])], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(times, op=torch.distributed.ReduceOp.MAX)
+    total_ms, prefill_ms, decode_ms = times.tolist()
+    stats = get_cache_stats(model)
+    if rank == 0:
+        tokens = world * B * NEW
+        line = {
+            "metric": "config4 end-to-end greedy tokens/s (prefill + decode) through patch_unsloth_attention",
+            "value": tokens / (total_ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": NEW, "warmup": 1,
+            "ms_per_step": decode_ms / max(NEW - 1, 1), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16 weights, activations and cache tiers; INT8 cold-tier codes",
+            "data": "synthetic (random-init weights, uniform random prompt ids)",
+            "config": {"workload": "config4: random-init Mistral-7B shape, batch 8, 4096-token prompt, 512 greedy "
+                                   "tokens, spectral cache k=16 / 512-token blocks / 64 hot",
+                       "parallelism": f"batch replicas x{world}" if world > 1 else "single GPU",
+                       "global_batch": world * B, "seq_len": T + NEW},
+            "prefill_ms": prefill_ms, "decode_ms": decode_ms,
+            "decode_tokens_per_s": world * B * (NEW - 1) / (decode_ms / 1e3),
+            "e2e": {"value": tokens / (total_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": B * 8},
+            "cache_stats": {k: v for k, v in stats.items() if k != "per_layer_stats"},
+            "first_tokens": out_host[0, :8].tolist(), "setup_s": setup_s, "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier(device_ids=[local])
+        torch.distributed.destroy_process_group()
 
 
 def run_ours(args, c):
@@ -616,37 +844,17 @@ def run_ours(args, c):
     if gather is not None:
         par["gather_equal"] = bool(flags[1].item() == 0.0)
 
-    # ---- rSVD blocks/s, config 3's largest batch (4096 blocks, k=32, q=2, p=8)
-    nb_rs = 4096 // world
-    g = torch.Generator(device=dev).manual_seed(3)
-    Mrs = (torch.randn(nb_rs, 512, 48, generator=g, device=dev) * (0.9 ** torch.arange(48, device=dev))) @ \
-        torch.randn(nb_rs, 48, 128, generator=g, device=dev)
-    Mrs = (Mrs + 0.05 * torch.randn(nb_rs, 512, 128, generator=g, device=dev)).half()
-    om = torch.randn(nb_rs, 128, 40, generator=g, device=dev)
-    for _ in range(2):
-        U, S, Vh = _ops.rsvd(Mrs, om, 32, 2, want_factors=True)
-    barrier()
-    ev6, ev7 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 3
-    ev6.record(stream)
-    for _ in range(reps):
-        _ops.rsvd(Mrs, om, 32, 2, want_factors=True)
-    ev7.record(stream)
-    barrier()
-    rs_ms = torch.tensor([ev6.elapsed_time(ev7) / reps], dtype=torch.float64, device=dev)
-    if world > 1:
-        torch.distributed.all_reduce(rs_ms, op=torch.distributed.ReduceOp.MAX)
-    rs_ms = rs_ms.item()
-    Mf = Mrs.float()
-    rs_err = float((torch.linalg.norm(Mf - (U * S[:, None, :]) @ Vh, dim=(1, 2))
-                    / torch.linalg.norm(Mf, dim=(1, 2))).mean())
-    del Mf, Mrs, om, U, S, Vh
+    # ---- config 3 (rSVD + INT8 sweep; headline point 4096 blocks, k=32, q=2) and, on one
+    #      GPU, config 1 (decode + per-step block compression)
+    peak, peak_tc, peak_kind = read_peaks()
+    sweep = rsvd_sweep(dev, world, stream, barrier, (peak, peak_tc))
+    head = next(r for r in sweep if (r["blocks"], r["k"], r["n_iter"]) == (4096, 32, 2))
+    cfg1 = run_config1(args, dev, stream, barrier) if world == 1 and not args.no_config1 else None
 
     if rank == 0:
         tokens = B * args.steps
         value = tokens / (dev_ms / 1e3)
         e2e = tokens / (e2e_ms / 1e3)
-        peak, _, peak_kind = read_peaks()
         bytes_launch = algorithmic_bytes_per_step(c, Hl)
         achieved = bytes_launch / (kern_ms / 1e3) / 1e9
         traffic, traffic_cmd = measured_traffic(c, world)
@@ -669,8 +877,10 @@ def run_ours(args, c):
                          "kernel": f"spx_decode_attn ({PATH_NAMES[path]} cold tier + hot/merge)",
                          "algorithmic_bytes_per_launch": bytes_launch, "launch_ms": kern_ms},
             "parity": par,
-            "rsvd": {"blocks_per_s": nb_rs * world / (rs_ms / 1e3), "blocks": 4096, "k": 32, "n_iter": 2,
-                     "oversampling": 8, "ms": rs_ms, "mean_rel_error": rs_err},
+            "rsvd": dict(head, outputs="INT8 codes + scale + FP16 basis (the cache's compression call)"),
+            "rsvd_sweep": [{k: v for k, v in r.items() if k != "roofline"} | {"frac": r["roofline"]["frac"]}
+                           for r in sweep],
+            "config1": cfg1,
             "cpu_baseline": None,
             "clocks": clk.summary(),
             "gpu_launches": DECODE_LAUNCHES * args.steps,
@@ -687,6 +897,8 @@ def run_ours(args, c):
             gather.close()
         torch.distributed.barrier(device_ids=[local])
         torch.distributed.destroy_process_group()
+    if cfg1 is not None and not cfg1["parity"]["passed"]:
+        raise SystemExit(f"config-1 parity failed: {cfg1['parity']['cos_min']:.6f}")
     if not par["passed"]:
         raise SystemExit(f"parity failed: cos_min={par['cos_min']:.6f} max_abs={par['max_abs']:.3e}")
 
@@ -713,6 +925,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-rsvd", action="store_true", help="reference arm: skip the rSVD sample")
+    ap.add_argument("--no-config1", action="store_true", help="skip the config-1 decode + compression leg")
+    ap.add_argument("--workload", default="config2", choices=["config2", "config4"],
+                    help="config2: the decode benchmark (default); config4: the end-to-end model loop")
+    ap.add_argument("--new-tokens", type=int, default=512, help="config4: greedy tokens per sequence")
     ap.add_argument("--layers", type=int, default=None, help="override the layer count (profiling only)")
     args = ap.parse_args()
     c = dict(CFG)
@@ -722,6 +938,8 @@ def main():
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     if args.impl == "reference":
         run_reference(args, c)
+    elif args.workload == "config4":
+        run_config4(args)
     else:
         run_ours(args, c)
 

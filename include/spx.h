@@ -51,7 +51,7 @@
 extern "C" {
 #endif
 
-#define SPX_ABI_VERSION 2
+#define SPX_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define SPX_API __attribute__((visibility("default")))
@@ -126,9 +126,10 @@ typedef struct spx_decode_args {
   const float* rope_freq;  /* optional HOST pointer to head_dim/2 floats: the RoPE frequencies
                               theta_i such that the first-half table entries are
                               cos/sin(position * theta_i) (times one common magnitude, if any).
-                              With it (and tied tables in ABSOLUTE mode) the cold tier runs the
-                              projection kernel; NULL keeps the reconstruct kernel.  Read during
-                              the call only. */
+                              With it (tied tables or DISTANCE mode) the projection kernel can
+                              run the cold tier, selected by the environment variable
+                              SPX_DECODE_PATH=proj; the reconstruct kernel is the default.  Read
+                              during the call only. */
 } spx_decode_args;
 
 SPX_API size_t spx_decode_workspace_size(const spx_decode_args* args);
@@ -160,6 +161,46 @@ SPX_API int spx_decode_path(const spx_decode_args* args);
  * GPU work overlaps (other streams, other host threads) race: serialise them. */
 #define SPX_NOALLOC_SCRATCH_BYTES (64u << 20)
 SPX_API int spx_decode_attn_noalloc(const spx_decode_args* args, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Multi-query (prefill) attention over the compressed cache.  Replaces the dense path of
+ * integration.py:292-346 (get_kv at spectral_cache.py:557-612, RoPE of the keys at their
+ * cached positions with the first half of the tables, softmax(Q K^T * scale + mask) V)
+ * without materialising K, V or the scores: key and value tiles are rebuilt from the
+ * codes and bases inside the kernel.  Keys are in cache order (cold blocks, then hot).
+ * Same cache layout and pointers as spx_decode_args; head_dim 128, f16 or bf16,
+ * n_rep in {1,2,4,8}, block_size a multiple of 64, ranks 16..64.
+ * ------------------------------------------------------------------------------- */
+typedef struct spx_prefill_args {
+  int32_t batch, num_q_heads, num_kv_heads, head_dim;
+  int32_t q_len;           /* queries per sequence */
+  int32_t block_size, num_blocks, block_capacity, rank_k, rank_v, hot_len, hot_capacity;
+  int32_t dtype;           /* spx_dtype of q, bases, hot tier and out */
+  int32_t rope_len;        /* rows of the cos/sin tables (positions are clamped into range) */
+  int32_t causal;          /* 1: a key whose position exceeds the query's position is masked */
+  int32_t mask_dtype;      /* SPX_F32 or dtype: element type of mask */
+  float scale;             /* softmax scale */
+  const void* q;           /* dtype [B][H_q][q_len][D], RoPE already applied */
+  const int64_t* q_pos;    /* [q_len] query positions (shared by the batch) */
+  const int8_t* codes_k;   /* as spx_decode_args, without the layer dimension */
+  const int8_t* codes_v;
+  const float* scale_k;
+  const float* scale_v;
+  const void* basis_k;
+  const void* basis_v;
+  const int64_t* block_pos;
+  const void* hot_k;
+  const void* hot_v;
+  const int64_t* hot_pos;
+  const float* cos_table;  /* f32 [rope_len][D] */
+  const float* sin_table;
+  const void* mask;        /* optional additive mask: element (b, h, i, j), j over keys in cache
+                              order, at b*mask_stride_b + h*mask_stride_h + i*mask_stride_q + j */
+  int64_t mask_stride_b, mask_stride_h, mask_stride_q;
+  void* out;               /* dtype [B][H_q][q_len][D] */
+} spx_prefill_args;
+
+SPX_API int spx_prefill_attn(const spx_prefill_args* args, void* stream);
 
 /* ---------------------------------------------------------------------------------
  * Batched randomized SVD + block compression.  Replaces rsvd.py:28-157 and

@@ -33,6 +33,7 @@ def test_library_loads_and_exports_every_declared_symbol():
 
 STRUCTS = {
     "spx_decode_args": N.DecodeArgs,
+    "spx_prefill_args": N.PrefillArgs,
     "spx_rsvd_args": N.RsvdArgs,
     "spx_quant_args": N.QuantArgs,
     "spx_reconstruct_args": N.ReconstructArgs,

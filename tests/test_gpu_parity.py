@@ -376,6 +376,41 @@ def test_rsvd_many_blocks(nb, m, dtype):
     assert np.abs(err - err64).max() <= 1e-3, (err, err64)
 
 
+@pytest.mark.parametrize("m,k,q,dtype", [(512, 32, 2, torch.float16), (512, 16, 2, torch.bfloat16),
+                                         (384, 32, 1, torch.float16), (256, 16, 0, torch.float16),
+                                         (128, 32, 2, torch.bfloat16), (512, 32, 0, torch.bfloat16)])
+def test_rsvd_fused_kernel_matches_chain(monkeypatch, m, k, q, dtype):
+    """The fused subspace iteration (one CTA per block, M resident in shared memory, the
+    panels in tensor memory) against the multi-kernel chain on the same inputs: the same
+    products, pass rules and pivots, so singular values agree to float32 rounding and
+    the reconstructions to 1e-4; both match the float64 reference algorithm's error
+    within 1e-3.  300 blocks: more than two waves of one CTA per SM."""
+    from unsloth_spectral import _ops
+    g = torch.Generator().manual_seed(40 + m + k + q)
+    nb = 300
+    sig = 0.9 ** torch.arange(48, dtype=torch.float32)
+    M16 = ((torch.randn(nb, m, 48, generator=g) * sig) @ torch.randn(nb, 48, 128, generator=g)
+           + 0.01 * torch.randn(nb, m, 128, generator=g)).to(dtype)
+    Omega = torch.randn(nb, 128, k + 8, generator=g)
+    monkeypatch.setenv("SPX_RSVD_PATH", "fused")
+    U, S, Vh = _ops.rsvd(M16.cuda(), Omega.cuda(), k, q)
+    monkeypatch.setenv("SPX_RSVD_PATH", "chain")
+    Uc, Sc, Vhc = _ops.rsvd(M16.cuda(), Omega.cuda(), k, q)
+    monkeypatch.delenv("SPX_RSVD_PATH")
+    assert torch.isfinite(S).all() and torch.isfinite(U).all() and torch.isfinite(Vh).all()
+    torch.testing.assert_close(S, Sc, rtol=1e-4, atol=1e-5 * Sc[:, :1].max().item())
+    R = (U * S[:, None, :]) @ Vh
+    Rc = (Uc * Sc[:, None, :]) @ Vhc
+    rel = (R - Rc).norm(dim=(1, 2)) / Rc.norm(dim=(1, 2))
+    assert rel.max().item() <= 1e-4, rel.max().item()
+    idx = [0, 1, 147, 148, 149, 295, 296, nb - 1]
+    Mf = M16[idx].float().numpy()
+    err = so.relative_reconstruction_error(Mf, U[idx].cpu().numpy(), S[idx].cpu().numpy(), Vh[idx].cpu().numpy())
+    U64, S64, Vh64 = so.batched_randomized_svd(Mf, k, q, 8, Omega[idx].numpy())
+    err64 = so.relative_reconstruction_error(Mf, U64, S64, Vh64)
+    assert np.abs(err - err64).max() <= 1e-3, (err, err64)
+
+
 def test_rsvd_zero_block():
     """An all-zero block compresses to zero singular values and zero codes, no NaN."""
     from unsloth_spectral import _ops

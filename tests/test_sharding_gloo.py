@@ -101,3 +101,18 @@ def test_bench_shard_byte_accounting():
     for world in (2, 4, 8):
         assert bench.algorithmic_bytes_per_step(c, c["kv_heads"] // world) * world == total
     assert abs(total - 26.06e9) < 0.01e9
+
+
+def test_bench_rsvd_sweep_grid_and_roofline():
+    """The config-3 sweep covers Nb {8, 128, 4096} x k {16, 32} x q {0, 2}, every Nb
+    splits evenly over 1/2/4/8 ranks, and the rSVD roofline counts the algorithmic bytes
+    (M read, sketch read, INT8 codes + FP16 basis + scale written) and product FLOPs."""
+    import bench
+    assert sorted(bench.SWEEP) == sorted((nb, k, q) for nb in (8, 128, 4096) for k in (16, 32) for q in (0, 2))
+    assert all(nb % w == 0 for nb, _, _ in bench.SWEEP for w in (1, 2, 4, 8))
+    r = bench.rsvd_roofline(4096, 32, 2, 1.0, (6502.2, 1658.6))
+    per_block = 512 * 128 * 2 + 128 * 40 * 4 + 512 * 32 + 32 * 128 * 2 + 4
+    assert r["algorithmic_bytes"] == 4096 * per_block
+    assert r["product_flops"] == 4096 * 2.0 * 512 * 128 * 40 * 6
+    assert abs(r["achieved"] - 4096 * per_block / 1e-3 / 1e9) < 1e-6
+    assert r["bound"] == "hbm" and abs(r["frac"] - r["achieved"] / 6502.2) < 1e-12

@@ -13,6 +13,8 @@
 // the final basis (as stable as Householder QR for these panels), one for intermediate
 // bases unless their conditioning asks for more.
 #include <math.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include <algorithm>
 
@@ -127,33 +129,6 @@ __global__ void __launch_bounds__(256) gemm_mty_kernel(const T* __restrict__ M, 
   }
 }
 
-// 1 / sqrt(x) for a positive finite float64 x, to float32 accuracy (it only scales the
-// float32 copy of L): x is scaled by an even power of two into [1, 4), the rsqrtf value
-// of that is refined by one Newton-Raphson step y <- y (3 - m y^2) / 2 and the power of
-// two put back.  Subnormal x takes the library path.
-__device__ __forceinline__ float rsqrt_pos_f(double x) {
-  if (x < 2.2250738585072014e-308) return (float)(1.0 / sqrt(x));
-  const int e = ((__double2hiint(x) >> 20) & 0x7ff) - 1023;
-  const int k = e >> 1;   // floor(e / 2)
-  const float m = (float)(x * __hiloint2double((1023 - 2 * k) << 20, 0));
-  float y = rsqrtf(m);
-  y = y * fmaf(-0.5f * m * y, y, 1.5f);
-  return (float)((double)y * __hiloint2double((1023 - k) << 20, 0));
-}
-
-// 1 / x for a positive finite float64 x: x = m 2^e with m in [1, 2), the float32
-// reciprocal of m refined by one Newton-Raphson step y <- y + y (1 - m y) (relative
-// error ~6e-8 -> ~4e-15, far below the float32 result the factor feeds), times 2^-e.
-// Subnormal or huge x takes the library path.
-__device__ __forceinline__ double recip_pos(double x) {
-  const int e = ((__double2hiint(x) >> 20) & 0x7ff) - 1023;
-  if (e <= -1023 || e >= 1023) return 1.0 / x;
-  const double s = __hiloint2double((1023 - e) << 20, 0);   // 2^-e
-  const double m = x * s;
-  double y = (double)__frcp_rn((float)m);
-  y = fma(y, fma(-m, y, 1.0), y);
-  return y * s;
-}
 
 // ------------------------------------- Cholesky-QR orthonormalisation, three kernels
 // X: f32 [rows][r] per matrix, orthonormalised in place.  Each pass forms the Gram
@@ -182,11 +157,6 @@ constexpr int kGramChunk = 128;
 // a fixed order, so the result is deterministic.  The chunk's row pitch P covers every
 // column a tile reads (columns r .. 4 NB4 - 1 are zero), so the inner loop has no bounds
 // tests.  The last pair of an odd row of tiles computes a dummy second tile, not stored.
-__host__ __device__ constexpr int gram_npair(int nb4) {
-  int n = 0;
-  for (int ta = 0; ta < nb4; ++ta) n += (nb4 - ta + 1) / 2;
-  return n;
-}
 template <int RMAX>
 struct GramTiling {
   static constexpr int NB4 = (RMAX + 3) / 4;
@@ -992,16 +962,32 @@ static int run_chain(const spx_rsvd_args* a, const RsvdWs& w, cudaStream_t st) {
     if (tc) rsvd_tc_gemm(1, a->in_dtype, M, ms, Y, Z, Nb, m, r, st);
     else gemm_mty_kernel<T><<<gmty, 256, 0, st>>>(M, ms, Y, Z, m, n, r);
   };
-  mx(a->omega, w.Y);
-  orth(w.Y, m, a->n_iter == 0 ? 2 : 1);
-  for (int it = 0; it < a->n_iter; ++it) {
+  // Two implementations of the same sequence and pass rules: the fused kernel
+  // (spx_rsvd_fused.cu: one CTA per matrix, everything on chip, one CTA per SM) and the
+  // multi-kernel chain below (each step a grid of its own, several CTAs per SM hiding the
+  // latency of the small dense steps).  Measured on B200 (k 16/32, q 0/2): the fused
+  // kernel is 1.3-2.2x faster up to about 3.5 waves of matrices, level at 512-1024, slower
+  // beyond; SPX_RSVD_PATH=fused|chain forces one.
+  const char* path = getenv("SPX_RSVD_PATH");
+  const bool can_fuse = rsvd_fused_supported(a->in_dtype, a->M, ms, a->omega, m, n, r);
+  bool fused = can_fuse && 2 * (int64_t)Nb <= 7 * (int64_t)nsm;
+  if (path && strcmp(path, "fused") == 0) fused = can_fuse;
+  if (path && strcmp(path, "chain") == 0) fused = false;
+  int rc = SPX_OK;
+  if (fused) {
+    rc = rsvd_fused(a->in_dtype, a->M, ms, a->omega, w.Y, w.Z, Nb, m, r, a->n_iter, st);
+  } else {
+    mx(a->omega, w.Y);
+    orth(w.Y, m, a->n_iter == 0 ? 2 : 1);
+    for (int it = 0; it < a->n_iter; ++it) {
+      mty(w.Y, w.Z);
+      orth(w.Z, n, 1);
+      mx(w.Z, w.Y);
+      orth(w.Y, m, it == a->n_iter - 1 ? 2 : 1);
+    }
     mty(w.Y, w.Z);
-    orth(w.Z, n, 1);
-    mx(w.Z, w.Y);
-    orth(w.Y, m, it == a->n_iter - 1 ? 2 : 1);
+    rc = launch_status("rsvd gemm/orth chain");
   }
-  mty(w.Y, w.Z);
-  int rc = launch_status("rsvd gemm/orth chain");
   if (rc != SPX_OK) return rc;
   const size_t ssvd = small_svd_smem(n, r);
   cudaFuncSetAttribute(small_svd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssvd);

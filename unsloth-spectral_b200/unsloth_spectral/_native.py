@@ -83,6 +83,16 @@ class BlockValueArgs(C.Structure):
         (n, C.c_void_p) for n in ("attn", "coeffs", "basis", "out")]
 
 
+class PrefillArgs(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in (
+        "batch", "num_q_heads", "num_kv_heads", "head_dim", "q_len", "block_size", "num_blocks", "block_capacity",
+        "rank_k", "rank_v", "hot_len", "hot_capacity", "dtype", "rope_len", "causal", "mask_dtype")] + [
+        ("scale", C.c_float)] + [(n, C.c_void_p) for n in (
+            "q", "q_pos", "codes_k", "codes_v", "scale_k", "scale_v", "basis_k", "basis_v", "block_pos", "hot_k",
+            "hot_v", "hot_pos", "cos_table", "sin_table", "mask")] + [
+        (n, C.c_int64) for n in ("mask_stride_b", "mask_stride_h", "mask_stride_q")] + [("out", C.c_void_p)]
+
+
 EXPORTS = {
     "spx_decode_workspace_size": (C.c_size_t, [C.POINTER(DecodeArgs)]),
     "spx_decode_attn": (C.c_int, [C.POINTER(DecodeArgs), C.c_void_p]),
@@ -94,13 +104,14 @@ EXPORTS = {
     "spx_reconstruct": (C.c_int, [C.POINTER(ReconstructArgs), C.c_void_p]),
     "spx_block_scores": (C.c_int, [C.POINTER(BlockScoreArgs), C.c_void_p]),
     "spx_block_values": (C.c_int, [C.POINTER(BlockValueArgs), C.c_void_p]),
+    "spx_prefill_attn": (C.c_int, [C.POINTER(PrefillArgs), C.c_void_p]),
     "spx_abi_version": (C.c_int, []),
     "spx_status_string": (C.c_char_p, [C.c_int]),
     "spx_last_error": (C.c_char_p, []),
     "spx_check_device": (C.c_int, []),
 }
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 _lib = None
 _load_error = None
 _device_ok = {}

@@ -224,6 +224,68 @@ def decode(q: torch.Tensor, tiers, cos: torch.Tensor, sin: torch.Tensor, query_p
     return out
 
 
+def prefill_supported(q: torch.Tensor, tiers) -> bool:
+    """Shapes ``spx_prefill_attn`` covers: head_dim 128, f16/bf16, n_rep in {1,2,4,8},
+    blocks a multiple of 64 tokens, stored ranks up to 64."""
+    t = tiers
+    if t is None or q.dim() != 4 or q.shape[-1] != 128 or t.dtype not in (torch.float16, torch.bfloat16):
+        return False
+    if q.dtype != t.dtype or q.shape[1] % t.num_heads or q.shape[1] // t.num_heads not in (1, 2, 4, 8):
+        return False
+    if t.num_blocks and (t.block_size % 64 or t.rank_k_pad > 64 or t.rank_v_pad > 64):
+        return False
+    return t.num_blocks > 0 or t.hot_len > 0
+
+
+def prefill(q: torch.Tensor, tiers, cos: torch.Tensor, sin: torch.Tensor, q_pos: torch.Tensor, *,
+            mask: Optional[torch.Tensor] = None, causal: bool = False, scale: Optional[float] = None) -> torch.Tensor:
+    """``softmax(Q K^T * scale + mask) V`` over the compressed cache by ``spx_prefill_attn``
+    (keys rebuilt from codes and bases, rotated at their cached positions inside the
+    kernel).  ``q`` ``[B, H_q, T_q, D]`` (RoPE applied), ``q_pos`` ``[T_q]`` int64 positions,
+    ``mask`` an optional additive mask broadcastable to ``[B, H_q, T_q, T_keys]`` over the
+    keys in cache order; ``causal`` masks keys past each query's position.  Returns
+    ``[B, H_q, T_q, D]`` in the cache dtype."""
+    dev = q.device
+    lib = N.lib_for(dev)
+    t = tiers
+    B, Hq, Tq, D = q.shape
+    q = q.contiguous()
+    cos32 = rope_table_f32(cos, dev)
+    sin32 = rope_table_f32(sin, dev)
+    qp = q_pos.reshape(-1).to(device=dev, dtype=torch.int64).contiguous()
+    if qp.numel() != Tq:
+        raise ValueError(f"q_pos has {qp.numel()} positions for {Tq} queries")
+    out = torch.empty(B, Hq, Tq, D, dtype=t.dtype, device=dev)
+    mk, mdt, strides = None, N.SPX_F32, (0, 0, 0)
+    if mask is not None:
+        T_total = t.num_blocks * t.block_size + t.hot_len
+        if mask.shape[-1] != T_total:
+            raise ValueError(f"attention_mask covers {mask.shape[-1]} keys, cache holds {T_total}")
+        mk = mask.to(dev)
+        if mk.dtype not in (torch.float32, t.dtype):
+            mk = mk.float()
+        while mk.dim() < 4:
+            mk = mk.unsqueeze(0)
+        mk = mk.expand(B, Hq, Tq, T_total)
+        if mk.stride(-1) != 1:
+            mk = mk.contiguous()
+        mdt = N.SPX_F32 if mk.dtype == torch.float32 else N.dtype_code(mk.dtype)
+        strides = (mk.stride(0), mk.stride(1), mk.stride(2))
+    a = N.PrefillArgs(
+        batch=B, num_q_heads=Hq, num_kv_heads=t.num_heads, head_dim=D, q_len=Tq, block_size=t.block_size,
+        num_blocks=t.num_blocks, block_capacity=t.block_capacity, rank_k=t.rank_k_pad, rank_v=t.rank_v_pad,
+        hot_len=t.hot_len, hot_capacity=t.hot_capacity, dtype=N.dtype_code(t.dtype), rope_len=cos32.shape[0],
+        causal=int(bool(causal)), mask_dtype=mdt, scale=float(1.0 / math.sqrt(D) if scale is None else scale),
+        q=N.ptr(q), q_pos=N.ptr(qp), codes_k=N.ptr(t.codes_k), codes_v=N.ptr(t.codes_v), scale_k=N.ptr(t.scale_k),
+        scale_v=N.ptr(t.scale_v), basis_k=N.ptr(t.basis_k), basis_v=N.ptr(t.basis_v), block_pos=N.ptr(t.block_pos),
+        hot_k=N.ptr(t.hot_k), hot_v=N.ptr(t.hot_v), hot_pos=N.ptr(t.hot_pos), cos_table=N.ptr(cos32),
+        sin_table=N.ptr(sin32), mask=N.ptr(mk), mask_stride_b=strides[0], mask_stride_h=strides[1],
+        mask_stride_q=strides[2], out=N.ptr(out))
+    N.check(lib, lib.spx_prefill_attn(a, N.stream_handle(dev)), "spx_prefill_attn")
+    del mk, qp, cos32, sin32
+    return out
+
+
 def reconstruct(codes, scale, basis, *, batch, num_heads, head_dim, block_size, num_blocks, block_capacity, rank,
                 rank_major, out, out_tokens):
     lib = N.lib_for(out.device)

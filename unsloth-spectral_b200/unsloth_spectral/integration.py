@@ -23,6 +23,7 @@ from typing import Optional, Tuple
 import torch
 import torch.nn.functional as F
 
+from . import _ops
 from .spectral_attention import apply_rope, spectral_attention_forward
 from .spectral_cache import SpectralCache
 
@@ -92,9 +93,34 @@ def rope_tables_for(self, seq_len: int, device) -> Tuple[torch.Tensor, torch.Ten
     return tabs
 
 
-def _dense_attention(q, cache: SpectralCache, cos, sin, n_rep, head_dim, attention_mask, dtype):
-    """Reconstruct K/V, RoPE the keys at their positions, dense softmax attention
-    (integration.py:292-346, the prefill / short-context path)."""
+def _mask_is_causal(mask: torch.Tensor, q_pos: torch.Tensor, k_pos: torch.Tensor) -> bool:
+    """True when the additive ``mask`` (broadcastable to ``[.., T_q, T_k]``) is 0 where the
+    key position is at most the query position and effectively -inf (<= -1e4) where it is
+    larger: adding it then equals the causal rule.  One device read (prefill only)."""
+    if mask.shape[-2] != q_pos.numel() or mask.shape[-1] != k_pos.numel():
+        return False
+    future = k_pos.reshape(1, -1) > q_pos.reshape(-1, 1)
+    m = mask.float()
+    ok = torch.where(future, m <= -1e4, m == 0).all()
+    return bool(ok.item())
+
+
+def _dense_attention(q, cache: SpectralCache, cos, sin, n_rep, head_dim, attention_mask, dtype, q_pos=None):
+    """Attention of a multi-token query over the whole cache (integration.py:292-346, the
+    prefill / short-context path): softmax(Q RoPE(K)^T / sqrt(D) + mask) V with the keys
+    rotated at their cached positions.  Runs ``spx_prefill_attn`` (K and V rebuilt tile by
+    tile from the codes inside the kernel); a mask that is exactly the causal rule is
+    applied as that rule, so the kernel skips the future tiles.  Shapes the kernel does not
+    cover (head_dim != 128, float32 caches, n_rep > 8) reconstruct K/V and run the dense
+    product as the reference does."""
+    t = cache.tiers
+    if q_pos is not None and _ops.prefill_supported(q, t):
+        qp = q_pos.reshape(-1)[-q.shape[2]:].to(q.device)
+        causal = False
+        mask = attention_mask
+        if mask is not None and q.shape[2] > 1 and _mask_is_causal(mask, qp, cache.get_all_positions()):
+            causal, mask = True, None
+        return _ops.prefill(q, t, cos, sin, qp, mask=mask, causal=causal, scale=1.0 / math.sqrt(head_dim)).to(dtype)
     K, V = cache.get_kv()
     pos = cache.get_all_positions()
     K = apply_rope(K, cos[pos][None, None], sin[pos][None, None]).to(dtype)
@@ -141,7 +167,7 @@ def create_spectral_forward(original_forward, block_size: int = 512, k_rank_keys
             out = spectral_attention_forward(q, past_key_value, cos, sin, kv_seq_len - 1, attention_mask,
                                              1.0 / math.sqrt(hd))
         else:
-            out = _dense_attention(q, past_key_value, cos, sin, nh // nkv, hd, attention_mask, q.dtype)
+            out = _dense_attention(q, past_key_value, cos, sin, nh // nkv, hd, attention_mask, q.dtype, position_ids)
         out = out.transpose(1, 2).reshape(bsz, q_len, nh * hd)
         out = self.o_proj(out)
         if use_cache:
@@ -185,7 +211,8 @@ def create_spectral_forward_inference(block_size: int = 512, k_rank_keys: int = 
                 out = spectral_attention_forward(q, past_key_value, cos, sin, qpos, attention_mask,
                                                  1.0 / math.sqrt(hd))
         else:
-            out = _dense_attention(q, past_key_value, cos, sin, nh // nkv, hd, attention_mask, q.dtype)
+            out = _dense_attention(q, past_key_value, cos, sin, nh // nkv, hd, attention_mask, q.dtype,
+                                   torch.full((1,), qpos, dtype=torch.long, device=hidden_states.device))
         out = self.o_proj(out.transpose(1, 2).reshape(bsz, 1, nh * hd))
         return out, past_key_value
 

@@ -1,0 +1,183 @@
+"""In-repo Llama/Mistral-architecture decoder and greedy token loop driven through the
+patched attention layers -- the caller of the decode path without Unsloth.
+
+The reference runs inside Unsloth: ``patch_unsloth_attention`` replaces every layer's
+``self_attn.forward`` and Unsloth's ``LlamaAttention_fast_forward_inference``, and its
+rebuilt ``LlamaModel_fast_forward_inference`` (integration.py:808-878) walks the layers
+for one new token: RMSNorm, the single-token attention with the layer's
+``SpectralCache``, residual, RMSNorm, SwiGLU MLP, residual; final norm and LM head.
+This module is that loop for a model whose attention modules carry the attributes the
+patched forwards read (``config`` with head counts / ``head_dim`` / ``rope_theta``,
+``q_proj`` .. ``o_proj``):
+
+* prompt: ``self_attn.forward`` per layer (the patched prefill: pre-RoPE keys go into
+  the layer's cache, full blocks are compressed in one batched rSVD launch, attention
+  over the reconstructed cache with a causal mask);
+* each new token: ``self_attn._spx_inference`` per layer (the patched single-token
+  forward, routed to ``kernels.spectral_attention_decode``), greedy argmax.
+
+Weights are random (``N(0, std^2)``, the architecture only), created directly on the
+device.  ``MISTRAL_7B`` is the 32-layer, hidden-4096, 32/8-head, FFN-14336, vocab-32768,
+RoPE-theta-1e6 shape.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from types import SimpleNamespace
+from typing import List, Optional
+
+import torch
+import torch.nn.functional as F
+
+from .integration import patch_unsloth_attention
+
+
+@dataclass
+class LlamaShape:
+    layers: int = 32
+    hidden: int = 4096
+    heads: int = 32
+    kv_heads: int = 8
+    head_dim: int = 128
+    ffn: int = 14336
+    vocab: int = 32768
+    rope_theta: float = 1e6
+    eps: float = 1e-5
+
+
+MISTRAL_7B = LlamaShape()
+
+
+class RMSNorm(torch.nn.Module):
+    def __init__(self, dim: int, eps: float, device, dtype):
+        super().__init__()
+        self.weight = torch.nn.Parameter(torch.ones(dim, device=device, dtype=dtype))
+        self.eps = eps
+
+    def forward(self, x):
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)).to(x.dtype) * self.weight
+
+
+def _linear(i: int, o: int, device, dtype, std: float, gen) -> torch.nn.Linear:
+    lin = torch.nn.Linear(i, o, bias=False, device="meta")
+    lin.weight = torch.nn.Parameter(torch.empty(o, i, device=device, dtype=dtype).normal_(0.0, std, generator=gen))
+    return lin
+
+
+class Attention(torch.nn.Module):
+    """Projections and the config attributes of an HF Llama attention module; its
+    ``forward`` is replaced by ``patch_unsloth_attention``."""
+
+    def __init__(self, s: LlamaShape, device, dtype, std, gen):
+        super().__init__()
+        self.config = SimpleNamespace(num_attention_heads=s.heads, num_key_value_heads=s.kv_heads, head_dim=s.head_dim,
+                                      hidden_size=s.hidden, rope_theta=s.rope_theta)
+        self.head_dim = s.head_dim
+        self.q_proj = _linear(s.hidden, s.heads * s.head_dim, device, dtype, std, gen)
+        self.k_proj = _linear(s.hidden, s.kv_heads * s.head_dim, device, dtype, std, gen)
+        self.v_proj = _linear(s.hidden, s.kv_heads * s.head_dim, device, dtype, std, gen)
+        self.o_proj = _linear(s.heads * s.head_dim, s.hidden, device, dtype, std, gen)
+
+    def forward(self, *a, **k):  # pragma: no cover - replaced by the patch
+        raise RuntimeError("call patch_unsloth_attention(model) first")
+
+
+class MLP(torch.nn.Module):
+    def __init__(self, s: LlamaShape, device, dtype, std, gen):
+        super().__init__()
+        self.gate_proj = _linear(s.hidden, s.ffn, device, dtype, std, gen)
+        self.up_proj = _linear(s.hidden, s.ffn, device, dtype, std, gen)
+        self.down_proj = _linear(s.ffn, s.hidden, device, dtype, std, gen)
+
+    def forward(self, x):
+        return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))
+
+
+class DecoderLayer(torch.nn.Module):
+    def __init__(self, s: LlamaShape, device, dtype, std, gen):
+        super().__init__()
+        self.input_layernorm = RMSNorm(s.hidden, s.eps, device, dtype)
+        self.self_attn = Attention(s, device, dtype, std, gen)
+        self.post_attention_layernorm = RMSNorm(s.hidden, s.eps, device, dtype)
+        self.mlp = MLP(s, device, dtype, std, gen)
+
+
+class SpectralLlama(torch.nn.Module):
+    """``model.model.layers[i].self_attn`` as HF lays it out, so ``patch_unsloth_attention``
+    and ``get_cache_stats`` apply unchanged."""
+
+    def __init__(self, shape: LlamaShape = MISTRAL_7B, device="cuda", dtype=torch.bfloat16, std: float = 0.02,
+                 seed: int = 0):
+        super().__init__()
+        device = torch.device(device)
+        gen = torch.Generator(device=device).manual_seed(seed)
+        self.shape = shape
+        self.model = torch.nn.Module()
+        self.model.embed_tokens = torch.nn.Embedding(shape.vocab, shape.hidden, device="meta")
+        self.model.embed_tokens.weight = torch.nn.Parameter(
+            torch.empty(shape.vocab, shape.hidden, device=device, dtype=dtype).normal_(0.0, std, generator=gen))
+        self.model.layers = torch.nn.ModuleList(DecoderLayer(shape, device, dtype, std, gen)
+                                                for _ in range(shape.layers))
+        self.model.norm = RMSNorm(shape.hidden, shape.eps, device, dtype)
+        self.lm_head = _linear(shape.hidden, shape.vocab, device, dtype, std, gen)
+
+    def patch(self, **kw):
+        """``patch_unsloth_attention`` with this model (integration.py:728)."""
+        kw.setdefault("verbose", False)
+        return patch_unsloth_attention(self, **kw)
+
+    @torch.no_grad()
+    def prefill(self, input_ids: torch.Tensor):
+        """Run the prompt ``[B, T]`` through the patched ``forward`` of every layer (causal
+        mask); returns (logits of the last position ``[B, vocab]``, per-layer caches)."""
+        B, T = input_ids.shape
+        dev = input_ids.device
+        h = self.model.embed_tokens(input_ids)
+        pos = torch.arange(T, device=dev)[None]
+        mask = torch.full((T, T), float("-inf"), device=dev, dtype=h.dtype).triu_(1)[None, None]
+        caches: List = []
+        for layer in self.model.layers:
+            a, _, cache = layer.self_attn.forward(layer.input_layernorm(h), attention_mask=mask, position_ids=pos,
+                                                  past_key_value=None, use_cache=True)
+            caches.append(cache)
+            h = h + a
+            h = h + layer.mlp(layer.post_attention_layernorm(h))
+        return self.lm_head(self.model.norm(h[:, -1])), caches
+
+    @torch.no_grad()
+    def decode_step(self, token: torch.Tensor, position: torch.Tensor, caches: List):
+        """One new token ``[B]`` at device position ``position`` (``[1, 1]`` int64) through
+        the patched single-token forward of every layer; returns logits ``[B, vocab]``."""
+        h = self.model.embed_tokens(token[:, None])
+        for i, layer in enumerate(self.model.layers):
+            a, caches[i] = layer.self_attn._spx_inference(layer.input_layernorm(h), caches[i], position)
+            h = h + a
+            h = h + layer.mlp(layer.post_attention_layernorm(h))
+        return self.lm_head(self.model.norm(h[:, -1]))
+
+    @torch.no_grad()
+    def generate(self, input_ids: torch.Tensor, max_new_tokens: int, timer=None):
+        """Greedy decoding: the prompt, then ``max_new_tokens`` tokens, each the argmax of
+        the previous step's logits.  Positions stay on the device (no host reads inside
+        the loop).  ``timer(name)``, if given, is called after the prefill ("prefill")
+        and at the end ("decode").  Returns the new tokens ``[B, max_new_tokens]``."""
+        B, T = input_ids.shape
+        logits, caches = self.prefill(input_ids)
+        if timer is not None:
+            timer("prefill")
+        out = torch.empty(B, max_new_tokens, dtype=torch.long, device=input_ids.device)
+        tok = logits.argmax(-1)
+        pos = torch.full((1, 1), T, dtype=torch.long, device=input_ids.device)
+        for s in range(max_new_tokens):
+            out[:, s] = tok
+            if s + 1 == max_new_tokens:
+                break
+            logits = self.decode_step(tok, pos, caches)
+            tok = logits.argmax(-1)
+            pos += 1
+        if timer is not None:
+            timer("decode")
+        self._caches = caches
+        return out
