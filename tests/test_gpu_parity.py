@@ -587,6 +587,23 @@ def test_fast_kernel_matches_oracle_and_generic(case, mode, generic_path):
     generic_path(False)
 
 
+@pytest.mark.parametrize("case", [FAST_CASES[0], FAST_CASES[2], FAST_CASES[4]])
+@pytest.mark.parametrize("mode", ["forward", "decode"])
+def test_fast_kernel_bf16_cache(case, mode, generic_path):
+    """A BF16 cache runs the reconstruct kernel (bases and queries converted to FP16 where
+    they are staged) and matches the oracle over the same BF16 values, and the generic
+    FP32 kernel."""
+    r = _random_case(*case)
+    generic_path(False)
+    assert _path_of(r, torch.bfloat16, mode) == 1
+    fast, ref = _run_random(r, torch.bfloat16, mode)
+    _close(fast, ref)
+    generic_path(True)
+    gen, _ = _run_random(r, torch.bfloat16, mode)
+    _close(fast, gen)
+    generic_path(False)
+
+
 # (case, plan): plans drive several items and multi-block ranges through one CTA, the
 # way large workloads run (units per item, blocks per range, CTAs)
 PLAN_CASES = [

@@ -1,4 +1,7 @@
-// Fast cold-tier decode kernel for sm_100a (FP16 cache, D = 128, tied or distance RoPE).
+// Fast cold-tier decode kernel for sm_100a (FP16 or BF16 cache, D = 128, tied or distance
+// RoPE).  A BF16 cache has its bases and queries converted to FP16 where they are staged in
+// shared memory (key basis -> B tile, value basis -> padded rows, query fragments); the
+// arithmetic below is the same for both.
 //
 // Work decomposition.  A unit is one (layer, sequence, KV head); a unit-block is one unit
 // restricted to one cold block j.  The launch covers items = (group of G units) x (range
@@ -148,7 +151,20 @@ struct Cfg {
   static_assert(BYTES <= 227 * 1024, "shared memory");
 };
 
-template <int RK, int RV, int MT>
+// Eight 16-bit values of the input type -> eight f16 (bf16 input: exact for magnitudes the
+// f16 range holds; bases are orthonormal rows, queries are O(1)).
+template <bool BF>
+__device__ __forceinline__ uint32_t to_h2(uint32_t w) {
+  if (!BF) return w;
+  const float lo = __uint_as_float(w << 16), hi = __uint_as_float(w & 0xffff0000u);
+  return pack_f2(lo, hi);
+}
+template <bool BF>
+__device__ __forceinline__ uint4 to_h8(uint4 v) {
+  return BF ? make_uint4(to_h2<BF>(v.x), to_h2<BF>(v.y), to_h2<BF>(v.z), to_h2<BF>(v.w)) : v;
+}
+
+template <int RK, int RV, int MT, bool BF>
 __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items I) {
   using C = Cfg<RK, RV, MT>;
   extern __shared__ __align__(1024) uint8_t sm[];
@@ -278,7 +294,7 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
       {
         const uint4* src = reinterpret_cast<const uint4*>(st + C::B_BV);
         for (int e = et; e < RV * 16; e += NEP)
-          *reinterpret_cast<uint4*>(sm + C::OFF_BVP + (e >> 4) * C::QP + (e & 15) * 16) = src[e];
+          *reinterpret_cast<uint4*>(sm + C::OFF_BVP + (e >> 4) * C::QP + (e & 15) * 16) = to_h8<BF>(src[e]);
       }
       named_sync(BAR_EPI, NEP);
       // partials and stage s are consumed: hand them back, refill the stage
@@ -369,7 +385,7 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
               nc = a + 8 * (b >> 1);
               k = 8 * (b & 1) + ((a + W) & 7);
             }
-            dstb[nc * RK + k] = srcb[k * 16 + nc];
+            dstb[nc * RK + k] = to_h8<BF>(srcb[k * 16 + nc]);
           }
         }
         // key codes -> FP16 A tiles, one M-tile at a time
@@ -520,7 +536,10 @@ __global__ void __launch_bounds__(NT, 1) cold_fast_kernel(DecodeParams p, Items 
       uint2 qf[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k)
-        qf[k] = hl ? *reinterpret_cast<const uint2*>(st + C::B_Q + g * C::QP + 32 * k + 8 * t) : make_uint2(0u, 0u);
+      {
+        const uint2 v = hl ? *reinterpret_cast<const uint2*>(st + C::B_Q + g * C::QP + 32 * k + 8 * t) : make_uint2(0u, 0u);
+        qf[k] = make_uint2(to_h2<BF>(v.x), to_h2<BF>(v.y));
+      }
       // ---- scores: K~ from TMEM (next M-tile loading while this one computes) --------
       float sc[MT][4];
       uint32_t kr[2][32], ro[2][32];
@@ -694,16 +713,21 @@ int launch(DecodeParams p, cudaStream_t st) {
   rope_pack_kernel<<<rg, 128, 0, st>>>(p);
   int rc = launch_status("rope_pack_kernel");
   if (rc != SPX_OK) return rc;
-  cudaFuncSetAttribute(cold_fast_kernel<RK, RV, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::BYTES);
   const Items items{pl.G, pl.JR, pl.ngroups, pl.nitems, p.nblk, units};
-  cold_fast_kernel<RK, RV, MT><<<pl.grid, NT, C::BYTES, st>>>(p, items);
+  if (p.dtype == SPX_BF16) {
+    cudaFuncSetAttribute(cold_fast_kernel<RK, RV, MT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::BYTES);
+    cold_fast_kernel<RK, RV, MT, true><<<pl.grid, NT, C::BYTES, st>>>(p, items);
+  } else {
+    cudaFuncSetAttribute(cold_fast_kernel<RK, RV, MT, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::BYTES);
+    cold_fast_kernel<RK, RV, MT, false><<<pl.grid, NT, C::BYTES, st>>>(p, items);
+  }
   return launch_status("cold_fast_kernel");
 }
 
 }  // namespace fastk
 
 bool decode_fast_supported(const DecodeParams& p) {
-  if (p.nblk <= 0 || p.D != 128 || p.dtype != SPX_F16 || p.mask != nullptr) return false;
+  if (p.nblk <= 0 || p.D != 128 || (p.dtype != SPX_F16 && p.dtype != SPX_BF16) || p.mask != nullptr) return false;
   if (!(p.tied || p.mode == SPX_ROPE_DISTANCE)) return false;
   if (!(p.RK == 16 || p.RK == 32) || !(p.RV == 16 || p.RV == 32)) return false;
   if (!(p.Tb == 256 || p.Tb == 512)) return false;
