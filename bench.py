@@ -699,6 +699,82 @@ def run_config4(args):
         torch.distributed.destroy_process_group()
 
 
+# ---------------------------------------------------------------- kernel legs ------
+def run_prefill(args):
+    """The prefill attention kernel alone, one layer of config 4's prompt (batch 8, 32/8
+    heads, 4096 causal tokens over a k=16 cache of 8 blocks; --small: batch 2, 2048 tokens):
+    spx_prefill_attn with the causal rule, with the equivalent additive mask, and the eager
+    reconstruct-and-multiply path of the reference, timed with CUDA events."""
+    _use_ours()
+    from unsloth_spectral import SpectralCache, _ops, integration as I, synthetic as syn
+    dev = torch.device("cuda")
+    dtype = torch.bfloat16
+    B, H, nrep, T = (2, 8, 4, 2048) if args.small else (8, 8, 4, 4096)
+    K, V = syn.kv_layer_batched(1, 0, B, H, T, 128, 24, 0.85, dev, dtype=dtype)
+    cache = SpectralCache(H, 128, block_size=512, k_rank_keys=16, k_rank_values=16, device=dev, dtype=dtype)
+    cache.append(K, V, torch.arange(T, device=dev)[None])
+    del K, V
+    cos, sin = syn.rope_tables(T + 8, 128, 1e6, device=dev)
+    g = torch.Generator(device=dev).manual_seed(1)
+    q = (torch.randn(B, H * nrep, T, 128, generator=g, device=dev) / math.sqrt(128) * 4).to(dtype)
+    pos = torch.arange(T, device=dev)
+    mask = torch.full((T, T), float("-inf"), device=dev).triu_(1)[None, None].to(dtype)
+
+    def timed(fn, n):
+        for _ in range(max(args.warmup, 1)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    causal_ms = timed(lambda: _ops.prefill(q, cache.tiers, cos, sin, pos, causal=True), args.steps)
+    mask_ms = timed(lambda: _ops.prefill(q, cache.tiers, cos, sin, pos, mask=mask), args.steps)
+    eager_ms = None if args.small else timed(lambda: I._dense_attention(q, cache, cos, sin, nrep, 128, mask, dtype, None), 3)
+    flops = 4.0 * B * H * nrep * 128 * T * T / 2   # causal half of QK^T and PV
+    print(json.dumps({"metric": "prefill attention over the compressed cache, ms per layer", "value": causal_ms,
+                      "unit": "ms", "higher_is_better": False, "dtype": "bf16 (mma.sync, f32 accumulate)",
+                      "config": {"workload": f"B{B} x {H * nrep}/{H} heads x {T} causal tokens, k=16 cache"},
+                      "causal_tflops": flops / (causal_ms / 1e3) / 1e12, "additive_mask_ms": mask_ms,
+                      "eager_reference_path_ms": eager_ms}), flush=True)
+
+
+def run_rsvd(args):
+    """One spx_rsvd_compress configuration (config-3 blocks, INT8 outputs) for profiling:
+    --blocks, --k, --q; SPX_RSVD_PATH selects the implementation."""
+    _use_ours()
+    dev = torch.device("cuda")
+    from unsloth_spectral import _ops
+    nb, k, q = args.blocks, args.k, args.q
+    M = rsvd_blocks(nb, k, dev, 7)
+    om = torch.randn(nb, 128, k + 8, generator=torch.Generator(device=dev).manual_seed(5), device=dev)
+    codes = torch.empty(nb, 512, k, dtype=torch.int8, device=dev)
+    qs = torch.empty(nb, dtype=torch.float32, device=dev)
+    basis = torch.empty(nb, k, 128, dtype=torch.float16, device=dev)
+
+    def call():
+        _ops.rsvd(M, om, k, q, want_factors=False, codes=codes, codes_strides=(512 * k, k, 1), rank_pad=k,
+                  qscale=qs, scale_stride=1, basis=basis, basis_stride=k * 128)
+
+    for _ in range(max(args.warmup, 1)):
+        call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    print(json.dumps({"metric": "rSVD + INT8 blocks/s", "value": nb / (ms / 1e3), "unit": "blocks/s", "ms": ms,
+                      "config": {"blocks": nb, "k": k, "n_iter": q,
+                                 "path": os.environ.get("SPX_RSVD_PATH", "auto")}}), flush=True)
+
+
 def run_ours(args, c):
     _use_ours()
     from unsloth_spectral import _native as N, _ops
@@ -926,8 +1002,13 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-rsvd", action="store_true", help="reference arm: skip the rSVD sample")
     ap.add_argument("--no-config1", action="store_true", help="skip the config-1 decode + compression leg")
-    ap.add_argument("--workload", default="config2", choices=["config2", "config4"],
-                    help="config2: the decode benchmark (default); config4: the end-to-end model loop")
+    ap.add_argument("--workload", default="config2", choices=["config2", "config4", "prefill", "rsvd"],
+                    help="config2: the decode benchmark (default); config4: the end-to-end model loop; "
+                         "prefill / rsvd: one kernel leg (profiling)")
+    ap.add_argument("--small", action="store_true", help="prefill: the small profiling case")
+    ap.add_argument("--blocks", type=int, default=4096, help="rsvd: blocks per call")
+    ap.add_argument("--k", type=int, default=32, help="rsvd: rank")
+    ap.add_argument("--q", type=int, default=2, help="rsvd: power iterations")
     ap.add_argument("--new-tokens", type=int, default=512, help="config4: greedy tokens per sequence")
     ap.add_argument("--layers", type=int, default=None, help="override the layer count (profiling only)")
     args = ap.parse_args()
@@ -940,6 +1021,10 @@ def main():
         run_reference(args, c)
     elif args.workload == "config4":
         run_config4(args)
+    elif args.workload == "prefill":
+        run_prefill(args)
+    elif args.workload == "rsvd":
+        run_rsvd(args)
     else:
         run_ours(args, c)
 
