@@ -158,7 +158,9 @@ SPX_API int spx_decode_path(const spx_decode_args* args);
  * The first call on a device looks up the array's device address (cudaGetSymbolAddress,
  * with that device current); make that first call before any stream capture.  All calls
  * on a device share the one array and it keeps the last call's contents, so calls whose
- * GPU work overlaps (other streams, other host threads) race: serialise them. */
+ * GPU work overlaps (other streams, other host threads) race: serialise them.  The
+ * address is cached per device ordinal for the life of the process: a cudaDeviceReset,
+ * or a non-primary context created with the driver API, is not supported. */
 #define SPX_NOALLOC_SCRATCH_BYTES (64u << 20)
 SPX_API int spx_decode_attn_noalloc(const spx_decode_args* args, void* stream);
 
