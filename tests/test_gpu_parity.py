@@ -728,6 +728,26 @@ def test_proj_kernel_distance_mode_keys_past_the_query(decode_path):
     _close(proj, ref)
 
 
+@pytest.mark.parametrize("mode", ["decode", "forward"])
+def test_fast_kernel_headline_shape(decode_path, monkeypatch, mode):
+    """The reconstruct kernel (the default cold tier) at the timed configuration's
+    geometry: 64 blocks of 512 at k=32, n_rep 4, 64 hot tokens, the work plan of the full
+    run (32 units per item, 16-block ranges, so every CTA merges 16 blocks per unit in
+    its FP16-accumulator arithmetic), on a reduced batch (4 sequences x 8 KV heads);
+    against the float32 oracle and the generic FP32 kernel."""
+    r = _random_case(76, 4, 8, 4, 128, 512, 64, 32, 32, 64, False)
+    monkeypatch.setenv("SPX_FAST_PLAN", "32,16,4")
+    decode_path("fast")
+    assert _path_of(r, torch.float16, mode) == 1
+    fast, ref = _run_random(r, torch.float16, mode)
+    _close(fast, ref)
+    monkeypatch.delenv("SPX_FAST_PLAN")
+    decode_path("generic")
+    gen, _ = _run_random(r, torch.float16, mode)
+    decode_path(None)
+    _close(fast, gen)
+
+
 def test_proj_kernel_headline_shape(decode_path, monkeypatch):
     """The timed configuration's geometry (64 blocks of 512 at k=32, n_rep 4, 64 hot,
     the work plan of the full run: 32 units per item, 16-block ranges) on a reduced
