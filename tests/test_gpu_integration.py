@@ -158,3 +158,20 @@ def test_decode_step_with_device_positions_does_not_synchronise():
                 torch.cuda.set_sync_debug_mode("default")
         torch.cuda.synchronize()
         assert torch.isfinite(out).all()
+
+
+def test_get_kv_with_landmarks_on_a_compressed_cache():
+    """Landmarks first, then the reconstructed cold blocks and the hot tier, with their
+    positions (spectral_cache.py:808-852)."""
+    from unsloth_spectral import SpectralCache
+    from unsloth_spectral import synthetic as syn
+    dev = torch.device("cuda")
+    K, V = syn.kv_layer_batched(1, 3, 1, 4, 600, 128, 24, 0.85, dev)
+    c = SpectralCache(4, 128, block_size=512, k_rank_keys=16, k_rank_values=16, device=dev, dtype=torch.float16)
+    c.append(K, V, torch.arange(600, device=dev)[None])
+    lk, lv = K[:, :, :5].clone(), V[:, :, :5].clone()
+    c.add_landmarks(lk, lv, torch.arange(5, device=dev)[None])
+    Kw, Vw, P = c.get_kv_with_landmarks()
+    Kc, Vc = c.get_kv()
+    assert torch.equal(Kw, torch.cat([lk, Kc], 2)) and torch.equal(Vw, torch.cat([lv, Vc], 2))
+    assert P.shape == (1, 605) and P[0, :5].tolist() == list(range(5)) and P[0, 5:].tolist() == list(range(600))

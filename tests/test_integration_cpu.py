@@ -41,3 +41,35 @@ def test_llama_layout_matches_what_the_patch_walks():
     assert abs(float(attn.q_proj.weight.std()) - 0.02) < 0.005
     with pytest.raises(RuntimeError):
         attn(torch.zeros(1, 1, 64))
+
+
+def test_attention_importance_and_landmarks_follow_the_reference_rules():
+    """spectral_cache.py:710-852: the importance is an EMA (alpha 0.1) of the attention
+    averaged over batch, heads and queries, grown with zero padding; block weights are
+    slices of it; landmarks concatenate along the token axis and come first in
+    get_kv_with_landmarks."""
+    from unsloth_spectral import SpectralCache
+    off = SpectralCache(2, 16, block_size=4, device="cpu", dtype=torch.float32)
+    off.update_attention_importance(torch.rand(1, 2, 1, 8), 8)
+    assert off.attention_importance is None and off.get_block_attention_weights(0) is None
+    c = SpectralCache(2, 16, block_size=4, device="cpu", dtype=torch.float32, use_attention_weighted_svd=True)
+    a1 = torch.rand(2, 2, 1, 6)
+    c.update_attention_importance(a1, 6)
+    m1 = a1.mean(dim=(0, 1, 2))
+    assert torch.allclose(c.attention_importance, m1)
+    a2 = torch.rand(2, 2, 1, 9)
+    c.update_attention_importance(a2, 9)
+    m2 = a2.mean(dim=(0, 1, 2))
+    want = torch.cat([m1, torch.zeros(3)]) * 0.9 + 0.1 * m2
+    assert torch.allclose(c.attention_importance, want)
+    assert torch.allclose(c.get_block_attention_weights(1), want[4:8])
+    assert c.get_block_attention_weights(2) is None   # tokens 8..11 not all tracked
+    K1, V1 = torch.randn(1, 2, 3, 16), torch.randn(1, 2, 3, 16)
+    K2, V2 = torch.randn(1, 2, 2, 16), torch.randn(1, 2, 2, 16)
+    c.add_landmarks(K1, V1, torch.tensor([[0, 1, 2]]))
+    c.add_landmarks(K2, V2, torch.tensor([[7, 9]]))
+    K, V, P = c.get_kv_with_landmarks()
+    assert torch.equal(K, torch.cat([K1, K2], 2)) and torch.equal(V, torch.cat([V1, V2], 2))
+    assert P.tolist() == [[0, 1, 2, 7, 9]]
+    c.reset()
+    assert c.landmark_K is None and c.attention_importance is None and c.get_kv_with_landmarks() == (None, None, None)

@@ -15,8 +15,8 @@ Same constructor, attributes and methods as the reference's ``SpectralCache``
 ``cold_blocks``, ``hot_K``, ``hot_V`` and ``hot_position_ids`` remain available as
 reference-layout views (``cold_blocks`` dequantises on access).  Batch sizes above 1
 are supported; positions are shared by the batch (the reference reads row 0 too).
-The landmark / attention-weighted-SVD options are accepted but unimplemented, as in
-the reference, where no entry point calls them.
+Attention-importance tracking and landmark tokens keep the reference's behaviour as
+cache state; as in the reference, no entry point consumes them.
 """
 from __future__ import annotations
 
@@ -627,17 +627,68 @@ class SpectralCache:
         return (f"SpectralCache(tokens={self.total_tokens}, blocks={s['num_blocks']}, "
                 f"compression={s['compression_ratio']:.2f}x)")
 
-    # -- reference options with no entry point -------------------------------------------
-    def update_attention_importance(self, attention_weights, query_position):
+    # -- attention importance and landmark tokens (spectral_cache.py:706-852) ------------
+    # The reference keeps these as cache state that no entry point of its own consumes:
+    # nothing calls update_attention_importance, compression does not read the weights,
+    # and the attention paths read get_kv, not get_kv_with_landmarks.  They are kept with
+    # the same behaviour for callers that use them directly.
+    def update_attention_importance(self, attention_weights: torch.Tensor, query_position: int):
+        """Exponential moving average (alpha 0.1) of the attention ``[B, H, 1, T_kv]`` a
+        query paid to each cached token, averaged over batch, heads and queries; grows with
+        the cache (spectral_cache.py:710-750).  No-op unless use_attention_weighted_svd."""
         if not self.use_attention_weighted_svd:
             return
-        raise NotImplementedError("attention-weighted SVD is not implemented")
+        avg = attention_weights.mean(dim=(0, 1, 2))
+        if self.attention_importance is None:
+            self.attention_importance = avg.clone()
+            return
+        alpha = 0.1
+        if self.attention_importance.shape[0] < avg.shape[0]:
+            pad = torch.zeros(avg.shape[0] - self.attention_importance.shape[0], device=avg.device, dtype=avg.dtype)
+            self.attention_importance = torch.cat([self.attention_importance, pad])
+        n = avg.shape[0]
+        self.attention_importance[:n] = (1 - alpha) * self.attention_importance[:n] + alpha * avg
 
-    def get_block_attention_weights(self, block_idx):
-        return None
+    def get_block_attention_weights(self, block_idx: int) -> Optional[torch.Tensor]:
+        """Importance of the tokens of block ``block_idx`` ``[block_size]``, or None when
+        not tracked (or not yet covering the block) (spectral_cache.py:752-775)."""
+        if self.attention_importance is None:
+            return None
+        start = block_idx * self.block_size
+        end = start + self.block_size
+        if end > self.attention_importance.shape[0]:
+            return None
+        return self.attention_importance[start:end]
 
-    def add_landmarks(self, K, V, position_ids):
-        raise NotImplementedError("landmark tokens are not implemented")
+    def add_landmarks(self, K: torch.Tensor, V: torch.Tensor, position_ids: torch.Tensor):
+        """Keep tokens ``[B, H, T, D]`` uncompressed as landmarks (spectral_cache.py:781-806)."""
+        if self.landmark_K is None:
+            self.landmark_K, self.landmark_V = K.clone(), V.clone()
+            self.landmark_position_ids = position_ids.clone()
+        else:
+            self.landmark_K = torch.cat([self.landmark_K, K], dim=2)
+            self.landmark_V = torch.cat([self.landmark_V, V], dim=2)
+            self.landmark_position_ids = torch.cat([self.landmark_position_ids, position_ids], dim=1)
+        if self.debug_logging:
+            print(f"[SpectralCache] Added {K.shape[2]} landmark tokens; total {self.landmark_K.shape[2]}")
 
-    def get_kv_with_landmarks(self):
-        raise NotImplementedError("landmark tokens are not implemented")
+    def get_kv_with_landmarks(self) -> Tuple[Optional[torch.Tensor], Optional[torch.Tensor], Optional[torch.Tensor]]:
+        """Landmarks, then the cold blocks (reconstructed), then the hot tier:
+        ``(K [B, H, T, D], V, position_ids [B, T])`` (spectral_cache.py:808-852)."""
+        K, V = self.get_kv()
+        pos = self.get_all_positions()
+        Ks, Vs, Ps = [], [], []
+        if self.landmark_K is not None:
+            Ks.append(self.landmark_K)
+            Vs.append(self.landmark_V)
+            if self.landmark_position_ids is not None:
+                Ps.append(self.landmark_position_ids.to(pos.device if pos.numel() else self.landmark_K.device))
+        if K is not None:
+            Ks.append(K.to(self.landmark_K.dtype) if self.landmark_K is not None else K)
+            Vs.append(V.to(self.landmark_V.dtype) if self.landmark_V is not None else V)
+            Ps.append(pos[None].expand(K.shape[0], -1))
+        if not Ks:
+            return None, None, None
+        B = Ks[0].shape[0]
+        Ps = [p.expand(B, -1) if p.shape[0] == 1 else p for p in Ps]
+        return torch.cat(Ks, dim=2), torch.cat(Vs, dim=2), (torch.cat(Ps, dim=1) if Ps else None)
