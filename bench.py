@@ -660,19 +660,26 @@ def run_config4(args):
     stream = torch.cuda.current_stream(dev)
     model.generate(prompt, 4)   # warm-up: the same kernels, a short tail
     torch.cuda.synchronize(dev)
-    ev = {k: torch.cuda.Event(enable_timing=True) for k in ("start", "prefill", "decode")}
-    if world > 1:
-        torch.distributed.barrier(device_ids=[local])
-    with ClockSampler(local) as clk:
+
+    def run(graphs):
+        ev = {k: torch.cuda.Event(enable_timing=True) for k in ("start", "prefill", "decode")}
+        if world > 1:
+            torch.distributed.barrier(device_ids=[local])
+        torch.manual_seed(1000 + rank)   # the rSVD sketches: the same in both runs
         ev["start"].record(stream)
-        toks = model.generate(prompt, NEW, timer=lambda name: ev[name].record(stream))
-        out_host = toks.cpu()
-    torch.cuda.synchronize(dev)
-    times = torch.tensor([ev["start"].elapsed_time(ev["decode"]), ev["start"].elapsed_time(ev["prefill"]),
+        toks = model.generate(prompt, NEW, timer=lambda name: ev[name].record(stream), cuda_graphs=graphs)
+        host = toks.cpu()
+        torch.cuda.synchronize(dev)
+        t = torch.tensor([ev["start"].elapsed_time(ev["decode"]), ev["start"].elapsed_time(ev["prefill"]),
                           ev["prefill"].elapsed_time(ev["decode"])], dtype=torch.float64, device=dev)
-    if world > 1:
-        torch.distributed.all_reduce(times, op=torch.distributed.ReduceOp.MAX)
-    total_ms, prefill_ms, decode_ms = times.tolist()
+        if world > 1:
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return host, t.tolist()
+
+    eager_host, (eager_total, _, eager_decode) = run(False)
+    with ClockSampler(local) as clk:
+        out_host, (total_ms, prefill_ms, decode_ms) = run(True)
+    same = bool(torch.equal(eager_host, out_host))
     stats = get_cache_stats(model)
     if rank == 0:
         tokens = world * B * NEW
@@ -688,6 +695,10 @@ def run_config4(args):
                        "global_batch": world * B, "seq_len": T + NEW},
             "prefill_ms": prefill_ms, "decode_ms": decode_ms,
             "decode_tokens_per_s": world * B * (NEW - 1) / (decode_ms / 1e3),
+            "decode": "CUDA graph of the per-layer patched single-token step, replayed between block "
+                      "compressions (llama_loop._decode_graphed)",
+            "eager": {"tokens_per_s": tokens / (eager_total / 1e3), "decode_ms": eager_decode,
+                      "same_tokens_as_graphed": same},
             "e2e": {"value": tokens / (total_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": B * 8},
             "cache_stats": {k: v for k, v in stats.items() if k != "per_layer_stats"},

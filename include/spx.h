@@ -51,7 +51,7 @@
 extern "C" {
 #endif
 
-#define SPX_ABI_VERSION 3
+#define SPX_ABI_VERSION 4
 
 #if defined(__GNUC__)
 #define SPX_API __attribute__((visibility("default")))
@@ -130,6 +130,11 @@ typedef struct spx_decode_args {
                               run the cold tier, selected by the environment variable
                               SPX_DECODE_PATH=proj; the reconstruct kernel is the default.  Read
                               during the call only. */
+  const int32_t* hot_len_device;  /* optional DEVICE pointer: the hot tier holds
+                              min(*hot_len_device, hot_len) tokens, read by the kernels when
+                              they run; hot_len is then only the bound that sizes the launch.
+                              Lets a caller capture decode steps in a CUDA graph while the
+                              hot tier grows.  NULL: hot_len tokens. */
 } spx_decode_args;
 
 SPX_API size_t spx_decode_workspace_size(const spx_decode_args* args);

@@ -61,3 +61,27 @@ def test_decode_step_has_no_host_sync():
             torch.cuda.set_sync_debug_mode("default")
         torch.cuda.synchronize()
     assert torch.isfinite(logits.float()).all()
+
+
+def test_cuda_graph_decode_matches_eager():
+    """The decode loop replayed from CUDA graphs (hot tier grown through its device
+    length, one capture per segment between block compressions) produces exactly the
+    eager loop's tokens and cache state, across a compression (600-token prompt: 88 hot
+    tokens after the prefill, the 424th new token fills a block)."""
+    from unsloth_spectral.llama_loop import LlamaShape, SpectralLlama
+    dev = torch.device("cuda")
+    shape = LlamaShape(layers=2, hidden=512, heads=8, kv_heads=2, head_dim=128, ffn=1024, vocab=1000)
+    model = SpectralLlama(shape, device=dev, dtype=torch.float16, seed=8)
+    model.patch(block_size=512, k_rank_keys=16, k_rank_values=16, hot_buffer_size=64)
+    prompt = torch.randint(0, shape.vocab, (2, 600), generator=torch.Generator(device=dev).manual_seed(9), device=dev)
+    torch.manual_seed(12)
+    eager = model.generate(prompt, 480)
+    st_e = [(c.total_tokens, c.num_cold_blocks, c.hot_len) for c in model._caches]
+    hot_e = model._caches[1].hot_K.clone()
+    torch.manual_seed(12)
+    graphed = model.generate(prompt, 480, cuda_graphs=True)
+    st_g = [(c.total_tokens, c.num_cold_blocks, c.hot_len) for c in model._caches]
+    assert st_e == st_g == [(600 + 479, 2, 600 + 479 - 1024)] * 2
+    assert torch.equal(eager, graphed)
+    assert torch.equal(hot_e, model._caches[1].hot_K)
+    assert int(model._caches[0].tiers.hot_len_device()) == model._caches[0].hot_len

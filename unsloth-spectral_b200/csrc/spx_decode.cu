@@ -159,12 +159,19 @@ __global__ void __launch_bounds__(256) hot_merge_kernel(DecodeParams p) {
   constexpr int RR = NREP > 0 ? NREP : kMaxRep;
   const int g = blockIdx.x, lb = blockIdx.y;
   const int b = lb % p.B;
-  const int D = p.D, half = D / 2, nrep = NREP > 0 ? NREP : p.nrep, hot = p.hot, nb = p.nblk, nc = p.ncold;
+  const int D = p.D, half = D / 2, nrep = NREP > 0 ? NREP : p.nrep, nb = p.nblk, nc = p.ncold;
+  // shared-memory layout by the launch bound p.hot; tokens used: the run-time length
+  const int hmax = p.hot;
+  int hot = hmax;
+  if (p.hot_dev) {
+    const int hd = *p.hot_dev;
+    hot = hd < 0 ? 0 : (hd < hmax ? hd : hmax);
+  }
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   extern __shared__ float sm[];
   float* sq = sm;                   // [nrep][D]
-  float* ssc = sq + nrep * D;       // [nrep][hot]
-  float* sml = ssc + nrep * hot;    // [nrep][2]
+  float* ssc = sq + nrep * D;       // [nrep][hmax]
+  float* sml = ssc + nrep * hmax;   // [nrep][2]
   float* swt = sml + 2 * nrep;      // [nrep][nc + 1] merge weights, then 1/L
   float* sred = swt + nrep * (nc + 1);   // [slices][nrep][D] partial value sums
   int* spos = reinterpret_cast<int*>(sred + (blockDim.x / D) * nrep * D);   // [hot] clamped table rows
@@ -172,8 +179,8 @@ __global__ void __launch_bounds__(256) hot_merge_kernel(DecodeParams p) {
   // staged copies (STAGE): K rows [hot][D], V rows [hot][D] (T), records [nc][nrep][D + 4] f32
   uint8_t* stg = reinterpret_cast<uint8_t*>(sm) + hot_merge_base_floats(p) * sizeof(float);
   T* sK = reinterpret_cast<T*>(stg);
-  T* sV = sK + (size_t)hot * D;
-  float* sR = reinterpret_cast<float*>(sV + (size_t)hot * D);
+  T* sV = sK + (size_t)hmax * D;
+  float* sR = reinterpret_cast<float*>(sV + (size_t)hmax * D);
   if (STAGE) {
     const uint8_t* gk = reinterpret_cast<const uint8_t*>(reinterpret_cast<const T*>(p.hk) + lbg * p.HC * D);
     const uint8_t* gv = reinterpret_cast<const uint8_t*>(reinterpret_cast<const T*>(p.hv) + lbg * p.HC * D);
@@ -228,19 +235,19 @@ __global__ void __launch_bounds__(256) hot_merge_kernel(DecodeParams p) {
         float v = warp_sum(s[h]) * p.scale;
         if (p.mask && p.mask[((int64_t)b * p.Hq + g * nrep + h) * p.mask_stride + (int64_t)nb * p.Tb + t] == 0)
           v = -INFINITY;
-        if (lane == 0) ssc[h * hot + t] = v;
+        if (lane == 0) ssc[h * hmax + t] = v;
       }
     }
   }
   __syncthreads();
   for (int h = warp; h < nrep; h += nwarps) {
     float m = -INFINITY;
-    for (int t = lane; t < hot; t += 32) m = fmaxf(m, ssc[h * hot + t]);
+    for (int t = lane; t < hot; t += 32) m = fmaxf(m, ssc[h * hmax + t]);
     m = warp_max(m);
     float l = 0.f;
     for (int t = lane; t < hot; t += 32) {
-      const float e = m == -INFINITY ? 0.f : __expf(ssc[h * hot + t] - m);
-      ssc[h * hot + t] = e;
+      const float e = m == -INFINITY ? 0.f : __expf(ssc[h * hmax + t] - m);
+      ssc[h * hmax + t] = e;
       l += e;
     }
     l = warp_sum(l);
@@ -280,7 +287,7 @@ __global__ void __launch_bounds__(256) hot_merge_kernel(DecodeParams p) {
         const float v = to_f(hv[(int64_t)t * D + d]);
 #pragma unroll
         for (int h = 0; h < RR; ++h)
-          if (NREP > 0 || h < nrep) acc[h] = fmaf(ssc[h * hot + t], v, acc[h]);
+          if (NREP > 0 || h < nrep) acc[h] = fmaf(ssc[h * hmax + t], v, acc[h]);
       }
 #pragma unroll
       for (int h = 0; h < RR; ++h)
@@ -440,6 +447,7 @@ static int make_params(const spx_decode_args* a, DecodeParams* p) {
   p->rope_len = a->rope_len;
   p->mask_stride = a->mask_stride;
   p->freq = a->rope_freq;
+  p->hot_dev = a->hot_len_device;
   p->nparts = a->num_blocks > 0 ? a->num_blocks : 1;
   p->ncold = a->num_blocks;
   p->qpos = a->query_position;

@@ -31,6 +31,7 @@ struct DecodeParams {
   void* rope; // path scratch after the partials: packed RoPE words [nblk][Tb/16][32][32] u32
               // (reconstruct path) or ProjScratch (projection path)
   const float* freq;  // HOST copy of the RoPE frequencies theta_i [D/2], or nullptr
+  const int* hot_dev; // DEVICE hot-tier length (tokens used: min(*hot_dev, hot)), or nullptr
   int path;           // DecodePath
 };
 

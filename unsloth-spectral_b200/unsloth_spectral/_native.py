@@ -44,7 +44,7 @@ class DecodeArgs(C.Structure):
         (n, C.c_void_p) for n in (
             "q", "codes_k", "codes_v", "scale_k", "scale_v", "basis_k", "basis_v", "block_pos", "hot_k",
             "hot_v", "hot_pos", "cos_table", "sin_table", "mask", "out", "workspace")] + [
-        ("workspace_bytes", C.c_size_t), ("rope_freq", C.c_void_p)]
+        ("workspace_bytes", C.c_size_t), ("rope_freq", C.c_void_p), ("hot_len_device", C.c_void_p)]
 
 
 class RsvdArgs(C.Structure):
@@ -111,7 +111,7 @@ EXPORTS = {
     "spx_check_device": (C.c_int, []),
 }
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 _lib = None
 _load_error = None
 _device_ok = {}

@@ -196,14 +196,18 @@ def decode_args(q: torch.Tensor, tiers, cos: torch.Tensor, sin: torch.Tensor, qu
     a = N.DecodeArgs(
         num_layers=L, batch=B, num_q_heads=Hq, num_kv_heads=t.num_heads, head_dim=D,
         block_size=t.block_size, num_blocks=t.num_blocks, block_capacity=t.block_capacity,
-        rank_k=t.rank_k_pad, rank_v=t.rank_v_pad, hot_len=t.hot_len, hot_capacity=t.hot_capacity,
+        rank_k=t.rank_k_pad, rank_v=t.rank_v_pad,
+        hot_len=t.hot_len if getattr(t, "hot_bound", None) is None else min(max(t.hot_len, t.hot_bound),
+                                                                              t.hot_capacity),
+        hot_capacity=t.hot_capacity,
         dtype=N.dtype_code(t.dtype), rope_mode=rope_mode, rope_tied=int(bool(tied)), rope_len=cos32.shape[0],
         query_position=int(query_position), scale=float(scale), mask_stride=mask_stride,
         q=N.ptr(q), codes_k=N.ptr(t.codes_k), codes_v=N.ptr(t.codes_v), scale_k=N.ptr(t.scale_k),
         scale_v=N.ptr(t.scale_v), basis_k=N.ptr(t.basis_k), basis_v=N.ptr(t.basis_v),
         block_pos=N.ptr(t.block_pos), hot_k=N.ptr(t.hot_k), hot_v=N.ptr(t.hot_v), hot_pos=N.ptr(t.hot_pos),
         cos_table=N.ptr(cos32), sin_table=N.ptr(sin32), mask=N.ptr(mask_u8), out=N.ptr(out),
-        rope_freq=N.ptr(freq))
+        rope_freq=N.ptr(freq),
+        hot_len_device=N.ptr(t.hot_len_device()) if hasattr(t, "hot_len_device") else None)
     return a, out, (q, cos32, sin32, mask_u8, freq)
 
 

@@ -201,7 +201,13 @@ def create_spectral_forward_inference(block_size: int = 512, k_rank_keys: int = 
         kv_seq_len = 1 + past_key_value.total_tokens
         cos, sin = rope_tables_for(self, kv_seq_len + 1, hidden_states.device)
         qpos = kv_seq_len - 1
-        q = apply_rope(q.float(), cos[qpos], sin[qpos]).to(q.dtype)
+        # the query is rotated at position_ids, as the reference's decode path does
+        # (integration.py:600-612); without them, at the next cache position
+        if position_ids is not None:
+            pid = position_ids.reshape(-1, position_ids.shape[-1])[:, -1:].to(hidden_states.device)
+            q = apply_rope(q.float(), cos[pid][:, None], sin[pid][:, None]).to(q.dtype)
+        else:
+            q = apply_rope(q.float(), cos[qpos], sin[qpos]).to(q.dtype)
         past_key_value.append(k_pre, v, position_ids)
         if use_spectral_attention and past_key_value.total_tokens > block_size:
             if use_kernels:

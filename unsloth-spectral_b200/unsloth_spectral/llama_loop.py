@@ -30,7 +30,7 @@ from typing import List, Optional
 import torch
 import torch.nn.functional as F
 
-from .integration import patch_unsloth_attention
+from .integration import patch_unsloth_attention, rope_tables_for
 
 
 @dataclass
@@ -158,11 +158,13 @@ class SpectralLlama(torch.nn.Module):
         return self.lm_head(self.model.norm(h[:, -1]))
 
     @torch.no_grad()
-    def generate(self, input_ids: torch.Tensor, max_new_tokens: int, timer=None):
+    def generate(self, input_ids: torch.Tensor, max_new_tokens: int, timer=None, cuda_graphs: bool = False):
         """Greedy decoding: the prompt, then ``max_new_tokens`` tokens, each the argmax of
         the previous step's logits.  Positions stay on the device (no host reads inside
-        the loop).  ``timer(name)``, if given, is called after the prefill ("prefill")
-        and at the end ("decode").  Returns the new tokens ``[B, max_new_tokens]``."""
+        the loop).  ``cuda_graphs``: replay the decode step from a CUDA graph between block
+        compressions (``_decode_graphed``).  ``timer(name)``, if given, is called after
+        the prefill ("prefill") and at the end ("decode").  Returns the new tokens
+        ``[B, max_new_tokens]``."""
         B, T = input_ids.shape
         logits, caches = self.prefill(input_ids)
         if timer is not None:
@@ -170,14 +172,78 @@ class SpectralLlama(torch.nn.Module):
         out = torch.empty(B, max_new_tokens, dtype=torch.long, device=input_ids.device)
         tok = logits.argmax(-1)
         pos = torch.full((1, 1), T, dtype=torch.long, device=input_ids.device)
-        for s in range(max_new_tokens):
-            out[:, s] = tok
-            if s + 1 == max_new_tokens:
-                break
-            logits = self.decode_step(tok, pos, caches)
-            tok = logits.argmax(-1)
-            pos += 1
+        if cuda_graphs:
+            self._decode_graphed(tok, pos, caches, out)
+        else:
+            for s in range(max_new_tokens):
+                out[:, s] = tok
+                if s + 1 == max_new_tokens:
+                    break
+                logits = self.decode_step(tok, pos, caches)
+                tok = logits.argmax(-1)
+                pos += 1
         if timer is not None:
             timer("decode")
         self._caches = caches
         return out
+
+    @torch.no_grad()
+    def _decode_graphed(self, tok: torch.Tensor, pos: torch.Tensor, caches: List, out: torch.Tensor):
+        """The decode loop with the step captured in a CUDA graph.  One step's kernels
+        depend on the host only through the cold-tier block count and the tensors'
+        addresses; the hot tier grows through its device length (single-token appends
+        write at it and advance it on the device, the merge kernel reads it).  So between
+        two block compressions the step is captured once and replayed, the caches' host
+        counters advanced per replay; the step whose append fills a block (compression,
+        host-side) and the first step of a segment (warm-up of the capture stream) run
+        eagerly.  Same kernels and results as the eager loop."""
+        n = out.shape[1]
+        dev = tok.device
+        stream = torch.cuda.Stream(device=dev)
+        stream.wait_stream(torch.cuda.current_stream(dev))
+        tok, s = tok.clone(), 0
+        out[:, 0] = tok
+        with torch.cuda.stream(stream):
+            while s + 1 < n:
+                t0 = caches[0].tiers
+                room = caches[0].block_size - 1 - t0.hot_len   # appends before one fills a block
+                if room < 3 or n - 1 - s < 3:
+                    logits = self.decode_step(tok, pos, caches)
+                    tok.copy_(logits.argmax(-1))
+                    pos.add_(1)
+                    s += 1
+                    out[:, s] = tok
+                    continue
+                k = min(room, n - 1 - s)
+                # everything the step caches on first use is created here, eagerly and outside
+                # the graph's memory pool: hot-tier buffers of full size, RoPE tables long
+                # enough for the segment, and (by one eager step on the capture stream) the
+                # stream's decode workspace and cuBLAS state
+                for c in caches:
+                    c.tiers.ensure_hot(c.block_size)
+                    c.tiers.hot_bound = c.block_size
+                for layer in self.model.layers:
+                    rope_tables_for(layer.self_attn, caches[0].total_tokens + k + 2, dev)
+                logits = self.decode_step(tok, pos, caches)
+                tok.copy_(logits.argmax(-1))
+                pos.add_(1)
+                s += 1
+                out[:, s] = tok
+                for c in caches:
+                    c.tiers.hot_len_device()
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=stream):
+                    g_logits = self.decode_step(tok, pos, caches)
+                    tok.copy_(g_logits.argmax(-1))
+                    pos.add_(1)
+                for r in range(k - 1):
+                    if r:
+                        for c in caches:
+                            c.note_replayed_tokens(1)
+                    graph.replay()
+                    s += 1
+                    out[:, s] = tok
+                del graph, g_logits
+                for c in caches:
+                    c.tiers.hot_bound = None
+        torch.cuda.current_stream(dev).wait_stream(stream)

@@ -59,11 +59,39 @@ class DeviceTiers:
         self.rank_k, self.rank_v = rank_k, rank_v
         self.rank_k_pad, self.rank_v_pad = _pad16(rank_k), _pad16(rank_v)
         self.num_blocks = 0
-        self.hot_len = 0
+        # hot-tier length: a host int and a device int32 copy the decode kernels read (so
+        # a decode step can be replayed from a CUDA graph while the tier grows).  Host-side
+        # assignments mark the device copy stale; hot_len_device() refreshes it, and
+        # advance_hot() moves both by device arithmetic only.
+        self._hot_len = 0
+        self._hot_stale = False
+        self._hot_len_dev = torch.zeros((), dtype=torch.int32, device=self.device)
+        self.hot_bound = None   # launch bound for the hot tier while a CUDA graph replays steps
         self.block_capacity = 0
         self.hot_capacity = 0
         self._alloc_cold(block_capacity)
         self._alloc_hot(hot_capacity or (block_size + 64))
+
+    @property
+    def hot_len(self) -> int:
+        return self._hot_len
+
+    @hot_len.setter
+    def hot_len(self, n: int):
+        self._hot_len = int(n)
+        self._hot_stale = True
+
+    def hot_len_device(self) -> torch.Tensor:
+        """Device int32 copy of the hot length, refreshed after host-side changes."""
+        if self._hot_stale:
+            self._hot_len_dev.fill_(self._hot_len)
+            self._hot_stale = False
+        return self._hot_len_dev
+
+    def advance_hot(self, n: int):
+        """Grow the hot length by n on the host and, by a device add, on the device."""
+        self.hot_len_device().add_(n)
+        self._hot_len += n
 
     # -- allocation --------------------------------------------------------------
     def _alloc_cold(self, cap):
@@ -272,15 +300,26 @@ class SpectralCache:
         t = self._tiers_for(B, K_new.device)
         n0 = t.hot_len
         t.ensure_hot(n0 + T_new)
-        t.hot_k[:, :, n0:n0 + T_new].copy_(K_new)
-        t.hot_v[:, :, n0:n0 + T_new].copy_(V_new)
-        if position_ids is None:
-            t.hot_pos[n0:n0 + T_new] = torch.arange(self.current_position, self.current_position + T_new,
-                                                    device=t.device)
-        else:
+        pid = None
+        if position_ids is not None:
             pid = position_ids.reshape(-1, position_ids.shape[-1])[0] if position_ids.dim() > 1 else position_ids
-            t.hot_pos[n0:n0 + T_new].copy_(pid.to(torch.int64), non_blocking=True)
-        t.hot_len = n0 + T_new
+        if T_new == 1 and pid is not None and pid.device == t.device:
+            # a decode token: written at the device hot length, which advances on the
+            # device, so the step has no host-dependent addresses (CUDA-graph safe)
+            idx = t.hot_len_device().view(1).long()
+            t.hot_k.index_copy_(2, idx, K_new.to(t.dtype))
+            t.hot_v.index_copy_(2, idx, V_new.to(t.dtype))
+            t.hot_pos.index_copy_(0, idx, pid.reshape(1).to(torch.int64))
+            t.advance_hot(1)
+        else:
+            t.hot_k[:, :, n0:n0 + T_new].copy_(K_new)
+            t.hot_v[:, :, n0:n0 + T_new].copy_(V_new)
+            if pid is None:
+                t.hot_pos[n0:n0 + T_new] = torch.arange(self.current_position, self.current_position + T_new,
+                                                        device=t.device)
+            else:
+                t.hot_pos[n0:n0 + T_new].copy_(pid.to(torch.int64), non_blocking=True)
+            t.hot_len = n0 + T_new
         self.total_tokens += T_new
         self.current_position += T_new
         self._blocks_view = None
@@ -397,6 +436,17 @@ class SpectralCache:
                 t.scale_v[:, :, dst] = scale.permute(1, 2, 0)
                 t.minmax_v[:, :, dst] = mm.permute(1, 2, 0, 3)
                 t.basis_v[:, :, dst] = basis.permute(1, 2, 0, 3, 4)
+
+    def note_replayed_tokens(self, n: int = 1):
+        """Host bookkeeping of ``n`` single-token appends that a replayed CUDA graph made
+        on the device (the graph re-runs the kernels, not this Python): the counters
+        ``append`` would have advanced.  The caller guarantees that none of these appends
+        filled a block (no compression happened)."""
+        t = self.tiers
+        t._hot_len += n
+        self.total_tokens += n
+        self.current_position += n
+        self._blocks_view = None
 
     # -- reference-layout views -------------------------------------------------------
     @property
