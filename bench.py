@@ -786,6 +786,57 @@ def run_rsvd(args):
                                  "path": os.environ.get("SPX_RSVD_PATH", "auto")}}), flush=True)
 
 
+class _LayerTiers:
+    """One layer's slice of the bench's 32-layer storage, with the attributes the
+    package's decode path reads from a cache's device tiers (no copy)."""
+
+    def __init__(self, c, t, l):
+        self.num_heads = t["codes_k"].shape[2]
+        self.head_dim, self.block_size = c["head_dim"], c["block"]
+        self.num_blocks = self.block_capacity = c["blocks"]
+        self.rank_k = self.rank_v = self.rank_k_pad = self.rank_v_pad = c["rank"]
+        self.hot_len = self.hot_capacity = c["hot"]
+        self.hot_bound = None
+        self.dtype, self.device = torch.float16, t["codes_k"].device
+        for name in ("codes_k", "codes_v", "scale_k", "scale_v", "basis_k", "basis_v", "hot_k", "hot_v"):
+            setattr(self, name, t[name][l])
+        self.block_pos, self.hot_pos = t["block_pos"], t["hot_pos"]
+        self._len = torch.full((), c["hot"], dtype=torch.int32, device=self.device)
+
+    def hot_len_device(self):
+        return self._len
+
+
+def run_api_leg(c, t, qs_dev, cos, sin, qpos, args, stream, barrier):
+    """Decode steps through the package's public entry point, one call per layer."""
+    from unsloth_spectral import SpectralCache
+    from unsloth_spectral.kernels import spectral_attention_decode
+    L, B, D = c["layers"], c["batch"], c["head_dim"]
+    caches = []
+    for l in range(L):
+        sc = SpectralCache(c["kv_heads"], D, block_size=c["block"], k_rank_keys=c["rank"], k_rank_values=c["rank"],
+                           device=t["codes_k"].device, dtype=torch.float16)
+        sc.tiers = _LayerTiers(c, t, l)
+        caches.append(sc)
+    nq = len(qs_dev)
+
+    def step(i):
+        q = qs_dev[i % nq]
+        for l in range(L):
+            spectral_attention_decode(q[l].reshape(B, -1, 1, D), caches[l], cos, sin, qpos)
+
+    for i in range(args.warmup):
+        step(i)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    barrier()
+    return e0.elapsed_time(e1) / args.steps
+
+
 def run_ours(args, c):
     _use_ours()
     from unsloth_spectral import _native as N, _ops
@@ -898,6 +949,12 @@ def run_ours(args, c):
     barrier()
     e2e_ms = ev4.elapsed_time(ev5)
 
+    # ---- the drop-in API: one kernels.spectral_attention_decode call per layer, over
+    #      SpectralCache objects whose tiers are the layers' slices of the same storage
+    api_ms = None
+    if world == 1:
+        api_ms = run_api_leg(c, tiers, qs_dev, cos, sin, qpos, args, stream, barrier)
+
     # ---- max over ranks
     times = torch.tensor([dev_ms, kern_ms, e2e_ms], dtype=torch.float64, device=dev)
     if world > 1:
@@ -970,6 +1027,10 @@ def run_ours(args, c):
             "config1": cfg1,
             "cpu_baseline": None,
             "clocks": clk.summary(),
+            "api": None if api_ms is None else {
+                "tokens_per_s": B / (api_ms / 1e3), "ms_per_step": api_ms, "calls_per_step": L,
+                "path": "kernels.spectral_attention_decode once per layer (B=32, one SpectralCache per layer), "
+                        "Python argument building included"},
             "gpu_launches": DECODE_LAUNCHES * args.steps,
             "setup_s": setup_s, "rsvd_setup_s": rsvd_setup_s,
         }
