@@ -110,3 +110,27 @@ def test_patched_prefill_uses_kernel_and_matches_eager_path():
     got = I._dense_attention(q, cache, cos, sin, nrep, 128, mask, q.dtype, pos)
     eager = I._dense_attention(q, cache, cos, sin, nrep, 128, mask, q.dtype, None)
     _close(got, eager.float())
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_prefill_tcgen05_and_mma_kernels_agree(monkeypatch, dtype):
+    """The tcgen05 kernel (SPX_PREFILL_PATH=tc: 128-token key tiles, S and O in tensor
+    memory) and the mma.sync kernel (the default) on the same prompt, both against the
+    float32 reference; causal, with a partial last query tile and a partial hot tile."""
+    from unsloth_spectral import _ops
+    from unsloth_spectral import synthetic as syn
+    dev = torch.device("cuda")
+    B, H, nrep, n_tok, Tq = 2, 4, 4, 1700, 300
+    cache = _cache(B, H, n_tok, dtype, 32, 16, seed=11)
+    cos, sin = syn.rope_tables(n_tok + 8, 128, 1e6, device=dev)
+    q = (torch.randn(B, H * nrep, Tq, 128, generator=torch.Generator(device=dev).manual_seed(2), device=dev)
+         / math.sqrt(128) * 4).to(dtype)
+    q_pos = torch.arange(n_tok - Tq, n_tok, device=dev)
+    ref = _reference(q, cache, cos, sin, q_pos, causal=True)
+    mma = _ops.prefill(q, cache.tiers, cos, sin, q_pos, causal=True)
+    monkeypatch.setenv("SPX_PREFILL_PATH", "tc")
+    tc = _ops.prefill(q, cache.tiers, cos, sin, q_pos, causal=True)
+    monkeypatch.delenv("SPX_PREFILL_PATH")
+    _close(tc, ref)
+    _close(mma, ref)
+    _close(tc, mma.float())

@@ -23,8 +23,11 @@
 // The rebuilt tiles cost 2 * 64 * 128 * (R_K + R_V) FLOPs per tile against
 // 4 * 128 * 64 * 128 for the attention itself (about 12 % at R = 16).
 #include <math.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include "spx_common.cuh"
+#include "spx_prefill.cuh"
 #include "spx_sm100.cuh"
 
 namespace spx {
@@ -39,27 +42,7 @@ constexpr int PITCH = 136;   // shared row pitch (elements) of the K / V / basis
 constexpr int RMAX = 64;
 constexpr float LOG2E_F = 1.4426950408889634f;
 
-struct Params {
-  int B, Hq, H, nrep, QT, qlen, T, nblk, nbc, RK, RV, hot, HC, causal, mask_f32, rope_len;
-  float scale;
-  const void* q;
-  const int64_t* qpos;
-  const int8_t* ck;
-  const int8_t* cv;
-  const float* sk;
-  const float* sv;
-  const void* bk;
-  const void* bv;
-  const int64_t* bpos;
-  const void* hk;
-  const void* hv;
-  const int64_t* hpos;
-  const float* cosT;
-  const float* sinT;
-  const void* mask;
-  int64_t msb, msh, msq;
-  void* out;
-};
+using Params = PrefillParams;
 
 template <typename T>
 struct Ty;
@@ -479,6 +462,17 @@ int spx_prefill_attn(const spx_prefill_args* a, void* stream) {
   const dim3 grid((a->q_len + p.QT - 1) / p.QT, a->batch * a->num_kv_heads);
   SPX_REQUIRE(grid.y <= 65535u, SPX_ERR_SHAPE, "batch * num_kv_heads above 65535");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // SPX_PREFILL_PATH=tc selects the tcgen05 kernel (spx_prefill_tc.cu; blocks of a
+  // multiple of 128 tokens); the default is the mma.sync kernel below, measured 3x faster
+  // (8.6 against 27.5 ms per layer at config 4's prompt: the tcgen05 kernel runs its tile
+  // phases one after another on one CTA per SM)
+  const char* path = getenv("SPX_PREFILL_PATH");
+  const bool tc = path && strcmp(path, "tc") == 0 && prefill_tc_supported(a->block_size, a->num_blocks);
+  if (tc) {
+    SPX_REQUIRE(aligned16(a->q) && aligned16(a->out) && (a->hot_len == 0 || (aligned16(a->hot_k) && aligned16(a->hot_v))),
+                SPX_ERR_ALIGN, "q, out and the hot tier need 16-byte alignment");
+    return prefill_tc_launch(p, a->dtype, st);
+  }
   if (a->dtype == SPX_F16) {
     cudaFuncSetAttribute(pfa::prefill_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, pfa::SMEM);
     pfa::prefill_kernel<__half><<<grid, pfa::NT, pfa::SMEM, st>>>(p);
