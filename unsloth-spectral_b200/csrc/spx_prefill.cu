@@ -463,14 +463,15 @@ int spx_prefill_attn(const spx_prefill_args* a, void* stream) {
   SPX_REQUIRE(grid.y <= 65535u, SPX_ERR_SHAPE, "batch * num_kv_heads above 65535");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   // SPX_PREFILL_PATH=tc selects the tcgen05 kernel (spx_prefill_tc.cu; blocks of a
-  // multiple of 128 tokens); the default is the mma.sync kernel below, measured 3x faster
-  // (8.6 against 27.5 ms per layer at config 4's prompt: the tcgen05 kernel runs its tile
+  // multiple of 128 tokens); the default is the mma.sync kernel below, measured faster
+  // (8.6 against 11.3 ms per layer at config 4's prompt: the tcgen05 kernel runs its tile
   // phases one after another on one CTA per SM)
   const char* path = getenv("SPX_PREFILL_PATH");
   const bool tc = path && strcmp(path, "tc") == 0 && prefill_tc_supported(a->block_size, a->num_blocks);
   if (tc) {
-    SPX_REQUIRE(aligned16(a->q) && aligned16(a->out) && (a->hot_len == 0 || (aligned16(a->hot_k) && aligned16(a->hot_v))),
-                SPX_ERR_ALIGN, "q, out and the hot tier need 16-byte alignment");
+    SPX_REQUIRE(aligned16(a->q) && aligned16(a->out) && aligned16(a->cos_table) && aligned16(a->sin_table) &&
+                    (a->hot_len == 0 || (aligned16(a->hot_k) && aligned16(a->hot_v))),
+                SPX_ERR_ALIGN, "q, out, the tables and the hot tier need 16-byte alignment");
     return prefill_tc_launch(p, a->dtype, st);
   }
   if (a->dtype == SPX_F16) {

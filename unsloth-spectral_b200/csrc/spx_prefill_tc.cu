@@ -11,13 +11,14 @@
 //   1. cold tiles: the INT8 codes of the tile's keys and values are converted to 16-bit
 //      A operands (thread = key) and the block's bases staged as MN-major B operands;
 //      tcgen05 rebuilds K~ = codes_K B_K and V~ = codes_V B_V into TMEM (f32, columns
-//      0-127 / 128-255); warps 0-3 (TMEM lane = key) scale K~, rotate it in f32 at the
-//      keys' positions and store it as the K-major B operand of the scores, warps 4-7
-//      scale V~ into the B operand of the value product.  Hot tiles are copied and
-//      rotated instead.
+//      0-127 / 128-255); warps w and w + 4 (TMEM lane = key) each take half of the
+//      dimensions: scale K~, rotate it in f32 at the keys' positions and store it as the
+//      K-major B operand of the scores, and scale V~ into the B operand of the value
+//      product.  Hot tiles are copied and rotated instead.
 //   2. S = Q K~^T (M = 128 rows, N = 128 keys, K = 128 dims) into TMEM columns 256-383.
-//   3. Warps 0-3, thread = query row: scale (log2 units), causal rule, additive mask,
-//      row maximum over the tile; the running maximum used for the exponentials moves
+//   3. Thread = (query row, half of the tile's keys; warps w and w + 4 share a row, the
+//      halves' maxima and sums exchanged through shared memory): scale (log2 units),
+//      causal rule (one threshold per row on a cold tile), additive mask, row maximum; the running maximum used for the exponentials moves
 //      only when the row's maximum exceeds it by more than 8 (then the row of O in TMEM
 //      and the row sum are rescaled), so P = exp2(s - m_used) <= 256 fits the 16-bit
 //      operand; P is stored as the K-major A operand of the value product.
@@ -163,6 +164,7 @@ __global__ void __launch_bounds__(NT, 1) prefill_tc_kernel(Params p) {
   __shared__ int sbad;
   __shared__ float s_scale[2];
   __shared__ long long s_qmax[8];
+  __shared__ float s_pair[2][128];   // per-row partial maxima / sums of the two halves
   const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31, quad = w & 3;
   const int h = blockIdx.y % p.H, b = blockIdx.y / p.H;
   const int64_t u = (int64_t)b * p.H + h;
@@ -183,10 +185,12 @@ __global__ void __launch_bounds__(NT, 1) prefill_tc_kernel(Params p) {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   // this thread's query row (warps 0-3; TMEM lane = row): head hq, query qi
-  const int row = tid & 127;
+  // this thread's query row (TMEM lane = row; warps w and w + 4 share the row, each taking
+  // half of its keys / dims): head hq, query qi
+  const int row = tid & 127, hlf = tid >> 7;
   const int hq = h * p.nrep + row / p.QT;
   const int qi = blockIdx.x * p.QT + row % p.QT;
-  const bool rowv = tid < 128 && qi < p.qlen;
+  const bool rowv = qi < p.qlen;
   const long long qp = rowv ? (long long)p.qpos[qi] : -1;
   {
     long long mq = qp;
@@ -353,6 +357,21 @@ __global__ void __launch_bounds__(NT, 1) prefill_tc_kernel(Params p) {
     }
     sync_ops();
     if (cold) {
+      // the key's table rows (half hlf of the first-half dims), loaded while the tensor
+      // core rebuilds the tile
+      const int key = 32 * quad + lane;   // TMEM lane = key
+      float4 c4[8], s4[8];
+      {
+        long long kp = sPos[key];
+        kp = kp < 0 ? 0 : (kp >= p.rope_len ? p.rope_len - 1 : kp);
+        const float4* crow = reinterpret_cast<const float4*>(p.cosT + kp * 128 + 32 * hlf);
+        const float4* srow = reinterpret_cast<const float4*>(p.sinT + kp * 128 + 32 * hlf);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          c4[i] = __ldg(crow + i);
+          s4[i] = __ldg(srow + i);
+        }
+      }
       // ---- K~ and V~ on the tensor cores (TMEM columns 0 and 128) ---------------------
       if (tid == 0 && !bad) {
         for (int ks = 0; ks < p.RK / 16; ++ks)
@@ -364,39 +383,34 @@ __global__ void __launch_bounds__(NT, 1) prefill_tc_kernel(Params p) {
         umma_commit(barA);
       }
       wait_mma();
-      const int key = 32 * quad + lane;   // TMEM lane = key
-      if (w < 4) {
-        // K~: scale, rotate at the key's position (f32), store as the K-major B operand
-        long long kp = sPos[key];
-        kp = kp < 0 ? 0 : (kp >= p.rope_len ? p.rope_len - 1 : kp);
+      {
+        // K~ half hlf (dims 32 hlf .. and 64 + 32 hlf ..): scale, rotate at the key's
+        // position (f32), store as the K-major B operand
         const float sc = s_scale[0];
-#pragma unroll 1
-        for (int hf = 0; hf < 2; ++hf) {
-          float x[32], y[32];
-          tld32(tq + 32 * hf, x);
-          tld32(tq + 64 + 32 * hf, y);
+        const int hf = hlf;
+        float x[32], y[32];
+        tld32(tq + 32 * hf, x);
+        tld32(tq + 64 + 32 * hf, y);
+        const float* cf = reinterpret_cast<const float*>(c4);
+        const float* sf = reinterpret_cast<const float*>(s4);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint32_t lw[4], hw[4];
+        for (int q = 0; q < 4; ++q) {
+          uint32_t lw[4], hw[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int i = 8 * q + 2 * e, d = 32 * hf + i;
-              const float2 c = *reinterpret_cast<const float2*>(p.cosT + kp * 128 + d);
-              const float2 sn = *reinterpret_cast<const float2*>(p.sinT + kp * 128 + d);
-              const float x0 = sc * x[i], x1 = sc * x[i + 1], y0 = sc * y[i], y1 = sc * y[i + 1];
-              lw[e] = Y::pack(x0 * c.x - y0 * sn.x, x1 * c.y - y1 * sn.y);
-              hw[e] = Y::pack(y0 * c.x + x0 * sn.x, y1 * c.y + x1 * sn.y);
-            }
-            const int ch = 4 * hf + q;   // 8-dim chunk of the first half
-            *reinterpret_cast<uint4*>(sm + OFF_K + ch * 2048 + key * 16) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-            *reinterpret_cast<uint4*>(sm + OFF_K + (8 + ch) * 2048 + key * 16) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          for (int e = 0; e < 4; ++e) {
+            const int i = 8 * q + 2 * e;
+            const float x0 = sc * x[i], x1 = sc * x[i + 1], y0 = sc * y[i], y1 = sc * y[i + 1];
+            lw[e] = Y::pack(x0 * cf[i] - y0 * sf[i], x1 * cf[i + 1] - y1 * sf[i + 1]);
+            hw[e] = Y::pack(y0 * cf[i] + x0 * sf[i], y1 * cf[i + 1] + x1 * sf[i + 1]);
           }
+          const int ch = 4 * hf + q;   // 8-dim chunk of the first half
+          *reinterpret_cast<uint4*>(sm + OFF_K + ch * 2048 + key * 16) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+          *reinterpret_cast<uint4*>(sm + OFF_K + (8 + ch) * 2048 + key * 16) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
         }
-      } else {
-        // V~: scale and store as the MN-major B operand (same byte layout)
+        // V~ dims 64 hlf .. + 63: scale and store as the MN-major B operand (same layout)
         const float sv = s_scale[1];
 #pragma unroll 1
-        for (int c32 = 0; c32 < 4; ++c32) {
+        for (int c32 = 2 * hlf; c32 < 2 * hlf + 2; ++c32) {
           float v[32];
           tld32(tq + 128 + 32 * c32, v);
 #pragma unroll
@@ -417,9 +431,18 @@ __global__ void __launch_bounds__(NT, 1) prefill_tc_kernel(Params p) {
       umma_commit(barA);
     }
     wait_mma();
-    // ---- online softmax, thread = query row ---------------------------------------------
-    if (w < 4) {
+    // ---- online softmax: thread = (query row, half of the tile's keys) ---------------------
+    {
+      // keys kk <= kmax are kept: the causal rule on a cold tile (consecutive positions) is
+      // one threshold per row; hot tiles and additive masks take the general path
+      int kmax = nk - 1;
+      if (p.causal && cold) {
+        const long long lim = qp - (p.bpos[j] + t0);
+        kmax = lim < 0 ? -1 : (lim >= nk ? nk - 1 : (int)lim);
+      }
+      const bool general = (p.causal && !cold) || (p.mask != nullptr);
       auto logit = [&](float sraw, int kk) -> float {
+        if (!general) return kk <= kmax ? sraw * sl2 : -INFINITY;
         float x = sraw * sl2;
         const bool keep = kk < nk && !(p.causal && (long long)sPos[kk] > qp);
         if (!keep) return -INFINITY;
@@ -431,20 +454,32 @@ __global__ void __launch_bounds__(NT, 1) prefill_tc_kernel(Params p) {
         }
         return x;
       };
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c32 = 0; c32 < 4; ++c32) {
+      // the half's 64 logits, kept in registers across the two passes
+      float lg[64];
+      {
         float v[32];
-        tld32(tq + 256 + 32 * c32, v);
+        tld32(tq + 256 + 64 * hlf, v);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) mx = fmaxf(mx, logit(v[e], 32 * c32 + e));
+        for (int e = 0; e < 32; ++e) lg[e] = logit(v[e], 64 * hlf + e);
+        tld32(tq + 256 + 64 * hlf + 32, v);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) lg[32 + e] = logit(v[e], 64 * hlf + 32 + e);
       }
-      if (mx > m_used + RESCALE) {   // also true for the first finite maximum
+      float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < 64; e += 2) {
+        m0 = fmaxf(m0, lg[e]);
+        m1 = fmaxf(m1, lg[e + 1]);
+      }
+      s_pair[hlf][row] = fmaxf(m0, m1);
+      __syncthreads();
+      const float mx = fmaxf(s_pair[0][row], s_pair[1][row]);
+      if (mx > m_used + RESCALE) {   // also true for the first finite maximum; same in both halves
         const float corr = exp2f(m_used - mx);   // 0 while m_used is -inf
         lsum *= corr;
         if (o_init) {
 #pragma unroll 1
-          for (int c32 = 0; c32 < 4; ++c32) {
+          for (int c32 = 2 * hlf; c32 < 2 * hlf + 2; ++c32) {
             float o[32];
             tld32(tq + 384 + 32 * c32, o);
 #pragma unroll
@@ -455,22 +490,20 @@ __global__ void __launch_bounds__(NT, 1) prefill_tc_kernel(Params p) {
         m_used = mx;
       }
       const float mu = m_used == -INFINITY ? 0.f : m_used;
-#pragma unroll 1
-      for (int c32 = 0; c32 < 4; ++c32) {
-        float v[32];
-        tld32(tq + 256 + 32 * c32, v);
-        uint32_t pw[16];
+      float l0 = 0.f, l1 = 0.f;
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const float p0 = exp2f(logit(v[e], 32 * c32 + e) - mu), p1 = exp2f(logit(v[e + 1], 32 * c32 + e + 1) - mu);
-          lsum += p0 + p1;
-          pw[e >> 1] = Y::pack(p0, p1);
+      for (int q = 0; q < 8; ++q) {   // 8-key chunks 8 hlf + q of the A operand
+        uint32_t pw[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = exp2f(lg[8 * q + 2 * e] - mu), p1 = exp2f(lg[8 * q + 2 * e + 1] - mu);
+          l0 += p0;
+          l1 += p1;
+          pw[e] = Y::pack(p0, p1);
         }
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          *reinterpret_cast<uint4*>(sm + OFF_P + (4 * c32 + q) * 2048 + row * 16) =
-              make_uint4(pw[4 * q], pw[4 * q + 1], pw[4 * q + 2], pw[4 * q + 3]);
+        *reinterpret_cast<uint4*>(sm + OFF_P + (8 * hlf + q) * 2048 + row * 16) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
       }
+      lsum += l0 + l1;   // this half's share of the row sum
     }
     sync_ops();
     // ---- O += P V~ (TMEM columns 384) ---------------------------------------------------
@@ -484,12 +517,14 @@ __global__ void __launch_bounds__(NT, 1) prefill_tc_kernel(Params p) {
     o_init = true;
     wait_mma();
   }
-  // ---- normalise and store, thread = row ------------------------------------------------
-  if (w < 4) {
-    const float inv = 1.f / lsum;
+  // ---- normalise and store: the two halves' row sums added, thread = (row, half of dims)
+  s_pair[hlf][row] = lsum;
+  __syncthreads();
+  {
+    const float inv = 1.f / (s_pair[0][row] + s_pair[1][row]);
     T* og = reinterpret_cast<T*>(p.out) + (((int64_t)b * p.Hq + hq) * p.qlen + qi) * 128;
 #pragma unroll 1
-    for (int c32 = 0; c32 < 4; ++c32) {
+    for (int c32 = 2 * hlf; c32 < 2 * hlf + 2; ++c32) {
       float o[32];
       tld32(tq + 384 + 32 * c32, o);
       if (rowv) {
