@@ -434,6 +434,34 @@ __global__ void __launch_bounds__(kCholThreads, RMAX <= 24 ? 10 : RMAX <= 40 ? 8
   }
 }
 
+// The same factor for r <= 40 with one warp per matrix (chol_warp: rows in registers, no
+// block barriers, the next pivot's reciprocal formed while a column's update issues):
+// 2.6x the throughput of chol_kernel at 4096 matrices on B200.  Same outputs and pass
+// rules; a pivot must also be a normal float64 to count.
+constexpr int kCholWarps = 2;
+template <int RMAX>
+__global__ void __launch_bounds__(kCholWarps * 32)
+    chol_warp_kernel(const double* __restrict__ Gw, float* __restrict__ Lw, int* __restrict__ np,
+                     int* __restrict__ list, int* __restrict__ cnt, int pass, int npass0, int r, int Nb) {
+  __shared__ double colbuf[kCholWarps][2 * RMAX];
+  __shared__ double scale_s[kCholWarps][RMAX];
+  const int wi = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool listed = pass >= npass0;
+  const int nk = listed ? *cnt : Nb;
+  for (int kk = blockIdx.x * kCholWarps + wi; kk < nk; kk += gridDim.x * kCholWarps) {
+    const int i = listed ? list[kk] : kk;
+    if (listed && pass >= np[i]) continue;
+    const int n0 = np[i];
+    const int n = chol_warp<RMAX>(Gw + (int64_t)i * r * r, r, r, Lw + (int64_t)i * r * r, r, colbuf[wi],
+                                  scale_s[wi], n0);
+    if (lane == 0 && pass == 0) {
+      np[i] = n;
+      if (n > n0) list[atomicAdd(cnt, 1)] = i;
+    }
+    __syncwarp();
+  }
+}
+
 // X := X L^{-T}, grid (matrices, 128-row chunks), 128 threads.  The chunk is staged in
 // shared memory with coalesced float4 copies (odd row pitch: a thread reads its own row
 // conflict-free), each thread substitutes its row in registers reading L four entries
@@ -936,14 +964,15 @@ static int run_chain(const spx_rsvd_args* a, const RsvdWs& w, cudaStream_t st) {
       const bool listed = pass >= npass;
       const int gg = listed ? std::min(Nb, 4 * nsm) : Nb;
       const int gc = listed ? std::min(Nb, 8 * nsm) : Nb;
+      const int gw = listed ? std::min((Nb + kCholWarps - 1) / kCholWarps, 4 * nsm) : (Nb + kCholWarps - 1) / kCholWarps;
       const dim3 gs(listed ? std::min(Nb, std::max(nsm, 8 * nsm / nch)) : Nb, nch);
       if (r <= 24) {
         gram_kernel<24><<<gg, gram_threads(r), sg, st>>>(X, w.G, w.np, w.list, w.cnt, pass, npass, rows, r);
-        chol_kernel<24><<<gc, kCholThreads, 0, st>>>(w.G, w.L, w.np, w.list, w.cnt, pass, npass, r);
+        chol_warp_kernel<24><<<gw, kCholWarps * 32, 0, st>>>(w.G, w.L, w.np, w.list, w.cnt, pass, npass, r, Nb);
         trsolve_kernel<24><<<gs, 128, ts, st>>>(X, w.L, w.np, w.list, w.cnt, pass, npass, rows, r);
       } else if (r <= 40) {
         gram_kernel<40><<<gg, gram_threads(r), sg, st>>>(X, w.G, w.np, w.list, w.cnt, pass, npass, rows, r);
-        chol_kernel<40><<<gc, kCholThreads, 0, st>>>(w.G, w.L, w.np, w.list, w.cnt, pass, npass, r);
+        chol_warp_kernel<40><<<gw, kCholWarps * 32, 0, st>>>(w.G, w.L, w.np, w.list, w.cnt, pass, npass, r, Nb);
         trsolve_kernel<40><<<gs, 128, ts, st>>>(X, w.L, w.np, w.list, w.cnt, pass, npass, rows, r);
       } else {
         gram_kernel<64><<<gg, gram_threads(r), sg, st>>>(X, w.G, w.np, w.list, w.cnt, pass, npass, rows, r);
@@ -965,12 +994,13 @@ static int run_chain(const spx_rsvd_args* a, const RsvdWs& w, cudaStream_t st) {
   // Two implementations of the same sequence and pass rules: the fused kernel
   // (spx_rsvd_fused.cu: one CTA per matrix, everything on chip, one CTA per SM) and the
   // multi-kernel chain below (each step a grid of its own, several CTAs per SM hiding the
-  // latency of the small dense steps).  Measured on B200 (k 16/32, q 0/2): the fused
-  // kernel is 1.3-2.2x faster up to about 3.5 waves of matrices, level at 512-1024, slower
-  // beyond; SPX_RSVD_PATH=fused|chain forces one.
+  // latency of the small dense steps).  Measured on B200 at k = 32, q = 2 with the
+  // one-warp Cholesky factor in both: fused 488k / 541k / 578k blocks/s at 296 / 1024 /
+  // 4096 matrices, chain 363k / 471k / 565k, so the fused kernel runs wherever its shape
+  // is supported; SPX_RSVD_PATH=fused|chain forces one.
   const char* path = getenv("SPX_RSVD_PATH");
   const bool can_fuse = rsvd_fused_supported(a->in_dtype, a->M, ms, a->omega, m, n, r);
-  bool fused = can_fuse && 2 * (int64_t)Nb <= 7 * (int64_t)nsm;
+  bool fused = can_fuse;
   if (path && strcmp(path, "fused") == 0) fused = can_fuse;
   if (path && strcmp(path, "chain") == 0) fused = false;
   int rc = SPX_OK;

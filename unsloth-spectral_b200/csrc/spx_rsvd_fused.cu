@@ -29,8 +29,8 @@
 // 128-row tile converted once to float64 while it is staged from TMEM into shared memory
 // over the idle B buffers, 4 x 4 register tiles of the upper
 // triangle, partial sums over 8 row subsets added in a fixed order), G = L L^T in float64
-// (right-looking, one barrier per column, pivots at rounding level of a zero column give
-// zero columns), X := X L^{-T} row by row in registers (thread = TMEM lane = row), written
+// by one warp (chol_warp: rows in registers, no block barriers; pivots at rounding level of
+// a zero column give zero columns), X := X L^{-T} row by row in registers (thread = TMEM lane = row), written
 // back into TMEM.  Passes: 2 for the final basis, 1 for intermediate ones, raised from
 // the first pass's pivot spread (> 1e6: 2, > 1e12: 3).
 //
@@ -66,7 +66,6 @@ struct Geo {
   static constexpr int P = (4 * NB4) | 1;         // Gram staging pitch (elements, odd)
   static constexpr int SP = RMAX + 4;             // output staging pitch (floats)
   static constexpr int BSZ = 128 * RP * 2;        // one 16-bit half of a B operand
-  static constexpr int OWN = (RMAX * (RMAX + 1) / 2 + NT - 1) / NT;   // Cholesky entries per thread
   static constexpr int ZC = 4 * RP;               // TMEM column of the Z accumulator
   static_assert(ZC + RP <= TMEM_COLS, "TMEM columns");
   static_assert(NPAIR * S <= NT, "one Gram item per thread");
@@ -189,7 +188,7 @@ template <typename T, int RMAX>
 __global__ void __launch_bounds__(NT, 1) rsvd_fused_kernel(FusedParams p) {
   using G = Geo<RMAX>;
   constexpr int RP = G::RP, R4 = G::R4, BSZ = G::BSZ, P = G::P, SP = G::SP, S = G::S, NB4 = G::NB4,
-                NTILE = G::NTILE, OWN = G::OWN, ZC = G::ZC;
+                NTILE = G::NTILE, ZC = G::ZC;
   constexpr uint32_t ID_MX = idesc(H16<T>::kFmt, 0, 1, RP);   // A = M (K-major), B MN-major
   constexpr uint32_t ID_MTY = idesc(H16<T>::kFmt, 1, 1, RP);  // A = M^T (MN-major)
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -197,8 +196,7 @@ __global__ void __launch_bounds__(NT, 1) rsvd_fused_kernel(FusedParams p) {
   __shared__ uint32_t tslot;
   __shared__ int sflag[2];   // [0]: a wait expired; [1]: passes asked for by the pivots
   __shared__ float sred[8];
-  __shared__ double colj[2][RMAX], diag[RMAX], pivs[RMAX], coef_s[RMAX], scale_s[RMAX];
-  __shared__ double dmax_s;
+  __shared__ double colj[2][RMAX], scale_s[RMAX];   // scratch of the Cholesky warp
 
   const int m = p.m, r = p.r, nt = m / 128;
   const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31, quad = w & 3, half = w >> 2;
@@ -356,20 +354,6 @@ __global__ void __launch_bounds__(NT, 1) rsvd_fused_kernel(FusedParams p) {
     it_c = it_two ? 4 * (tb + 1) : 4 * ta;
     it_t0 = ta * NB4 - ta * (ta - 1) / 2 + (tb - ta);
   }
-  // Cholesky entries of this thread (lower triangle, a >= c): a * 256 + c, or -1
-  int own[OWN];
-#pragma unroll
-  for (int q = 0; q < OWN; ++q) {
-    const int e = tid + NT * q;
-    own[q] = -1;
-    if (e < r * (r + 1) / 2) {
-      int a = (int)((sqrt(8.0 * e + 1.0) - 1.0) * 0.5);
-      while (a * (a + 1) / 2 > e) --a;
-      while ((a + 1) * (a + 2) / 2 <= e) ++a;
-      own[q] = a * 256 + (e - a * (a + 1) / 2);
-    }
-  }
-
   auto orth = [&](int ntl, uint32_t col0, uint32_t cstep, int npass0) {
     int npass = npass0;
     for (int pass = 0; pass < npass; ++pass) {
@@ -437,72 +421,10 @@ __global__ void __launch_bounds__(NT, 1) rsvd_fused_kernel(FusedParams p) {
         if (row < r && col < r && col <= row) sG[row * RMAX + col] = sum;
       }
       __syncthreads();
-      // G = L L^T (float64, right-looking); L (float32, inverse diagonal) -> sL
-      double gq[OWN];
-#pragma unroll
-      for (int q = 0; q < OWN; ++q) {
-        const int a = own[q] >> 8, c = own[q] & 255;
-        gq[q] = 0.0;
-        if (own[q] >= 0) {
-          gq[q] = sG[a * RMAX + c];
-          if (c == 0) colj[0][a] = gq[q];
-          if (c == a) diag[a] = gq[q];
-        }
-      }
-      __syncthreads();
-      if (tid == 0) {
-        double dm = 0.0;
-        for (int j = 0; j < r; ++j) dm = fmax(dm, diag[j]);
-        dmax_s = dm;
-        const double p0 = diag[0];
-        const bool okp = p0 > 1e-30 * dm && dm > 0.0;
-        pivs[0] = okp ? p0 : 0.0;
-        coef_s[0] = okp ? recip_pos(p0) : 0.0;
-      }
-      __syncthreads();
-      const double dmax = dmax_s;
-      for (int j = 0; j < r; ++j) {
-        const double coef = coef_s[j];
-        const double* cj = colj[j & 1];
-        double* cn = colj[(j + 1) & 1];
-#pragma unroll
-        for (int q = 0; q < OWN; ++q) {
-          const int a = own[q] >> 8, c = own[q] & 255;
-          if (own[q] >= 0 && c > j) {
-            const double v = fma(-cj[a] * coef, cj[c], gq[q]);
-            gq[q] = v;
-            if (c == j + 1) {
-              cn[a] = v;
-              if (a == j + 1) {
-                const bool okp = v > 1e-30 * dmax && dmax > 0.0;
-                pivs[j + 1] = okp ? v : 0.0;
-                coef_s[j + 1] = okp ? recip_pos(v) : 0.0;
-              }
-            }
-          }
-        }
-        if (tid == NT - 1) scale_s[j] = pivs[j] > 0.0 ? (double)rsqrt_pos_f(pivs[j]) : 0.0;
-        __syncthreads();
-      }
-#pragma unroll
-      for (int q = 0; q < OWN; ++q) {
-        const int a = own[q] >> 8, c = own[q] & 255;
-        if (own[q] >= 0 && a > c) sL[a * R4 + c] = (float)(gq[q] * scale_s[c]);
-      }
-      for (int j = tid; j < r; j += NT) sL[j * R4 + j] = (float)scale_s[j];
-      if (tid == 0) {
-        int n = npass;
-        if (pass == 0) {
-          double pmin = 1e300, pmax = 0.0;
-          for (int j = 0; j < r; ++j)
-            if (pivs[j] > 0.0) {
-              pmin = fmin(pmin, pivs[j]);
-              pmax = fmax(pmax, pivs[j]);
-            }
-          if (pmax > 1e6 * pmin && n < 2) n = 2;
-          if (pmax > 1e12 * pmin) n = 3;
-        }
-        sflag[1] = n;
+      // G = L L^T (float64, one warp: chol_warp); L (float32, inverse diagonal) -> sL
+      if (w == 0) {
+        const int n = chol_warp<RMAX>(sG, RMAX, r, sL, R4, &colj[0][0], scale_s, npass);
+        if (lane == 0) sflag[1] = pass == 0 ? n : npass;
       }
       __syncthreads();
       npass = sflag[1];
