@@ -291,20 +291,22 @@ __global__ void __launch_bounds__(GramTiling<RMAX>::NT, RMAX > 40 ? 1 : 4) gram_
 #pragma unroll
     for (int q = 0; q < GT::TPT; ++q) {
       if (it_a[q] < 0) continue;
-      double* dst = red + ((int64_t)it_s[q] * GT::NTILE + it_t0[q]) * 16;
+      // element-major, red[(entry * S + subset) * NTILE + tile]: conflict-free stores
+      // from the threads of a warp and consecutive reads for the summing threads
+      double* dst = red + (int64_t)it_s[q] * GT::NTILE + it_t0[q];
 #pragma unroll
-      for (int e = 0; e < 16; ++e) dst[e] = g[q][0][e];
+      for (int e = 0; e < 16; ++e) dst[(int64_t)e * GT::S * GT::NTILE] = g[q][0][e];
       if (it_two[q]) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) dst[16 + e] = g[q][1][e];   // tile (ta, tb + 1) is the next index
+        for (int e = 0; e < 16; ++e) dst[(int64_t)e * GT::S * GT::NTILE + 1] = g[q][1][e];   // tile (ta, tb + 1) is the next index
       }
     }
     __syncthreads();
     double* Gi = Gw + (int64_t)i * r * r;
-    for (int e = tid; e < GT::NTILE * 16; e += NT) {
-      const int tile = e >> 4, u = (e >> 2) & 3, v = e & 3;
+    for (int e2 = tid; e2 < GT::NTILE * 16; e2 += NT) {
+      const int idx = e2 / GT::NTILE, tile = e2 - idx * GT::NTILE, u = idx >> 2, v = idx & 3;
       double sum = 0.0;
-      for (int s2 = 0; s2 < GT::S; ++s2) sum += red[((int64_t)s2 * GT::NTILE + tile) * 16 + (e & 15)];
+      for (int s2 = 0; s2 < GT::S; ++s2) sum += red[((int64_t)idx * GT::S + s2) * GT::NTILE + tile];
       // tile index -> (ta, tb)
       int tb = tile, ta = 0;
       while (tb >= GT::NB4 - ta) {

@@ -397,20 +397,23 @@ __global__ void __launch_bounds__(NT, 1) rsvd_fused_kernel(FusedParams p) {
         }
       }
       __syncthreads();   // partials overwrite the B buffers and the staging tile
+      // partials element-major, red[(entry * S + subset) * NTILE + tile]: the threads of a
+      // warp (consecutive subsets and tiles) store to distinct banks, and the summing
+      // threads (consecutive tiles) read consecutive words
       if (it_a >= 0) {
-        double* dst = red + ((size_t)it_s * NTILE + it_t0) * 16;
+        double* dst = red + (size_t)it_s * NTILE + it_t0;
 #pragma unroll
-        for (int e = 0; e < 16; ++e) dst[e] = g0[e];
+        for (int e = 0; e < 16; ++e) dst[(size_t)e * S * NTILE] = g0[e];
         if (it_two) {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) dst[16 + e] = g1[e];   // tile (ta, tb + 1) is the next index
+          for (int e = 0; e < 16; ++e) dst[(size_t)e * S * NTILE + 1] = g1[e];   // tile (ta, tb + 1) is the next index
         }
       }
       __syncthreads();
-      for (int e = tid; e < NTILE * 16; e += NT) {
-        const int tile = e >> 4, u = (e >> 2) & 3, v = e & 3;
+      for (int e2 = tid; e2 < NTILE * 16; e2 += NT) {
+        const int idx = e2 / NTILE, tile = e2 - idx * NTILE, u = idx >> 2, v = idx & 3;
         double sum = 0.0;
-        for (int s2 = 0; s2 < S; ++s2) sum += red[((size_t)s2 * NTILE + tile) * 16 + (e & 15)];
+        for (int s2 = 0; s2 < S; ++s2) sum += red[((size_t)idx * S + s2) * NTILE + tile];
         int tb = tile, ta = 0;
         while (tb >= NB4 - ta) {
           tb -= NB4 - ta;
