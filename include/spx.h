@@ -319,6 +319,20 @@ SPX_API int spx_block_scores(const spx_block_score_args* args, void* stream);
 SPX_API int spx_block_values(const spx_block_value_args* args, void* stream);
 
 /* ---------------------------------------------------------------------------------
+ * RMSNorm of the decode loop's hidden rows, with the residual add fused in front.
+ * Replaces the fused RMSNorm that Unsloth's inference loop runs around the patched
+ * attention (the reference's rebuilt LlamaModel_fast_forward_inference,
+ * unsloth_spectral/integration.py:828-834, walks Unsloth's llama decoder, whose
+ * layernorms are Unsloth kernels outside the reference).  Rows of `dim` F16/BF16
+ * values, all pointers device pointers, 16-byte aligned, dim a multiple of 8 up to 8192:
+ *   h = x (+ residual), rounded to dtype; written to residual_out when residual is given
+ *   out = dtype(h * rsqrt(mean(h^2) + eps)) * weight   (product rounded to dtype)
+ * residual and residual_out are both NULL or both set; x may alias residual_out.
+ * ------------------------------------------------------------------------------- */
+SPX_API int spx_rmsnorm(const void* x, const void* residual, const void* weight, void* out, void* residual_out,
+                        int64_t rows, int dim, float eps, int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------
  * Utilities.
  * ------------------------------------------------------------------------------- */
 SPX_API int spx_abi_version(void);

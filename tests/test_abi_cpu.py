@@ -116,6 +116,18 @@ def test_rsvd_and_quant_host_validation_without_gpu():
     assert lib.spx_quantize_int8(q, None) == 1
 
 
+def test_rmsnorm_host_validation_without_gpu():
+    """spx_rmsnorm rejects bad arguments on the host, before any launch."""
+    lib = N.load()
+    assert lib.spx_rmsnorm(None, None, 256, 256, None, 4, 4096, 1e-5, N.SPX_BF16, None) == 1       # x missing
+    assert lib.spx_rmsnorm(256, 256, 256, 256, None, 4, 4096, 1e-5, N.SPX_BF16, None) == 1        # residual w/o out
+    assert lib.spx_rmsnorm(256, None, 256, 256, None, 4, 4100, 1e-5, N.SPX_BF16, None) == 2       # dim % 8
+    assert lib.spx_rmsnorm(256, None, 256, 256, None, 4, 16384, 1e-5, N.SPX_BF16, None) == 2      # dim too large
+    assert lib.spx_rmsnorm(256, None, 256, 256, None, 4, 4096, 1e-5, N.SPX_F32, None) == 3        # dtype
+    assert lib.spx_rmsnorm(264, None, 256, 256, None, 4, 4096, 1e-5, N.SPX_BF16, None) == 4       # alignment
+    assert lib.spx_rmsnorm(256, None, 256, 256, None, 0, 4096, 1e-5, N.SPX_BF16, None) == 0       # no rows
+
+
 def test_kernels_module_routes_to_library():
     import unsloth_spectral.kernels as K
     assert K.TRITON_AVAILABLE is True

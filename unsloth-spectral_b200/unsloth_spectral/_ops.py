@@ -107,6 +107,26 @@ def rope_freq(cos: torch.Tensor, sin: torch.Tensor):
     return out
 
 
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: Optional[torch.Tensor] = None):
+    """``spx_rmsnorm`` over the last dimension of FP16/BF16 ``x``: returns
+    ``dtype(h * rsqrt(mean(h^2) + eps)) * weight`` with ``h = x`` or, when ``residual`` is
+    given, ``h = x + residual`` (rounded to the dtype), returned as a second value."""
+    lib = N.lib_for(x.device)
+    dim = x.shape[-1]
+    xc = x.contiguous()
+    rows = xc.numel() // dim if dim else 0
+    out = torch.empty_like(xc)
+    rc = residual.contiguous() if residual is not None else None
+    h = torch.empty_like(xc) if residual is not None else None
+    dt = N.SPX_BF16 if x.dtype == torch.bfloat16 else N.SPX_F16 if x.dtype == torch.float16 else -1
+    if rows == 0:
+        return out if residual is None else (out, h)
+    N.check(lib, lib.spx_rmsnorm(N.ptr(xc), N.ptr(rc) if rc is not None else None, N.ptr(weight.contiguous()),
+                                 N.ptr(out), N.ptr(h) if h is not None else None, rows, dim, float(eps), dt,
+                                 N.stream_handle(x.device)), "spx_rmsnorm")
+    return out if residual is None else (out, h)
+
+
 def quantize_int8(x: torch.Tensor):
     """Per-leading-index INT8 quantisation; returns (codes int8, scale f32 [N],
     minmax f32 [N, 2], dequantised f32) -- bit-exact with the reference's

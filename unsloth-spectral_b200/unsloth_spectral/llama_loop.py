@@ -30,6 +30,7 @@ from typing import List, Optional
 import torch
 import torch.nn.functional as F
 
+from . import _ops
 from .integration import patch_unsloth_attention, rope_tables_for
 
 
@@ -50,14 +51,28 @@ MISTRAL_7B = LlamaShape()
 
 
 class RMSNorm(torch.nn.Module):
+    """``T(x * rsqrt(mean(x^2) + eps)) * weight``; on the GPU one ``spx_rmsnorm`` launch per
+    call (with ``add``, the residual add fused in front), the arithmetic of the float32
+    expression below, which runs only for CPU tensors (the layout tests)."""
+
     def __init__(self, dim: int, eps: float, device, dtype):
         super().__init__()
         self.weight = torch.nn.Parameter(torch.ones(dim, device=device, dtype=dtype))
         self.eps = eps
 
     def forward(self, x):
+        if x.is_cuda:
+            return _ops.rmsnorm(x, self.weight, self.eps)
         xf = x.float()
         return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)).to(x.dtype) * self.weight
+
+    def add(self, h, a):
+        """``h + a`` (the residual stream, in the dtype) and its norm, in one launch."""
+        if h.is_cuda:
+            out, hn = _ops.rmsnorm(a, self.weight, self.eps, residual=h)
+            return hn, out
+        hn = h + a
+        return hn, self.forward(hn)
 
 
 def _linear(i: int, o: int, device, dtype, std: float, gen) -> torch.nn.Linear:
@@ -138,24 +153,30 @@ class SpectralLlama(torch.nn.Module):
         pos = torch.arange(T, device=dev)[None]
         mask = torch.full((T, T), float("-inf"), device=dev, dtype=h.dtype).triu_(1)[None, None]
         caches: List = []
-        for layer in self.model.layers:
-            a, _, cache = layer.self_attn.forward(layer.input_layernorm(h), attention_mask=mask, position_ids=pos,
+        layers = self.model.layers
+        x = layers[0].input_layernorm(h)
+        for i, layer in enumerate(layers):
+            a, _, cache = layer.self_attn.forward(x, attention_mask=mask, position_ids=pos,
                                                   past_key_value=None, use_cache=True)
             caches.append(cache)
-            h = h + a
-            h = h + layer.mlp(layer.post_attention_layernorm(h))
-        return self.lm_head(self.model.norm(h[:, -1])), caches
+            h, x = layer.post_attention_layernorm.add(h, a)       # h + attention, its norm
+            nxt = layers[i + 1].input_layernorm if i + 1 < len(layers) else self.model.norm
+            h, x = nxt.add(h, layer.mlp(x))                      # h + MLP, the next norm
+        return self.lm_head(x[:, -1]), caches
 
     @torch.no_grad()
     def decode_step(self, token: torch.Tensor, position: torch.Tensor, caches: List):
         """One new token ``[B]`` at device position ``position`` (``[1, 1]`` int64) through
         the patched single-token forward of every layer; returns logits ``[B, vocab]``."""
         h = self.model.embed_tokens(token[:, None])
-        for i, layer in enumerate(self.model.layers):
-            a, caches[i] = layer.self_attn._spx_inference(layer.input_layernorm(h), caches[i], position)
-            h = h + a
-            h = h + layer.mlp(layer.post_attention_layernorm(h))
-        return self.lm_head(self.model.norm(h[:, -1]))
+        layers = self.model.layers
+        x = layers[0].input_layernorm(h)
+        for i, layer in enumerate(layers):
+            a, caches[i] = layer.self_attn._spx_inference(x, caches[i], position)
+            h, x = layer.post_attention_layernorm.add(h, a)
+            nxt = layers[i + 1].input_layernorm if i + 1 < len(layers) else self.model.norm
+            h, x = nxt.add(h, layer.mlp(x))
+        return self.lm_head(x[:, -1])
 
     @torch.no_grad()
     def generate(self, input_ids: torch.Tensor, max_new_tokens: int, timer=None, cuda_graphs: bool = False):
