@@ -93,6 +93,20 @@ def rope_tables_for(self, seq_len: int, device) -> Tuple[torch.Tensor, torch.Ten
     return tabs
 
 
+def _qkv(self, hidden_states):
+    """The query, key and value projections of ``hidden_states``.  A module that keeps its
+    three weights as row blocks of one tensor, ``spx_qkv_weight`` (the in-repo loop does),
+    gets them from one GEMM (one read of the input, one larger weight stream, which at the
+    decode step's batch of a few rows runs much closer to the bandwidth than three); any
+    other module runs its own ``q_proj`` / ``k_proj`` / ``v_proj`` as the reference does."""
+    w = getattr(self, "spx_qkv_weight", None)
+    if w is None:
+        return self.q_proj(hidden_states), self.k_proj(hidden_states), self.v_proj(hidden_states)
+    nq, nk = self.q_proj.weight.shape[0], self.k_proj.weight.shape[0]
+    qkv = torch.nn.functional.linear(hidden_states, w)
+    return qkv[..., :nq], qkv[..., nq:nq + nk], qkv[..., nq + nk:]
+
+
 def _mask_is_causal(mask: torch.Tensor, q_pos: torch.Tensor, k_pos: torch.Tensor) -> bool:
     """True when the additive ``mask`` (broadcastable to ``[.., T_q, T_k]``) is 0 where the
     key position is at most the query position and effectively -inf (<= -1e4) where it is
@@ -142,9 +156,10 @@ def create_spectral_forward(original_forward, block_size: int = 512, k_rank_keys
                          output_attentions=False, use_cache=False, cache_position=None, **kwargs):
         nh, nkv, hd = _attn_dims(self)
         bsz, q_len, _ = hidden_states.size()
-        q = self.q_proj(hidden_states).view(bsz, q_len, nh, hd).transpose(1, 2)
-        k_pre = self.k_proj(hidden_states).view(bsz, q_len, nkv, hd).transpose(1, 2)
-        v = self.v_proj(hidden_states).view(bsz, q_len, nkv, hd).transpose(1, 2)
+        qp, kp, vp = _qkv(self, hidden_states)
+        q = qp.view(bsz, q_len, nh, hd).transpose(1, 2)
+        k_pre = kp.view(bsz, q_len, nkv, hd).transpose(1, 2)
+        v = vp.view(bsz, q_len, nkv, hd).transpose(1, 2)
         if past_key_value is None:
             past_key_value = getattr(self, "_spectral_cache", None) if use_cache else None
         if not isinstance(past_key_value, SpectralCache):
@@ -189,9 +204,10 @@ def create_spectral_forward_inference(block_size: int = 512, k_rank_keys: int = 
         bsz, q_len, _ = hidden_states.size()
         assert q_len == 1, f"Inference path expects q_len=1, got {q_len}"
         nh, nkv, hd = _attn_dims(self)
-        q = self.q_proj(hidden_states).view(bsz, 1, nh, hd).transpose(1, 2)
-        k_pre = self.k_proj(hidden_states).view(bsz, 1, nkv, hd).transpose(1, 2)
-        v = self.v_proj(hidden_states).view(bsz, 1, nkv, hd).transpose(1, 2)
+        qp, kp, vp = _qkv(self, hidden_states)
+        q = qp.view(bsz, 1, nh, hd).transpose(1, 2)
+        k_pre = kp.view(bsz, 1, nkv, hd).transpose(1, 2)
+        v = vp.view(bsz, 1, nkv, hd).transpose(1, 2)
         if not isinstance(past_key_value, SpectralCache):
             past_key_value = SpectralCache(nkv, hd, block_size, k_rank_keys, k_rank_values, hot_buffer_size,
                                            device=hidden_states.device, dtype=hidden_states.dtype,

@@ -81,6 +81,12 @@ def _linear(i: int, o: int, device, dtype, std: float, gen) -> torch.nn.Linear:
     return lin
 
 
+def _linear_of(weight: torch.Tensor) -> torch.nn.Linear:
+    lin = torch.nn.Linear(weight.shape[1], weight.shape[0], bias=False, device="meta")
+    lin.weight = torch.nn.Parameter(weight)
+    return lin
+
+
 class Attention(torch.nn.Module):
     """Projections and the config attributes of an HF Llama attention module; its
     ``forward`` is replaced by ``patch_unsloth_attention``."""
@@ -90,9 +96,14 @@ class Attention(torch.nn.Module):
         self.config = SimpleNamespace(num_attention_heads=s.heads, num_key_value_heads=s.kv_heads, head_dim=s.head_dim,
                                       hidden_size=s.hidden, rope_theta=s.rope_theta)
         self.head_dim = s.head_dim
-        self.q_proj = _linear(s.hidden, s.heads * s.head_dim, device, dtype, std, gen)
-        self.k_proj = _linear(s.hidden, s.kv_heads * s.head_dim, device, dtype, std, gen)
-        self.v_proj = _linear(s.hidden, s.kv_heads * s.head_dim, device, dtype, std, gen)
+        # q / k / v weights are row blocks of one tensor (`spx_qkv_weight`, not saved: it
+        # shares their storage), so the patched forwards project with one GEMM
+        nq, nk = s.heads * s.head_dim, s.kv_heads * s.head_dim
+        w = torch.empty(nq + 2 * nk, s.hidden, device=device, dtype=dtype).normal_(0.0, std, generator=gen)
+        self.q_proj = _linear_of(w[:nq])
+        self.k_proj = _linear_of(w[nq:nq + nk])
+        self.v_proj = _linear_of(w[nq + nk:])
+        self.register_buffer("spx_qkv_weight", w, persistent=False)
         self.o_proj = _linear(s.heads * s.head_dim, s.hidden, device, dtype, std, gen)
 
     def forward(self, *a, **k):  # pragma: no cover - replaced by the patch
