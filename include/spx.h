@@ -333,6 +333,22 @@ SPX_API int spx_rmsnorm(const void* x, const void* residual, const void* weight,
                         int64_t rows, int dim, float eps, int dtype, void* stream);
 
 /* ---------------------------------------------------------------------------------
+ * Query RoPE of the single-token decode forward: the new token's query rotated at its
+ * position (the reference's decode path, unsloth_spectral/integration.py:600-612, rotates
+ * it with the tables before spectral_attention_decode), one launch for all sequences and
+ * heads.  x: `rows` rows of heads x head_dim values (F32/F16/BF16), consecutive rows
+ * x_row_stride elements apart, each row's heads contiguous; cos/sin f32 [rope_len][head_dim]
+ * tables, the first half used for both halves (half-split convention); position of row r
+ * = pos_device[r * pos_stride] (int64, device; pos_stride 0 broadcasts one position) or
+ * pos_host when pos_device is NULL, clamped to the table.  out: [rows][heads][head_dim],
+ * contiguous, dtype of x; each product and sum rounded in float32:
+ *   out[i] = x[i] c_i - x[i + h] s_i,  out[i + h] = x[i + h] c_i + x[i] s_i,  h = head_dim / 2.
+ * ------------------------------------------------------------------------------- */
+SPX_API int spx_rope_rows(const void* x, int64_t x_row_stride, const float* cos_table, const float* sin_table,
+                          int rope_len, const int64_t* pos_device, int64_t pos_stride, int64_t pos_host, void* out,
+                          int rows, int heads, int head_dim, int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------
  * Utilities.
  * ------------------------------------------------------------------------------- */
 SPX_API int spx_abi_version(void);

@@ -128,6 +128,15 @@ def test_rmsnorm_host_validation_without_gpu():
     assert lib.spx_rmsnorm(256, None, 256, 256, None, 0, 4096, 1e-5, N.SPX_BF16, None) == 0       # no rows
 
 
+def test_rope_rows_host_validation_without_gpu():
+    lib = N.load()
+    assert lib.spx_rope_rows(None, 1024, 256, 256, 100, None, 0, 5, 256, 2, 8, 128, N.SPX_BF16, None) == 1
+    assert lib.spx_rope_rows(256, 1024, 256, 256, 100, None, 0, 5, 256, 2, 8, 127, N.SPX_BF16, None) == 2
+    assert lib.spx_rope_rows(256, 512, 256, 256, 100, None, 0, 5, 256, 2, 8, 128, N.SPX_BF16, None) == 2
+    assert lib.spx_rope_rows(256, 1024, 256, 256, 100, None, 0, 5, 256, 2, 8, 128, 9, None) == 3
+    assert lib.spx_rope_rows(256, 1024, 256, 256, 100, None, 0, 5, 256, 0, 8, 128, N.SPX_BF16, None) == 0
+
+
 def test_kernels_module_routes_to_library():
     import unsloth_spectral.kernels as K
     assert K.TRITON_AVAILABLE is True

@@ -1,7 +1,9 @@
-"""spx_rmsnorm (the model loop's RMSNorm, residual add fused in front) against the
-float32 PyTorch expression of the same arithmetic: ``h = x + residual`` in the dtype
-(bit-exact), ``dtype(h * rsqrt(mean(h^2) + eps)) * weight`` within two units in the last
-place of the dtype (the mean's summation order and the reciprocal square root differ)."""
+"""The decode loop's small kernels against the PyTorch expressions they replace:
+spx_rmsnorm (RMSNorm with the residual add fused in front): ``h = x + residual`` in the
+dtype (bit-exact), ``dtype(h * rsqrt(mean(h^2) + eps)) * weight`` within two units in the
+last place of the dtype (the mean's summation order and the reciprocal square root
+differ); spx_rope_rows (the new token's query RoPE): bit-exact with ``apply_rope`` in
+float32, for positions per sequence, one position for all, and a host position."""
 import pytest
 import torch
 
@@ -47,3 +49,30 @@ def test_rmsnorm_leading_dims_and_zero_rows():
     torch.testing.assert_close(out.float(), _ref(x, w, 1e-6).float(), rtol=2 ** -6, atol=0)
     empty = torch.empty(0, 256, device="cuda", dtype=torch.bfloat16)
     assert _ops.rmsnorm(empty, w, 1e-6).shape == (0, 256)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("fused_qkv", [False, True])
+def test_rope_rows_matches_apply_rope(dtype, fused_qkv):
+    from unsloth_spectral import _ops
+    from unsloth_spectral import synthetic as syn
+    from unsloth_spectral.spectral_attention import apply_rope
+    B, nh, hd = 5, 8, 128
+    g = torch.Generator(device="cuda").manual_seed(3)
+    width = nh * hd + (2 * 2 * hd if fused_qkv else 0)   # q rows inside a [q | k | v] projection
+    full = torch.randn(B, 1, width, generator=g, device="cuda").to(dtype)
+    qp = full[..., :nh * hd]
+    cos, sin = syn.rope_tables(40000, hd, 1e6, device="cuda")
+    q = qp.view(B, 1, nh, hd).transpose(1, 2)
+    pos_rows = torch.tensor([[3], [900], [32767], [0], [12345]], device="cuda")
+    ref = apply_rope(q.float(), cos[pos_rows][:, None], sin[pos_rows][:, None]).to(dtype)
+    assert torch.equal(_ops.rope_rows(qp, nh, hd, cos, sin, pos_rows), ref)
+    wide = torch.arange(10, device="cuda").repeat(B, 1) * 7 + 100     # positions as the last column of [B, L]
+    pid = wide.reshape(-1, wide.shape[-1])[:, -1:]
+    ref = apply_rope(q.float(), cos[pid][:, None], sin[pid][:, None]).to(dtype)
+    assert torch.equal(_ops.rope_rows(qp, nh, hd, cos, sin, pid), ref)
+    one = torch.tensor([[777]], device="cuda")
+    ref = apply_rope(q.float(), cos[one][:, None], sin[one][:, None]).to(dtype)
+    assert torch.equal(_ops.rope_rows(qp, nh, hd, cos, sin, one), ref)
+    ref = apply_rope(q.float(), cos[4321], sin[4321]).to(dtype)
+    assert torch.equal(_ops.rope_rows(qp, nh, hd, cos, sin, None, 4321), ref)

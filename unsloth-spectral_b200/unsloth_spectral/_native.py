@@ -101,6 +101,8 @@ EXPORTS = {
     "spx_rsvd_workspace_size": (C.c_size_t, [C.POINTER(RsvdArgs)]),
     "spx_rsvd_compress": (C.c_int, [C.POINTER(RsvdArgs), C.c_void_p]),
     "spx_quantize_int8": (C.c_int, [C.POINTER(QuantArgs), C.c_void_p]),
+    "spx_rope_rows": (C.c_int, [C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int64,
+                                C.c_int64, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p]),
     "spx_rmsnorm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int,
                               C.c_float, C.c_int, C.c_void_p]),
     "spx_reconstruct": (C.c_int, [C.POINTER(ReconstructArgs), C.c_void_p]),

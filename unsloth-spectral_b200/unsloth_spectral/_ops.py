@@ -107,6 +107,26 @@ def rope_freq(cos: torch.Tensor, sin: torch.Tensor):
     return out
 
 
+def rope_rows(x: torch.Tensor, heads: int, head_dim: int, cos: torch.Tensor, sin: torch.Tensor,
+              pos: Optional[torch.Tensor] = None, pos_host: int = 0) -> torch.Tensor:
+    """``spx_rope_rows``: the rows of ``x`` (``[rows, ..., heads * head_dim]``, last
+    dimension contiguous, one token per row) rotated at ``pos`` (int64 device tensor of
+    one position per row, a strided column is fine, or one position for all) or at
+    ``pos_host``; returns ``[rows, heads, 1, head_dim]`` in the dtype of ``x``."""
+    lib = N.lib_for(x.device)
+    rows = x.shape[0]
+    assert x.stride(-1) == 1 and x.shape[-1] == heads * head_dim
+    out = torch.empty(rows, heads, 1, head_dim, dtype=x.dtype, device=x.device)
+    dt = {torch.float32: N.SPX_F32, torch.float16: N.SPX_F16, torch.bfloat16: N.SPX_BF16}[x.dtype]
+    pstride = 0
+    if pos is not None and pos.numel() > 1:
+        pstride = pos.stride(0)
+    N.check(lib, lib.spx_rope_rows(N.ptr(x), x.stride(0), N.ptr(cos), N.ptr(sin), cos.shape[0], N.ptr(pos),
+                                   pstride, int(pos_host), N.ptr(out), rows, heads, head_dim, dt,
+                                   N.stream_handle(x.device)), "spx_rope_rows")
+    return out
+
+
 def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: Optional[torch.Tensor] = None):
     """``spx_rmsnorm`` over the last dimension of FP16/BF16 ``x``: returns
     ``dtype(h * rsqrt(mean(h^2) + eps)) * weight`` with ``h = x`` or, when ``residual`` is

@@ -219,8 +219,14 @@ def create_spectral_forward_inference(block_size: int = 512, k_rank_keys: int = 
         qpos = kv_seq_len - 1
         # the query is rotated at position_ids, as the reference's decode path does
         # (integration.py:600-612); without them, at the next cache position
+        pid = None
         if position_ids is not None:
             pid = position_ids.reshape(-1, position_ids.shape[-1])[:, -1:].to(hidden_states.device)
+        if (hidden_states.is_cuda and cos.dtype == torch.float32 and cos.is_contiguous() and sin.is_contiguous()
+                and qp.stride(-1) == 1 and (pid is None or pid.shape[0] in (1, bsz))):
+            # one launch (spx_rope_rows), the same float32 arithmetic as apply_rope below
+            q = _ops.rope_rows(qp, nh, hd, cos, sin, pid, qpos)
+        elif pid is not None:
             q = apply_rope(q.float(), cos[pid][:, None], sin[pid][:, None]).to(q.dtype)
         else:
             q = apply_rope(q.float(), cos[qpos], sin[qpos]).to(q.dtype)
