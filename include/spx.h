@@ -349,6 +349,21 @@ SPX_API int spx_rope_rows(const void* x, int64_t x_row_stride, const float* cos_
                           int rows, int heads, int head_dim, int dtype, void* stream);
 
 /* ---------------------------------------------------------------------------------
+ * One decode token appended to the hot tier at its device length: the single-token
+ * branch of SpectralCache.append (unsloth_spectral/spectral_cache.py:164-319 appends the
+ * new key/value rows to the hot buffers).  k, v: [batch][heads][head_dim] rows (dtype),
+ * element (b, h, d) at b * stride_b + h * stride_h + d; hot_k, hot_v: the tier buffers
+ * [batch][heads][capacity][head_dim]; hot_pos int64 [capacity]; hot_len: the tier's device
+ * int32 length; pos: the token's int64 position (device).  Writes row hot_len and
+ * hot_pos[hot_len], then advances hot_len by one, in one launch; a length at or past the
+ * capacity writes nothing (the host keeps capacity ahead of the length).
+ * ------------------------------------------------------------------------------- */
+SPX_API int spx_hot_append(const void* k, const void* v, int64_t k_stride_b, int64_t k_stride_h, int64_t v_stride_b,
+                           int64_t v_stride_h, void* hot_k, void* hot_v, int64_t* hot_pos, int32_t* hot_len,
+                           const int64_t* pos, int batch, int heads, int head_dim, int capacity, int dtype,
+                           void* stream);
+
+/* ---------------------------------------------------------------------------------
  * Utilities.
  * ------------------------------------------------------------------------------- */
 SPX_API int spx_abi_version(void);

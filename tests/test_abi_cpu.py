@@ -137,6 +137,14 @@ def test_rope_rows_host_validation_without_gpu():
     assert lib.spx_rope_rows(256, 1024, 256, 256, 100, None, 0, 5, 256, 0, 8, 128, N.SPX_BF16, None) == 0
 
 
+def test_hot_append_host_validation_without_gpu():
+    lib = N.load()
+    assert lib.spx_hot_append(None, 256, 0, 0, 0, 0, 256, 256, 256, 256, 256, 1, 1, 8, 4, N.SPX_BF16, None) == 1
+    assert lib.spx_hot_append(256, 256, 0, 0, 0, 0, 256, 256, 256, 256, 256, 0, 1, 8, 4, N.SPX_BF16, None) == 2
+    assert lib.spx_hot_append(256, 256, -1, 0, 0, 0, 256, 256, 256, 256, 256, 1, 1, 8, 4, N.SPX_BF16, None) == 2
+    assert lib.spx_hot_append(256, 256, 0, 0, 0, 0, 256, 256, 256, 256, 256, 1, 1, 8, 4, 7, None) == 3
+
+
 def test_kernels_module_routes_to_library():
     import unsloth_spectral.kernels as K
     assert K.TRITON_AVAILABLE is True

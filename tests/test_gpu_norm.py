@@ -76,3 +76,35 @@ def test_rope_rows_matches_apply_rope(dtype, fused_qkv):
     assert torch.equal(_ops.rope_rows(qp, nh, hd, cos, sin, one), ref)
     ref = apply_rope(q.float(), cos[4321], sin[4321]).to(dtype)
     assert torch.equal(_ops.rope_rows(qp, nh, hd, cos, sin, None, 4321), ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_hot_append_matches_index_copy(dtype):
+    """spx_hot_append (the cache's single-token append, one launch) against the
+    index_copy_ formulation: three tokens appended from strided views of a fused
+    projection, rows / positions / device length identical; at full capacity it writes
+    nothing and leaves the length."""
+    from unsloth_spectral import _ops
+    B, H, D, cap = 3, 4, 128, 6
+    g = torch.Generator(device="cuda").manual_seed(5)
+    hk = torch.randn(B, H, cap, D, generator=g, device="cuda").to(dtype)
+    hv = torch.randn(B, H, cap, D, generator=g, device="cuda").to(dtype)
+    hp = torch.arange(cap, device="cuda") * 11
+    hl = torch.tensor(2, dtype=torch.int32, device="cuda")
+    rk, rv, rp = hk.clone(), hv.clone(), hp.clone()
+    for step in range(3):
+        full = torch.randn(B, 1, (2 + 2) * H * D // 2, generator=g, device="cuda").to(dtype)
+        k = full[..., :H * D].view(B, 1, H, D).transpose(1, 2)
+        v = full[..., H * D:2 * H * D].view(B, 1, H, D).transpose(1, 2)
+        pos = torch.tensor([1000 + step], device="cuda")
+        idx = torch.tensor([2 + step], device="cuda")
+        rk.index_copy_(2, idx, k)
+        rv.index_copy_(2, idx, v)
+        rp.index_copy_(0, idx, pos)
+        _ops.hot_append(k, v, hk, hv, hp, hl, pos)
+    assert torch.equal(hk, rk) and torch.equal(hv, rv) and torch.equal(hp, rp) and int(hl) == 5
+    k = torch.zeros(B, H, 1, D, device="cuda", dtype=dtype)
+    _ops.hot_append(k, k, hk, hv, hp, hl, torch.tensor([7], device="cuda"))
+    assert int(hl) == 6 and torch.equal(hk[:, :, :5], rk[:, :, :5])
+    _ops.hot_append(k, k, hk, hv, hp, hl, torch.tensor([8], device="cuda"))   # full: nothing written
+    assert int(hl) == 6 and int(hp[5]) == 7

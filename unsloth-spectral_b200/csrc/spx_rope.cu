@@ -75,3 +75,69 @@ int spx_rope_rows(const void* x, int64_t x_row_stride, const float* cos_table, c
         static_cast<float*>(out), heads, head_dim);
   return launch_status("rope_rows_kernel");
 }
+
+// ---------------------------------------------------------------------------------
+// One decode token appended to the hot tier at its device length (spx_hot_append): the
+// key and value rows of every (sequence, head) written at hot_len, the position at
+// hot_pos[hot_len], then hot_len + 1, in one CTA (every thread reads the length before
+// thread 0 advances it).  A length at or past the capacity writes nothing.
+namespace spx {
+namespace rope {
+
+template <typename T>
+__global__ void __launch_bounds__(512) hot_append_kernel(const T* __restrict__ k, const T* __restrict__ v,
+                                                         int64_t ksb, int64_t ksh, int64_t vsb, int64_t vsh,
+                                                         T* __restrict__ hk, T* __restrict__ hv,
+                                                         int64_t* __restrict__ hpos, int32_t* hlen,
+                                                         const int64_t* __restrict__ pos, int B, int H, int D,
+                                                         int cap) {
+  const int len = *hlen;
+  const bool room = len >= 0 && len < cap;
+  const int64_t n = (int64_t)B * H * D;
+  for (int64_t e = threadIdx.x; room && e < n; e += blockDim.x) {
+    const int d = (int)(e % D);
+    const int64_t bh = e / D;
+    const int h = (int)(bh % H), b = (int)(bh / H);
+    const int64_t dst = (bh * cap + len) * D + d;
+    hk[dst] = k[b * ksb + h * ksh + d];
+    hv[dst] = v[b * vsb + h * vsh + d];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && room) {
+    hpos[len] = *pos;
+    *hlen = len + 1;
+  }
+}
+
+}  // namespace rope
+}  // namespace spx
+
+int spx_hot_append(const void* k, const void* v, int64_t k_stride_b, int64_t k_stride_h, int64_t v_stride_b,
+                   int64_t v_stride_h, void* hot_k, void* hot_v, int64_t* hot_pos, int32_t* hot_len,
+                   const int64_t* pos, int batch, int heads, int head_dim, int capacity, int dtype, void* stream) {
+  SPX_REQUIRE(k && v && hot_k && hot_v && hot_pos && hot_len && pos, SPX_ERR_NULL,
+              "spx_hot_append: every pointer is required");
+  SPX_REQUIRE(dtype_ok(dtype), SPX_ERR_UNSUPPORTED, "spx_hot_append: bad dtype %d", dtype);
+  SPX_REQUIRE(batch >= 1 && heads >= 1 && head_dim >= 1 && capacity >= 1, SPX_ERR_SHAPE,
+              "spx_hot_append: bad shape batch %d heads %d head_dim %d capacity %d", batch, heads, head_dim,
+              capacity);
+  SPX_REQUIRE(k_stride_b >= 0 && k_stride_h >= 0 && v_stride_b >= 0 && v_stride_h >= 0, SPX_ERR_SHAPE,
+              "spx_hot_append: negative stride");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == SPX_BF16)
+    rope::hot_append_kernel<__nv_bfloat16><<<1, 512, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v), k_stride_b, k_stride_h,
+        v_stride_b, v_stride_h, static_cast<__nv_bfloat16*>(hot_k), static_cast<__nv_bfloat16*>(hot_v), hot_pos,
+        hot_len, pos, batch, heads, head_dim, capacity);
+  else if (dtype == SPX_F16)
+    rope::hot_append_kernel<__half><<<1, 512, 0, st>>>(
+        static_cast<const __half*>(k), static_cast<const __half*>(v), k_stride_b, k_stride_h, v_stride_b, v_stride_h,
+        static_cast<__half*>(hot_k), static_cast<__half*>(hot_v), hot_pos, hot_len, pos, batch, heads, head_dim,
+        capacity);
+  else
+    rope::hot_append_kernel<float><<<1, 512, 0, st>>>(
+        static_cast<const float*>(k), static_cast<const float*>(v), k_stride_b, k_stride_h, v_stride_b, v_stride_h,
+        static_cast<float*>(hot_k), static_cast<float*>(hot_v), hot_pos, hot_len, pos, batch, heads, head_dim,
+        capacity);
+  return launch_status("hot_append_kernel");
+}

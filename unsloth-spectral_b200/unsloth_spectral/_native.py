@@ -103,6 +103,9 @@ EXPORTS = {
     "spx_quantize_int8": (C.c_int, [C.POINTER(QuantArgs), C.c_void_p]),
     "spx_rope_rows": (C.c_int, [C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int64,
                                 C.c_int64, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p]),
+    "spx_hot_append": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_int64, C.c_void_p,
+                                 C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                 C.c_int, C.c_void_p]),
     "spx_rmsnorm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int,
                               C.c_float, C.c_int, C.c_void_p]),
     "spx_reconstruct": (C.c_int, [C.POINTER(ReconstructArgs), C.c_void_p]),

@@ -127,6 +127,21 @@ def rope_rows(x: torch.Tensor, heads: int, head_dim: int, cos: torch.Tensor, sin
     return out
 
 
+def hot_append(k: torch.Tensor, v: torch.Tensor, hot_k: torch.Tensor, hot_v: torch.Tensor, hot_pos: torch.Tensor,
+               hot_len: torch.Tensor, pos: torch.Tensor):
+    """``spx_hot_append``: one token's key/value rows ``[B, H, 1, D]`` (any strides, the
+    last dimension contiguous) written into the hot tier at the device length ``hot_len``
+    (int32 scalar), its position (int64 device scalar) into ``hot_pos``, the length
+    advanced by one -- one launch."""
+    lib = N.lib_for(k.device)
+    B, H, _, D = k.shape
+    assert k.stride(-1) == 1 and v.stride(-1) == 1 and hot_k.is_contiguous() and hot_v.is_contiguous()
+    dt = {torch.float32: N.SPX_F32, torch.float16: N.SPX_F16, torch.bfloat16: N.SPX_BF16}[k.dtype]
+    N.check(lib, lib.spx_hot_append(N.ptr(k), N.ptr(v), k.stride(0), k.stride(1), v.stride(0), v.stride(1),
+                                    N.ptr(hot_k), N.ptr(hot_v), N.ptr(hot_pos), N.ptr(hot_len), N.ptr(pos), B, H, D,
+                                    hot_k.shape[2], dt, N.stream_handle(k.device)), "spx_hot_append")
+
+
 def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: Optional[torch.Tensor] = None):
     """``spx_rmsnorm`` over the last dimension of FP16/BF16 ``x``: returns
     ``dtype(h * rsqrt(mean(h^2) + eps)) * weight`` with ``h = x`` or, when ``residual`` is

@@ -306,11 +306,18 @@ class SpectralCache:
         if T_new == 1 and pid is not None and pid.device == t.device:
             # a decode token: written at the device hot length, which advances on the
             # device, so the step has no host-dependent addresses (CUDA-graph safe)
-            idx = t.hot_len_device().view(1).long()
-            t.hot_k.index_copy_(2, idx, K_new.to(t.dtype))
-            t.hot_v.index_copy_(2, idx, V_new.to(t.dtype))
-            t.hot_pos.index_copy_(0, idx, pid.reshape(1).to(torch.int64))
-            t.advance_hot(1)
+            if (t.device.type == "cuda" and K_new.dtype == t.dtype and V_new.dtype == t.dtype
+                    and K_new.stride(-1) == 1 and V_new.stride(-1) == 1):
+                # one launch (spx_hot_append): rows, position and the length advance
+                _ops.hot_append(K_new, V_new, t.hot_k, t.hot_v, t.hot_pos, t.hot_len_device(),
+                                pid.reshape(1).to(torch.int64))
+                t._hot_len += 1
+            else:
+                idx = t.hot_len_device().view(1).long()
+                t.hot_k.index_copy_(2, idx, K_new.to(t.dtype))
+                t.hot_v.index_copy_(2, idx, V_new.to(t.dtype))
+                t.hot_pos.index_copy_(0, idx, pid.reshape(1).to(torch.int64))
+                t.advance_hot(1)
         else:
             t.hot_k[:, :, n0:n0 + T_new].copy_(K_new)
             t.hot_v[:, :, n0:n0 + T_new].copy_(V_new)
