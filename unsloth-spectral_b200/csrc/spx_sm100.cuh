@@ -307,7 +307,7 @@ static Plan plan(int units, int nblk, int sms) {
   Plan best{};
   if (plan_override(units, nblk, &best)) return best;
   long best_cost = -1;
-  for (int G : {32, 16, 8}) {
+  for (int G : {32, 16, 8, 4, 2, 1}) {   // small groups matter when units are few (one layer, small batch)
     const int Gu = G < units ? G : units;
     const int ngroups = (units + Gu - 1) / Gu;
     for (int nr = 1; nr <= nblk; ++nr) {
