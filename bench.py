@@ -938,13 +938,57 @@ def run_ours(args, c):
         else:
             out_host.copy_(out, non_blocking=True)
 
-    for i in range(args.warmup):
-        e2e_step(i)
+    # one GPU: the copies run on a copy stream and overlap the neighbouring steps' decode
+    # (double-buffered query and output), as a serving loop would run them; every step
+    # still copies its query in from pinned host memory and its output back out, and the
+    # end event waits for the last copy
+    if world == 1:
+        cs = torch.cuda.Stream(device=dev)
+        q2 = [q_dev, torch.empty_like(q_dev)]
+        o2 = [out, torch.empty_like(out)]
+        oh2 = [out_host, torch.empty_like(out_host).pin_memory()]
+        ev_in = [torch.cuda.Event() for _ in range(2)]
+        ev_dec = [torch.cuda.Event() for _ in range(2)]
+        ev_out = [torch.cuda.Event() for _ in range(2)]
+
+        def e2e_run(i0, n):
+            with torch.cuda.stream(cs):
+                q2[0].copy_(pinned_in[i0 % nq], non_blocking=True)
+                ev_in[0].record(cs)
+            for k in range(n):
+                b = k & 1
+                stream.wait_event(ev_in[b])
+                if k >= 2:
+                    stream.wait_event(ev_out[b])   # o2[b] copied out by step k - 2
+                a = decode_args(c, tiers, q2[b], o2[b], cos, sin, qpos, ws, Hl, freq)
+                N.check(lib, lib.spx_decode_attn(a, sh), "spx_decode_attn")
+                ev_dec[b].record(stream)
+                with torch.cuda.stream(cs):
+                    if k + 1 < n:
+                        if k >= 1:
+                            cs.wait_event(ev_dec[b ^ 1])   # q2[b ^ 1] read by step k - 1
+                        q2[b ^ 1].copy_(pinned_in[(i0 + k + 1) % nq], non_blocking=True)
+                        ev_in[b ^ 1].record(cs)
+                    cs.wait_event(ev_dec[b])
+                    oh2[b].copy_(o2[b], non_blocking=True)
+                    ev_out[b].record(cs)
+            stream.wait_event(ev_out[(n - 1) & 1])
+            if n >= 2:
+                stream.wait_event(ev_out[n & 1])
+
+    if world == 1:
+        e2e_run(0, args.warmup)
+    else:
+        for i in range(args.warmup):
+            e2e_step(i)
     barrier()
     ev4, ev5 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev4.record(stream)
-    for i in range(args.steps):
-        e2e_step(args.warmup + i)
+    if world == 1:
+        e2e_run(args.warmup, args.steps)
+    else:
+        for i in range(args.steps):
+            e2e_step(args.warmup + i)
     ev5.record(stream)
     barrier()
     e2e_ms = ev4.elapsed_time(ev5)
