@@ -16,6 +16,11 @@ patched forwards read (``config`` with head counts / ``head_dim`` / ``rope_theta
 * each new token: ``self_attn._spx_inference`` per layer (the patched single-token
   forward, routed to ``kernels.spectral_attention_decode``), greedy argmax.
 
+On the GPU the loop's own small operations are single launches of the library: each
+RMSNorm with the residual add in front of it (``spx_rmsnorm``), and the attention
+modules hold their q / k / v weights as one tensor so that the patched forwards project
+with one GEMM (the forwards' query RoPE and cache append are library kernels too).
+
 Weights are random (``N(0, std^2)``, the architecture only), created directly on the
 device.  ``MISTRAL_7B`` is the 32-layer, hidden-4096, 32/8-head, FFN-14336, vocab-32768,
 RoPE-theta-1e6 shape.
